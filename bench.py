@@ -1,0 +1,392 @@
+"""Benchmark of the KV-compression hot path on B200.
+
+    python bench.py [--gpus N --steps K --warmup W] [--impl engine|reference]
+
+Workload (per GPU, weak scaling): the 2-bit-mode configuration -- K and V
+tensors fp16 [B=1, H=16, S=40000, D=256] (N(0,1) with 2% Student-t(3)
+channels, seeded), compressed to code bits + residual sign bits + two norms
+per row.  One step = one fused launch over both tensors (1.28M rows).  Inputs
+(655 MB per step) exceed the 126 MB L2, so no flush is needed between steps.
+Also reported: decode attention over a 2-bit compressed cache (q bf16
+[32, 16, 128], S = 40000) in us per step and us per token.
+
+``--impl reference`` times the reference algorithm's CPU implementation (the
+oracle port of KudaHitamCUDA.cu:13-195, OpenMP over every host thread) on a
+bounded sample of the same workload.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import pathlib
+import statistics
+import subprocess
+import sys
+import threading
+import time
+
+ROOT = pathlib.Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT / "kudahitam-quant_b200"))
+sys.path.insert(0, str(ROOT))
+
+import numpy as np  # noqa: E402
+import torch  # noqa: E402
+
+METRIC = ("KV rows compressed/sec and HBM GB/s (% of peak); "
+          "decode-attn µs/token at 40k ctx")
+B, H, S, D = 1, 16, 40000, 256
+ROWS_PER_TENSOR = B * H * S
+ALG_BYTES_PER_ROW = D * 2 + 2 * D // 8 + 8   # read fp16 row; write 2 planes + 2 norms
+DEC_B, DEC_H, DEC_S, DEC_D = 32, 16, 40000, 128
+DEC_BYTES_PER_ROW = 2 * (2 * DEC_D // 8 + 8)  # K and V: 2 planes + 2 norms each
+FALLBACK_HBM_GBS = 6650.0
+
+# dram__bytes_read.sum + dram__bytes_write.sum per compressed row, from the ncu
+# capture summarised in profiles/ (None until a capture exists).
+NCU_TRAFFIC_BYTES_PER_ROW = None
+
+
+def peaks() -> tuple[float, str]:
+    p = ROOT / "MEASURED_PEAKS.json"
+    try:
+        return float(json.loads(p.read_text())["hbm_gbs"]), "measured"
+    except Exception:
+        return FALLBACK_HBM_GBS, "fallback"
+
+
+def synth_kv(seed: int, device) -> tuple[torch.Tensor, torch.Tensor]:
+    g = torch.Generator(device=device).manual_seed(seed)
+    out = []
+    for t in range(2):
+        x = torch.randn(B, H, S, D, device=device, generator=g)
+        n = round(0.02 * D)
+        ch = torch.randperm(D, device=device, generator=g)[: n]
+        # Student-t(3) = N / sqrt(chi2_3 / 3)
+        z = torch.randn(B, H, S, n, device=device, generator=g)
+        chi = (torch.randn(B, H, S, n, 3, device=device, generator=g) ** 2).sum(-1)
+        x[..., ch] = z / torch.sqrt(chi / 3.0)
+        out.append(x.half())
+    return out[0], out[1]
+
+
+class ClockSampler:
+    """nvidia-smi clock / throttle sampling during the timed region."""
+
+    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
+                 "--format=csv,noheader,nounits", "-lms", "100"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.t = threading.Thread(target=self._read, daemon=True)
+            self.t.start()
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            f = [x.strip() for x in ln.split(",")]
+            if len(f) < 9:
+                continue
+            try:
+                sm.append(float(f[1]))
+                mx = float(f[2])
+            except ValueError:
+                continue
+            for nm, v in zip(names, f[5:9]):
+                if v.lower().startswith("active"):
+                    reasons.add(nm)
+        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
+                "reasons": sorted(reasons), "samples": len(sm)}
+
+
+def dist_setup(args):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+        import torch.distributed as dist
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+        dist.barrier()
+
+
+def max_over_ranks(v: float, world: int) -> float:
+    if world == 1:
+        return v
+    from kudahitam.dist import max_over_ranks as m
+    return m(v, device=torch.device("cuda", torch.cuda.current_device()))
+
+
+def cpu_baseline_run(target_s: float = 10.0, max_rows: int = 1 << 22) -> dict:
+    """The oracle port on a bounded sample of the workload, all host threads."""
+    from oracle import oracle as O
+    from kudahitam.codebook import lloyd_max, rademacher
+    rng = np.random.default_rng(2)
+    d = rademacher(D, 1).numpy()
+    c = lloyd_max(1, D).numpy()
+
+    def sample(n):
+        x = rng.standard_normal((n, D)).astype(np.float32)
+        k = round(0.02 * D)
+        ch = rng.choice(D, k, replace=False)
+        x[:, ch] = rng.standard_t(3, size=(n, k))
+        return x.astype(np.float16)
+
+    n = 16384
+    x = sample(n)
+    t0 = time.perf_counter()
+    O.compress_v8(x, d, c, want=("norms", "rnorms", "signs", "idx"))
+    dt = time.perf_counter() - t0
+    n2 = int(min(max_rows, max(n, n * target_s / max(dt, 1e-6))))
+    x = sample(n2)
+    t0 = time.perf_counter()
+    O.compress_v8(x, d, c, want=("norms", "rnorms", "signs", "idx"))
+    dt = time.perf_counter() - t0
+    return {"value": n2 / dt, "unit": "rows/s", "cores": O.num_threads(), "kind": "port",
+            "sample": f"{n2} fp16 rows of the D=256 2-bit-mode workload, {dt:.2f} s"}
+
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    cfg = workload_config(1)
+    vals = []
+    for _ in range(args.warmup):
+        cpu_baseline_run(target_s=1.0, max_rows=1 << 16)
+    for _ in range(args.steps):
+        vals.append(cpu_baseline_run(target_s=5.0))
+    v = statistics.median([x["value"] for x in vals])
+    line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "rows/s",
+            "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic", "config": cfg,
+            "cpu_baseline": {**vals[-1], "value": v},
+            "e2e": {"value": v, "unit": "rows/s", "h2d_bytes_per_step": 0,
+                    "d2h_bytes_per_step": 0}}
+    print(json.dumps(line), flush=True)
+
+
+def workload_config(world: int) -> dict:
+    return {"workload": "kv-compress 2-bit mode (code bits + QJL residual signs + 2 norms), "
+                        "K and V fp16 [1,16,40000,256] per GPU",
+            "head_dim": D, "input_dtype": "fp16", "rows_per_step": 2 * ROWS_PER_TENSOR * world,
+            "global_batch": 2 * ROWS_PER_TENSOR * world, "seq_len": S,
+            "parallelism": f"shard b*h x{world}, no comm",
+            "l2": "inputs 655 MB per GPU per step > 126 MB L2: no flush"}
+
+
+def time_loop(fn, steps: int, stream) -> list[float]:
+    """Per-step CUDA-event times (ms) on `stream`."""
+    evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True))
+           for _ in range(steps)]
+    for a, b in evs:
+        a.record(stream)
+        fn()
+        b.record(stream)
+    torch.cuda.synchronize()
+    return [a.elapsed_time(b) for a, b in evs]
+
+
+def run_engine(args, world, rank, local):
+    from kudahitam import KudahitamCompressorV2, ops
+    from kudahitam.codebook import lloyd_max, rademacher
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    peak, peak_kind = peaks()
+
+    k, v = synth_kv(2 + 1000 * rank, dev)
+    d = rademacher(D, 1)
+    c = lloyd_max(1, D)
+    outs = [ops.empty_packed(k.shape, 1, True, dev), ops.empty_packed(v.shape, 1, True, dev)]
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        ops.compress_many([k, v], d, c, residual=True, outs=outs)
+
+    for _ in range(max(args.warmup, 3)):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    torch.cuda.synchronize()
+    with ClockSampler(local) as clk:
+        t0 = torch.cuda.Event(enable_timing=True)
+        t1 = torch.cuda.Event(enable_timing=True)
+        t0.record(stream)
+        for _ in range(args.steps):
+            step()
+        t1.record(stream)
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+    ms_local = t0.elapsed_time(t1)
+    ms = max_over_ranks(ms_local, world)
+    rows_all = 2 * ROWS_PER_TENSOR * world * args.steps
+    value = rows_all / (ms / 1e3)
+
+    # dominant kernel, per-launch times
+    per = time_loop(step, max(args.steps, 5), stream)
+    launch_ms = statistics.median(per)
+    rows_launch = 2 * ROWS_PER_TENSOR
+    achieved = rows_launch * ALG_BYTES_PER_ROW / (launch_ms / 1e3) / 1e9
+    roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+            "frac": achieved / peak, "peak_kind": peak_kind,
+            "traffic": (NCU_TRAFFIC_BYTES_PER_ROW * rows_launch
+                        if NCU_TRAFFIC_BYTES_PER_ROW else None),
+            "algorithmic_bytes": rows_launch * ALG_BYTES_PER_ROW,
+            "kernel": "compress_simt_kernel<__half,256,Sym2,RES>"}
+
+    # e2e through the public API with host buffers
+    comp = KudahitamCompressorV2(D, 1, seed=1)
+    hk = k.cpu().pin_memory()
+    hv = v.cpu().pin_memory()
+    gk = torch.empty_like(k)
+    gv = torch.empty_like(v)
+    host_out = {}
+
+    def e2e_step():
+        gk.copy_(hk, non_blocking=True)
+        gv.copy_(hv, non_blocking=True)
+        ck = comp.compress(gk)
+        cv = comp.compress(gv)
+        for name, ckv in (("k", ck), ("v", cv)):
+            p = ckv.packed
+            for f in ("code", "res", "norms", "rnorms"):
+                t = getattr(p, f)
+                key = name + f
+                if key not in host_out:
+                    host_out[key] = torch.empty(t.shape, dtype=t.dtype, pin_memory=True)
+                host_out[key].copy_(t, non_blocking=True)
+        return ck, cv
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    barrier(world)
+    e0 = torch.cuda.Event(enable_timing=True)
+    e1 = torch.cuda.Event(enable_timing=True)
+    e2e_steps = max(2, min(args.steps, 10))
+    e0.record(stream)
+    for _ in range(e2e_steps):
+        e2e_step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    e2e_ms = max_over_ranks(e0.elapsed_time(e1), world)
+    h2d = hk.numel() * 2 + hv.numel() * 2
+    d2h = sum(t.numel() * t.element_size() for t in host_out.values())
+    e2e = {"value": 2 * ROWS_PER_TENSOR * world * e2e_steps / (e2e_ms / 1e3), "unit": "rows/s",
+           "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": d2h,
+           "ms_per_step": e2e_ms / e2e_steps}
+    del hk, hv, gk, gv
+
+    dec = decode_bench(dev, args)
+
+    line = {"metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world,
+            "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
+            "dtype": "f32", "data": "synthetic", "config": workload_config(world),
+            "hbm_gbs": achieved, "hbm_frac_of_measured": achieved / peak,
+            "hbm_frac_of_spec_8000": achieved / 8000.0,
+            "roofline": roof, "e2e": e2e, "decode": dec,
+            "gpu_launches": args.steps, "clocks": clk.summary()}
+    if rank == 0 and world == 1 and not args.no_cpu_baseline:
+        line["cpu_baseline"] = cpu_baseline_run()
+    if rank == 0:
+        print(json.dumps(line), flush=True)
+
+
+def decode_bench(dev, args) -> dict:
+    from kudahitam import ops
+    from kudahitam.codebook import lloyd_max, rademacher
+    G = DEC_B * DEC_H
+    g = torch.Generator(device=dev).manual_seed(5)
+    dk, dv = rademacher(DEC_D, 10), rademacher(DEC_D, 11)
+    c = lloyd_max(1, DEC_D)
+    pk = ops.empty_packed((G, DEC_S, DEC_D), 1, True, dev)
+    pv = ops.empty_packed((G, DEC_S, DEC_D), 1, True, dev)
+    for p, dd in ((pk, dk), (pv, dv)):
+        for i in range(0, G, 64):
+            x = torch.randn(64, DEC_S, DEC_D, device=dev, generator=g).to(torch.bfloat16)
+            ops.compress(x, dd, c, out=p.rows(i * DEC_S, (i + 64) * DEC_S))
+    q = torch.randn(G, DEC_D, generator=torch.Generator().manual_seed(4)).to(torch.bfloat16).to(dev)
+    n_splits = ops.default_splits(G, DEC_S, dev)
+    ws = torch.empty(ops.decode_workspace_bytes(G, n_splits, DEC_D) // 4, device=dev)
+    out = torch.empty(G, DEC_D, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    qf = q.float()
+
+    def step():
+        ops.decode_partial(qf, pk, pv, dk, dv, c, 1 / math.sqrt(DEC_D), n_splits, ws, n_splits,
+                           0, DEC_S)
+        ops.decode_combine(ws, n_splits, dv, out)
+
+    for _ in range(3):
+        step()
+    per = time_loop(step, max(5, min(args.steps, 20)), stream)
+    ms = statistics.median(per)
+    bytes_step = G * DEC_S * DEC_BYTES_PER_ROW
+    peak, _ = peaks()
+    return {"config": "q bf16 [32,16,128]; K and V 2-bit-mode packed, S=40000",
+            "us_per_step": ms * 1e3, "us_per_token": ms * 1e3 / DEC_B,
+            "n_splits": n_splits, "gbs": bytes_step / (ms / 1e3) / 1e9,
+            "frac_of_measured_hbm": bytes_step / (ms / 1e3) / 1e9 / peak}
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["engine", "reference"], default="engine")
+    ap.add_argument("--no-cpu-baseline", action="store_true")
+    args = ap.parse_args()
+    if args.impl == "reference":
+        world = int(os.environ.get("WORLD_SIZE", "1"))
+        rank = int(os.environ.get("RANK", "0"))
+        run_reference(args, world, rank)
+        return
+    world, rank, local = dist_setup(args)
+    try:
+        run_engine(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -1,0 +1,189 @@
+/*
+ * kudahitam.h -- C ABI of the B200 (sm_100a) KV-cache compression engine.
+ *
+ * Everything here is plain C: raw pointers, sizes and an opaque stream handle
+ * (a cudaStream_t passed as void*; NULL = the legacy default stream).  No call
+ * allocates device memory: the caller owns every buffer.  Calls are
+ * asynchronous and stream-ordered; they return a status code and never abort
+ * the process or trap the GPU.
+ *
+ * Packed cache layout (per tensor of n_rows rows of head_dim D, D in {128,256}):
+ *   code_bits : uint32[n_rows][D/32]  (bits=1) -- Lloyd-Max index of element i
+ *               at bit (i & 31) of word (i >> 5); bit 1 = centroid c[1].
+ *               This is the reference's LSB-first 1-bit packing
+ *               (KudaHitamCUDA.cu:362-364 write, :756 read) read as 32-bit words.
+ *               uint32[n_rows][D/16]  (bits=2) -- 2-bit index of element i at
+ *               bits 2*(i & 15) of word (i >> 4) (nibble order of :358-360
+ *               extended to 2-bit fields).
+ *   res_bits  : uint32[n_rows][D/32] -- QJL sign of the residual after the
+ *               Hadamard projection, bit 1 = sign +1 (KudaHitamCUDA.cu:189-194).
+ *   norms     : float[n_rows]  -- ||x|| (1e-8 for an all-zero row, :50).
+ *   r_norms   : float[n_rows]  -- ||x - k_mse|| (1e-8 when zero, :158).
+ *
+ * Host pointers vs device pointers: x, code_bits, res_bits, norms, r_norms,
+ * q, out and workspace are DEVICE pointers.  d (the +-1 Rademacher diagonal)
+ * and centroids are HOST float arrays read during the call and baked into the
+ * launch, so they may be freed as soon as the call returns.
+ */
+#ifndef KUDAHITAM_H_
+#define KUDAHITAM_H_
+
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+typedef enum kh_status {
+  KH_OK = 0,
+  KH_EINVAL = 1,   /* bad size / mode / pointer combination                 */
+  KH_EALIGN = 2,   /* a pointer or row stride is not 16-byte aligned         */
+  KH_ELAUNCH = 3,  /* the kernel launch was rejected (cudaGetLastError)      */
+  KH_ECUDA = 4,    /* another CUDA runtime / driver call failed              */
+  KH_ENOTSUP = 5   /* valid request the engine does not implement            */
+} kh_status;
+
+typedef enum kh_dtype { KH_F32 = 0, KH_F16 = 1, KH_BF16 = 2 } kh_dtype;
+
+/* Human readable name of a status code (static storage). */
+const char* kh_status_string(int status);
+
+/* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
+int kh_version(void);
+
+/* Sticky device-side error word of the current device (bounded waits that
+ * gave up set a bit).  Synchronous: reads device memory.  0 = no error. */
+int kh_device_error(uint32_t* out_flags);
+int kh_clear_device_error(void);
+
+/*
+ * kh_compress -- fused single-pass KV compression of one tensor.
+ * Replaces ultra_fused_full_fusion_cuda (KudaHitamCUDA.cu:197-231, kernel
+ * :13-195), the op called by KudahitamCompressorV2.compress
+ * (KudaHitamQuant_full.py:334,356).
+ *
+ *   x          device [n_rows rows] x [head_dim] elements of `dtype`, row r at
+ *              x + r*row_stride elements.  16-byte aligned; row_stride*elt
+ *              must be a multiple of 16 bytes.
+ *   d_host     head_dim floats, each +1 or -1.
+ *   centroids  n_centroids floats (2 -> bits=1 codebook, 4 -> bits=2), sorted
+ *              ascending.
+ *   residual   0: "1-bit mode" (code_bits + norms only; res_bits and r_norms
+ *              may be NULL).  1: the reference's full output (code + residual
+ *              sign plane + both norms).
+ * Outputs are written for rows [0, n_rows).  n_rows == 0 is a no-op.
+ */
+int kh_compress(const void* x, int dtype, int64_t n_rows, int head_dim,
+                int64_t row_stride, const float* d_host,
+                const float* centroids_host, int n_centroids, int residual,
+                uint32_t* code_bits, uint32_t* res_bits, float* norms,
+                float* r_norms, void* stream);
+
+/*
+ * kh_compress_batched -- the same compression over n_segments independent
+ * tensors (e.g. K and V of every layer) in ONE launch.  Array arguments are
+ * HOST arrays of length n_segments holding per-segment device pointers / row
+ * counts / row strides.  All segments share dtype, head_dim, d, centroids and
+ * mode.  n_segments <= kh_max_segments().
+ * No reference counterpart (the reference compresses one tensor per call,
+ * KudaHitamQuant_full.py:621-649); it batches the same op.
+ */
+int kh_max_segments(void);
+int kh_compress_batched(int n_segments, const void* const* x,
+                        const int64_t* n_rows, const int64_t* row_stride,
+                        uint32_t* const* code_bits, uint32_t* const* res_bits,
+                        float* const* norms, float* const* r_norms, int dtype,
+                        int head_dim, const float* d_host,
+                        const float* centroids_host, int n_centroids,
+                        int residual, void* stream);
+
+/*
+ * kh_fwht_inplace -- orthonormal Walsh-Hadamard transform of float rows
+ * (x <- H x / sqrt(D)), in place.  Replaces fwht_cuda_forward
+ * (KudaHitamCUDA.cu:233-283), reached from fwht() (KudaHitamQuant_full.py:207-215).
+ * head_dim is a power of two in [2, 1024]; rows are contiguous.
+ */
+int kh_fwht_inplace(float* x, int64_t n_rows, int head_dim, void* stream);
+
+/*
+ * kh_materialize -- expand a packed cache back to the reference kernel's
+ * output tensors: idx uint8[n,D], k_mse float[n,D], signs int8[n,D]
+ * (KudaHitamCUDA.cu:105-111, :141-149, :189-194).  Any output may be NULL;
+ * signs needs res_bits.  k_mse = norm * d (.) H(c[idx]) / sqrt(D).
+ */
+int kh_materialize(const uint32_t* code_bits, const uint32_t* res_bits,
+                   const float* norms, int64_t n_rows, int head_dim,
+                   const float* d_host, const float* centroids_host,
+                   int n_centroids, uint8_t* out_idx, float* out_kmse,
+                   int8_t* out_signs, void* stream);
+
+/*
+ * kh_score -- asymmetric attention scores straight from the packed cache.
+ * Replaces KudahitamCompressorV2.asymmetric_attention_scores
+ * (KudaHitamQuant_full.py:373-377):
+ *   out[g,j,s] = q_gj . k_mse_gs + (1/sqrt(D)) <fwht(q_gj (.) d), sign_gs> r_norm_gs
+ * evaluated as norm*<q~, c[idx]> + r_norm/sqrt(D) <q~, sign> with
+ * q~ = H(q (.) d)/sqrt(D).
+ *   q      device float [n_groups][n_q][D]
+ *   cache  rows of group g are rows [g*seq_len, (g+1)*seq_len) of the packed
+ *          cache; res_bits / r_norms may be NULL (1-bit mode: no QJL term).
+ *   out    device float [n_groups][n_q][seq_len]
+ */
+int kh_score(const float* q, int64_t n_groups, int n_q, int head_dim,
+             const uint32_t* code_bits, const uint32_t* res_bits,
+             const float* norms, const float* r_norms, int64_t seq_len,
+             const float* d_host, const float* centroids_host, int n_centroids,
+             float* out, void* stream);
+
+/*
+ * Decode attention over a compressed K/V cache (split-K / flash-decoding).
+ * Not present in the reference, which stops at the scores
+ * (KudaHitamQuant_full.py:373-386); softmax(score * sm_scale) . V_hat with
+ *   V_hat_s = d (.) H( norm_s c[idx_s] / sqrt(D)
+ *                      + r_norm_s sqrt(2/pi) / D * sign_s )
+ * (the MSE reconstruction of KudaHitamCUDA.cu:141-149 plus the MSE-optimal
+ * dequantisation of the 1-bit QJL residual).  Both caches must carry the
+ * residual plane (residual=1 at compression).
+ *
+ * kh_decode_partial: one query per group, cache rows [seq_begin, seq_end) of
+ * each group (group stride seq_len rows).  Writes n_splits partial records of
+ * (D+2) floats per group -- (running max, running sum-exp, D rotated-domain
+ * accumulators) -- at partials + (g*part_stride + part_offset + split)*(D+2).
+ * kh_decode_combine merges n_parts records per group and writes
+ * out[g][D] = d (.) H(sum acc) / sum l.
+ * kh_decode_attn = partial + combine using a caller workspace of
+ * kh_decode_workspace_bytes(n_groups, n_splits, D) bytes.
+ */
+int64_t kh_decode_workspace_bytes(int64_t n_groups, int n_splits, int head_dim);
+
+int kh_decode_partial(const float* q, int64_t n_groups, int head_dim,
+                      const uint32_t* k_code, const uint32_t* k_res,
+                      const float* k_norms, const float* k_rnorms,
+                      const uint32_t* v_code, const uint32_t* v_res,
+                      const float* v_norms, const float* v_rnorms,
+                      int64_t seq_len, int64_t seq_begin, int64_t seq_end,
+                      const float* d_k_host, const float* d_v_host,
+                      const float* centroids_host, int n_centroids,
+                      float sm_scale, int n_splits, float* partials,
+                      int64_t part_stride, int64_t part_offset, void* stream);
+
+int kh_decode_combine(const float* partials, int64_t n_groups, int n_parts,
+                      int head_dim, const float* d_v_host, float* out,
+                      void* stream);
+
+int kh_decode_attn(const float* q, int64_t n_groups, int head_dim,
+                   const uint32_t* k_code, const uint32_t* k_res,
+                   const float* k_norms, const float* k_rnorms,
+                   const uint32_t* v_code, const uint32_t* v_res,
+                   const float* v_norms, const float* v_rnorms,
+                   int64_t seq_len, const float* d_k_host,
+                   const float* d_v_host, const float* centroids_host,
+                   int n_centroids, float sm_scale, int n_splits,
+                   void* workspace, int64_t workspace_bytes, float* out,
+                   void* stream);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* KUDAHITAM_H_ */

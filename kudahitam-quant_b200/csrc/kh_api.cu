@@ -1,0 +1,380 @@
+// kh_api.cu -- the extern "C" boundary: argument validation, codebook
+// preparation and dispatch to the kernel translation units.
+//
+// Error convention (the reference extension has none: it relies on
+// data_ptr<T>() throwing and never checks launches, KudaHitamCUDA.cu:197-231):
+// every entry point validates its arguments, returns a kh_status, checks the
+// launch with cudaGetLastError and never aborts.
+#include <cmath>
+#include <cstring>
+#include <mutex>
+
+#include <cudaTypedefs.h>
+
+#include "kh_common.cuh"
+#include "kh_internal.h"
+
+namespace kh {
+
+__device__ uint32_t g_kh_device_error = 0;
+
+namespace {
+constexpr int kMaxDevices = 64;
+std::mutex g_mu;
+uint32_t* g_err_ptr[kMaxDevices] = {};
+int g_sms[kMaxDevices] = {};
+PFN_cuTensorMapEncodeTiled_v12000 g_encode = nullptr;
+
+bool aligned16(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; }
+bool aligned4(const void* p) { return (reinterpret_cast<uintptr_t>(p) & 3) == 0; }
+
+int current_device() {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return -1;
+  return dev;
+}
+}  // namespace
+
+uint32_t* device_error_ptr() {
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) return nullptr;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_err_ptr[dev]) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_kh_device_error) != cudaSuccess) return nullptr;
+    g_err_ptr[dev] = static_cast<uint32_t*>(p);
+  }
+  return g_err_ptr[dev];
+}
+
+int sm_count() {
+  const int dev = current_device();
+  if (dev < 0 || dev >= kMaxDevices) return 148;
+  std::lock_guard<std::mutex> lk(g_mu);
+  if (!g_sms[dev]) {
+    int n = 0;
+    cudaDeviceGetAttribute(&n, cudaDevAttrMultiProcessorCount, dev);
+    g_sms[dev] = n > 0 ? n : 148;
+  }
+  return g_sms[dev];
+}
+
+CUresult encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dt,
+                              void* base, uint64_t inner, uint64_t rows,
+                              uint64_t row_stride_bytes, uint32_t box_inner,
+                              uint32_t box_rows, CUtensorMapSwizzle swz) {
+  {
+    std::lock_guard<std::mutex> lk(g_mu);
+    if (!g_encode) {
+      void* fn = nullptr;
+      cudaDriverEntryPointQueryResult q;
+      if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &fn,
+                                  cudaEnableDefault, &q) != cudaSuccess ||
+          q != cudaDriverEntryPointSuccess || !fn)
+        return CUDA_ERROR_NOT_FOUND;
+      g_encode = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(fn);
+    }
+  }
+  const cuuint64_t gdim[2] = {inner, rows};
+  const cuuint64_t gstride[1] = {row_stride_bytes};
+  const cuuint32_t box[2] = {box_inner, box_rows};
+  const cuuint32_t estr[2] = {1, 1};
+  return g_encode(map, dt, 2, base, gdim, gstride, box, estr,
+                  CU_TENSOR_MAP_INTERLEAVE_NONE, swz,
+                  CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                  CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+}
+
+namespace {
+
+bool valid_head_dim(int D) { return D == 128 || D == 256; }
+
+// Builds the codebook constants; rejects unsorted or non-finite centroids.
+bool make_codebook(const float* c, int n_c, Codebook* cb) {
+  if (!c || (n_c != 2 && n_c != 4)) return false;
+  memset(cb, 0, sizeof(*cb));
+  cb->n_c = n_c;
+  for (int i = 0; i < n_c; ++i) {
+    if (!std::isfinite(c[i])) return false;
+    if (i > 0 && !(c[i] > c[i - 1])) return false;
+    cb->c[i] = c[i];
+  }
+  for (int i = 0; i + 1 < n_c; ++i) cb->mid[i] = (c[i] + c[i + 1]) * 0.5f;
+  if (n_c == 2) {
+    cb->kind = (c[0] == -c[1]) ? kCbSym2 : kCbGen2;
+    cb->sel[0] = cb->mid[0] - c[0];
+    cb->sel[1] = cb->mid[0] - c[1];
+  } else {
+    cb->kind = kCbGen4;
+  }
+  return true;
+}
+
+bool make_dflip(const float* d, int D, uint32_t* flip) {
+  if (!d) return false;
+  for (int i = 0; i < D; ++i) {
+    if (d[i] == 1.0f) flip[i] = 0u;
+    else if (d[i] == -1.0f) flip[i] = 0x80000000u;
+    else return false;
+  }
+  return true;
+}
+
+bool check_d(const float* d, int D) {
+  uint32_t tmp[256];
+  return D <= 256 && make_dflip(d, D, tmp);
+}
+
+int check_segment(const void* x, int dtype, int64_t n_rows, int D,
+                  int64_t row_stride, const uint32_t* code, const uint32_t* res,
+                  const float* norms, const float* rnorms, int residual) {
+  if (n_rows < 0 || n_rows >= (int64_t(1) << 31)) return KH_EINVAL;
+  if (n_rows == 0) return KH_OK;
+  if (!x || !code || !norms) return KH_EINVAL;
+  if (residual && (!res || !rnorms)) return KH_EINVAL;
+  if (row_stride < D) return KH_EINVAL;
+  if (!aligned16(x) || ((row_stride * dtype_size(dtype)) & 15) != 0) return KH_EALIGN;
+  if (!aligned16(code) || !aligned4(norms)) return KH_EALIGN;
+  if (residual && (!aligned16(res) || !aligned4(rnorms))) return KH_EALIGN;
+  return KH_OK;
+}
+
+}  // namespace
+}  // namespace kh
+
+using namespace kh;
+
+extern "C" {
+
+const char* kh_status_string(int status) {
+  switch (status) {
+    case KH_OK: return "ok";
+    case KH_EINVAL: return "invalid argument";
+    case KH_EALIGN: return "pointer or stride not 16-byte aligned";
+    case KH_ELAUNCH: return "kernel launch failed";
+    case KH_ECUDA: return "CUDA runtime/driver call failed";
+    case KH_ENOTSUP: return "not supported";
+  }
+  return "unknown status";
+}
+
+int kh_version(void) { return 100; }
+
+int kh_device_error(uint32_t* out_flags) {
+  if (!out_flags) return KH_EINVAL;
+  uint32_t v = 0;
+  if (cudaMemcpyFromSymbol(&v, g_kh_device_error, sizeof(v)) != cudaSuccess)
+    return KH_ECUDA;
+  *out_flags = v;
+  return KH_OK;
+}
+
+int kh_clear_device_error(void) {
+  const uint32_t z = 0;
+  return cudaMemcpyToSymbol(g_kh_device_error, &z, sizeof(z)) == cudaSuccess
+             ? KH_OK
+             : KH_ECUDA;
+}
+
+int kh_max_segments(void) { return kMaxSegments; }
+
+int kh_compress(const void* x, int dtype, int64_t n_rows, int head_dim,
+                int64_t row_stride, const float* d_host,
+                const float* centroids_host, int n_centroids, int residual,
+                uint32_t* code_bits, uint32_t* res_bits, float* norms,
+                float* r_norms, void* stream) {
+  const void* xs[1] = {x};
+  const int64_t nr[1] = {n_rows};
+  const int64_t rs[1] = {row_stride};
+  uint32_t* cb[1] = {code_bits};
+  uint32_t* rb[1] = {res_bits};
+  float* nm[1] = {norms};
+  float* rn[1] = {r_norms};
+  return kh_compress_batched(1, xs, nr, rs, cb, rb, nm, rn, dtype, head_dim,
+                             d_host, centroids_host, n_centroids, residual,
+                             stream);
+}
+
+int kh_compress_batched(int n_segments, const void* const* x,
+                        const int64_t* n_rows, const int64_t* row_stride,
+                        uint32_t* const* code_bits, uint32_t* const* res_bits,
+                        float* const* norms, float* const* r_norms, int dtype,
+                        int head_dim, const float* d_host,
+                        const float* centroids_host, int n_centroids,
+                        int residual, void* stream) {
+  if (n_segments < 0 || n_segments > kMaxSegments) return KH_EINVAL;
+  if (dtype != KH_F32 && dtype != KH_F16 && dtype != KH_BF16) return KH_EINVAL;
+  if (!valid_head_dim(head_dim)) return KH_EINVAL;
+  if (residual != 0 && residual != 1) return KH_EINVAL;
+  if (n_segments == 0) return KH_OK;
+  if (!x || !n_rows || !row_stride || !code_bits || !norms) return KH_EINVAL;
+  if (residual && (!res_bits || !r_norms)) return KH_EINVAL;
+
+  static thread_local CompressRequest req;
+  memset(&req, 0, sizeof(req));
+  req.dtype = dtype;
+  req.head_dim = head_dim;
+  req.residual = residual;
+  if (!make_codebook(centroids_host, n_centroids, &req.cb)) return KH_EINVAL;
+  if (!make_dflip(d_host, head_dim, req.dflip)) return KH_EINVAL;
+  req.n_seg = n_segments;
+  int64_t total_rows = 0;
+  for (int i = 0; i < n_segments; ++i) {
+    uint32_t* rb = residual ? res_bits[i] : nullptr;
+    float* rn = residual ? r_norms[i] : nullptr;
+    const int st = check_segment(x[i], dtype, n_rows[i], head_dim,
+                                 row_stride[i], code_bits[i], rb, norms[i], rn,
+                                 residual);
+    if (st != KH_OK) return st;
+    req.seg[i] = CompressSegHost{x[i], n_rows[i], row_stride[i], code_bits[i],
+                                 rb, norms[i], rn};
+    total_rows += n_rows[i];
+  }
+  if (total_rows == 0) return KH_OK;
+  return launch_compress(req, static_cast<cudaStream_t>(stream));
+}
+
+int kh_fwht_inplace(float* x, int64_t n_rows, int head_dim, void* stream) {
+  if (n_rows < 0 || head_dim < 2 || head_dim > 1024 ||
+      (head_dim & (head_dim - 1)) != 0)
+    return KH_EINVAL;
+  if (n_rows == 0) return KH_OK;
+  if (!x) return KH_EINVAL;
+  if (!aligned4(x)) return KH_EALIGN;
+  return launch_fwht(x, n_rows, head_dim, static_cast<cudaStream_t>(stream));
+}
+
+int kh_materialize(const uint32_t* code_bits, const uint32_t* res_bits,
+                   const float* norms, int64_t n_rows, int head_dim,
+                   const float* d_host, const float* centroids_host,
+                   int n_centroids, uint8_t* out_idx, float* out_kmse,
+                   int8_t* out_signs, void* stream) {
+  if (n_rows < 0 || !valid_head_dim(head_dim)) return KH_EINVAL;
+  Codebook cb;
+  if (!make_codebook(centroids_host, n_centroids, &cb)) return KH_EINVAL;
+  if (!check_d(d_host, head_dim)) return KH_EINVAL;
+  if (n_rows == 0) return KH_OK;
+  if (!code_bits) return KH_EINVAL;
+  if (out_kmse && !norms) return KH_EINVAL;
+  if (out_signs && !res_bits) return KH_EINVAL;
+  if (!aligned4(code_bits) || (res_bits && !aligned4(res_bits)) ||
+      (out_kmse && !aligned4(out_kmse)))
+    return KH_EALIGN;
+  return launch_materialize(code_bits, res_bits, norms, n_rows, head_dim,
+                            d_host, cb, out_idx, out_kmse, out_signs,
+                            static_cast<cudaStream_t>(stream));
+}
+
+int kh_score(const float* q, int64_t n_groups, int n_q, int head_dim,
+             const uint32_t* code_bits, const uint32_t* res_bits,
+             const float* norms, const float* r_norms, int64_t seq_len,
+             const float* d_host, const float* centroids_host, int n_centroids,
+             float* out, void* stream) {
+  if (n_groups < 0 || n_q < 0 || seq_len < 0 || !valid_head_dim(head_dim))
+    return KH_EINVAL;
+  if (n_groups >= 65536) return KH_EINVAL;  // grid.y limit
+  Codebook cb;
+  if (!make_codebook(centroids_host, n_centroids, &cb)) return KH_EINVAL;
+  if (!check_d(d_host, head_dim)) return KH_EINVAL;
+  if ((res_bits == nullptr) != (r_norms == nullptr)) return KH_EINVAL;
+  if (n_groups == 0 || n_q == 0 || seq_len == 0) return KH_OK;
+  if (!q || !code_bits || !norms || !out) return KH_EINVAL;
+  if (!aligned16(code_bits) || (res_bits && !aligned16(res_bits)) ||
+      !aligned4(q) || !aligned4(out))
+    return KH_EALIGN;
+  return launch_score(q, n_groups, n_q, head_dim, code_bits, res_bits, norms,
+                      r_norms, seq_len, d_host, cb, out,
+                      static_cast<cudaStream_t>(stream));
+}
+
+int64_t kh_decode_workspace_bytes(int64_t n_groups, int n_splits,
+                                  int head_dim) {
+  if (n_groups < 0 || n_splits < 1 || !valid_head_dim(head_dim)) return -1;
+  return n_groups * (int64_t)n_splits * (head_dim + 2) * (int64_t)sizeof(float);
+}
+
+int kh_decode_partial(const float* q, int64_t n_groups, int head_dim,
+                      const uint32_t* k_code, const uint32_t* k_res,
+                      const float* k_norms, const float* k_rnorms,
+                      const uint32_t* v_code, const uint32_t* v_res,
+                      const float* v_norms, const float* v_rnorms,
+                      int64_t seq_len, int64_t seq_begin, int64_t seq_end,
+                      const float* d_k_host, const float* d_v_host,
+                      const float* centroids_host, int n_centroids,
+                      float sm_scale, int n_splits, float* partials,
+                      int64_t part_stride, int64_t part_offset, void* stream) {
+  (void)d_v_host;  // V's diagonal is applied by the combine step
+  if (n_groups < 0 || n_groups >= 65536 || !valid_head_dim(head_dim))
+    return KH_EINVAL;
+  if (n_splits < 1 || n_splits > 65535) return KH_EINVAL;
+  if (seq_len < 0 || seq_begin < 0 || seq_end < seq_begin || seq_end > seq_len)
+    return KH_EINVAL;
+  if (part_offset < 0 || part_stride < part_offset + n_splits) return KH_EINVAL;
+  if (!std::isfinite(sm_scale)) return KH_EINVAL;
+  DecodeRequest r;
+  memset(&r, 0, sizeof(r));
+  if (!make_codebook(centroids_host, n_centroids, &r.cb)) return KH_EINVAL;
+  if (n_centroids != 2) return KH_ENOTSUP;  // decode supports the bits=1 codebook
+  if (!check_d(d_k_host, head_dim)) return KH_EINVAL;
+  if (n_groups == 0) return KH_OK;
+  if (!q || !partials) return KH_EINVAL;
+  if (seq_end > seq_begin &&
+      (!k_code || !k_res || !k_norms || !k_rnorms || !v_code || !v_res ||
+       !v_norms || !v_rnorms))
+    return KH_EINVAL;
+  if (!aligned16(k_code) || !aligned16(k_res) || !aligned16(v_code) ||
+      !aligned16(v_res) || !aligned4(q) || !aligned4(partials))
+    return KH_EALIGN;
+  for (int i = 0; i < head_dim; ++i) r.dk[i] = d_k_host[i];
+  r.q = q;
+  r.n_groups = n_groups;
+  r.D = head_dim;
+  r.k_code = k_code; r.k_res = k_res; r.k_norms = k_norms; r.k_rnorms = k_rnorms;
+  r.v_code = v_code; r.v_res = v_res; r.v_norms = v_norms; r.v_rnorms = v_rnorms;
+  r.seq_len = seq_len; r.seq_begin = seq_begin; r.seq_end = seq_end;
+  r.sm_scale = sm_scale;
+  r.n_splits = n_splits;
+  r.partials = partials;
+  r.part_stride = part_stride;
+  r.part_offset = part_offset;
+  return launch_decode_partial(r, static_cast<cudaStream_t>(stream));
+}
+
+int kh_decode_combine(const float* partials, int64_t n_groups, int n_parts,
+                      int head_dim, const float* d_v_host, float* out,
+                      void* stream) {
+  if (n_groups < 0 || n_parts < 1 || !valid_head_dim(head_dim)) return KH_EINVAL;
+  if (!check_d(d_v_host, head_dim)) return KH_EINVAL;
+  if (n_groups == 0) return KH_OK;
+  if (!partials || !out) return KH_EINVAL;
+  if (!aligned4(partials) || !aligned4(out)) return KH_EALIGN;
+  return launch_decode_combine(partials, n_groups, n_parts, head_dim, d_v_host,
+                               out, static_cast<cudaStream_t>(stream));
+}
+
+int kh_decode_attn(const float* q, int64_t n_groups, int head_dim,
+                   const uint32_t* k_code, const uint32_t* k_res,
+                   const float* k_norms, const float* k_rnorms,
+                   const uint32_t* v_code, const uint32_t* v_res,
+                   const float* v_norms, const float* v_rnorms,
+                   int64_t seq_len, const float* d_k_host,
+                   const float* d_v_host, const float* centroids_host,
+                   int n_centroids, float sm_scale, int n_splits,
+                   void* workspace, int64_t workspace_bytes, float* out,
+                   void* stream) {
+  const int64_t need = kh_decode_workspace_bytes(n_groups, n_splits, head_dim);
+  if (need < 0) return KH_EINVAL;
+  if (n_groups == 0) return KH_OK;
+  if (!workspace || workspace_bytes < need) return KH_EINVAL;
+  int st = kh_decode_partial(q, n_groups, head_dim, k_code, k_res, k_norms,
+                             k_rnorms, v_code, v_res, v_norms, v_rnorms,
+                             seq_len, 0, seq_len, d_k_host, d_v_host,
+                             centroids_host, n_centroids, sm_scale, n_splits,
+                             static_cast<float*>(workspace), n_splits, 0,
+                             stream);
+  if (st != KH_OK) return st;
+  return kh_decode_combine(static_cast<const float*>(workspace), n_groups,
+                           n_splits, head_dim, d_v_host, out, stream);
+}
+
+}  // extern "C"

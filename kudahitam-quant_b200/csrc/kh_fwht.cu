@@ -1,0 +1,156 @@
+// kh_fwht.cu -- standalone orthonormal FWHT (the query projection) and the
+// packed-cache materialiser (reference-layout idx / k_mse / signs).
+#include <cmath>
+
+#include "kh_common.cuh"
+#include "kh_internal.h"
+
+namespace kh {
+namespace {
+
+// In-place x <- H x / sqrt(D) for rows of D floats, D a power of two <= 1024.
+// Same semantics as fwht_cuda_forward_kernel (KudaHitamCUDA.cu:233-273):
+// unnormalised Sylvester butterflies, then one multiply by 1/sqrt(D)
+// (:270-272).  A block stages kRowsPerBlock rows in shared memory.
+__global__ void __launch_bounds__(256)
+    fwht_rows_kernel(float* __restrict__ x, int64_t n_rows, int D,
+                     int rows_per_block) {
+  extern __shared__ float sh[];
+  const int64_t row0 = (int64_t)blockIdx.x * rows_per_block;
+  const int nr = (int)(n_rows - row0 < rows_per_block ? n_rows - row0 : rows_per_block);
+  const int n = nr * D;
+  float* g = x + row0 * D;
+  for (int i = threadIdx.x; i < n; i += blockDim.x) sh[i] = g[i];
+  __syncthreads();
+  for (int h = 1; h < D; h <<= 1) {
+    // n/2 butterflies per stage
+    for (int b = threadIdx.x; b < n / 2; b += blockDim.x) {
+      const int row = b / (D / 2);
+      const int k = b % (D / 2);
+      const int lo = row * D + (k / h) * 2 * h + (k % h);
+      const float a = sh[lo], c = sh[lo + h];
+      sh[lo] = a + c;
+      sh[lo + h] = a - c;
+    }
+    __syncthreads();
+  }
+  const float scale = 1.0f / sqrtf((float)D);
+  for (int i = threadIdx.x; i < n; i += blockDim.x) g[i] = sh[i] * scale;
+}
+
+struct alignas(16) MatParams {
+  const uint32_t* code;
+  const uint32_t* res;
+  const float* norms;
+  uint8_t* idx;
+  float* kmse;
+  int8_t* signs;
+  int64_t n_rows;
+  Codebook cb;
+  float d[256];
+};
+
+// One warp per row; lane l holds elements l + 32 j, j < D/32 (coalesced
+// writes).  Butterfly stages on element bits 0..4 exchange across lanes,
+// stages on bits 5.. stay in registers.
+template <int D, int NC>
+__global__ void __launch_bounds__(256)
+    materialize_kernel(const __grid_constant__ MatParams P) {
+  constexpr int J = D / 32;
+  constexpr int kWords = (NC == 2) ? D / 32 : D / 16;
+  const int lane = threadIdx.x & 31;
+  const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  if (row >= P.n_rows) return;  // whole warp exits together
+
+  const uint32_t* cw = P.code + row * kWords;
+  uint32_t idx[J];
+  float r[J];
+#pragma unroll
+  for (int j = 0; j < J; ++j) {
+    const int e = lane + 32 * j;
+    if (NC == 2) idx[j] = (cw[e >> 5] >> (e & 31)) & 1u;
+    else idx[j] = (cw[e >> 4] >> (2 * (e & 15))) & 3u;
+    r[j] = P.cb.c[idx[j]];
+  }
+  if (P.idx) {
+#pragma unroll
+    for (int j = 0; j < J; ++j) P.idx[row * D + lane + 32 * j] = (uint8_t)idx[j];
+  }
+  if (P.kmse) {
+#pragma unroll
+    for (int h = 1; h < 32; h <<= 1) {
+#pragma unroll
+      for (int j = 0; j < J; ++j) {
+        const float o = __shfl_xor_sync(0xffffffffu, r[j], h);
+        r[j] = (lane & h) ? (o - r[j]) : (r[j] + o);
+      }
+    }
+#pragma unroll
+    for (int h = 1; h < J; h <<= 1) {
+#pragma unroll
+      for (int j = 0; j < J; ++j) {
+        if ((j & h) == 0) {
+          const float a = r[j], b = r[j + h];
+          r[j] = a + b;
+          r[j + h] = a - b;
+        }
+      }
+    }
+    // k_mse = r * m_base * d, m_base = (1/sqrt(D)) * norm (KudaHitamCUDA.cu:142-148)
+    const float m_base = (1.0f / sqrtf((float)D)) * P.norms[row];
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const int e = lane + 32 * j;
+      P.kmse[row * D + e] = r[j] * m_base * P.d[e];
+    }
+  }
+  if (P.signs) {
+    const uint32_t* rw = P.res + row * (D / 32);
+#pragma unroll
+    for (int j = 0; j < J; ++j) {
+      const int e = lane + 32 * j;
+      P.signs[row * D + e] = ((rw[e >> 5] >> (e & 31)) & 1u) ? (int8_t)1 : (int8_t)-1;
+    }
+  }
+}
+
+}  // namespace
+
+kh_status launch_fwht(float* x, int64_t n_rows, int D, cudaStream_t stream) {
+  const int rows_per_block = D >= 2048 ? 1 : 2048 / D;
+  const int64_t blocks = (n_rows + rows_per_block - 1) / rows_per_block;
+  if (blocks > 0x7fffffff) return KH_EINVAL;
+  const size_t smem = (size_t)rows_per_block * D * sizeof(float);
+  fwht_rows_kernel<<<(unsigned)blocks, 256, smem, stream>>>(x, n_rows, D,
+                                                            rows_per_block);
+  return cudaGetLastError() == cudaSuccess ? KH_OK : KH_ELAUNCH;
+}
+
+kh_status launch_materialize(const uint32_t* code, const uint32_t* res,
+                             const float* norms, int64_t n_rows, int D,
+                             const float* d, const Codebook& cb, uint8_t* idx,
+                             float* kmse, int8_t* signs, cudaStream_t stream) {
+  MatParams P;
+  P.code = code;
+  P.res = res;
+  P.norms = norms;
+  P.idx = idx;
+  P.kmse = kmse;
+  P.signs = signs;
+  P.n_rows = n_rows;
+  P.cb = cb;
+  for (int i = 0; i < D; ++i) P.d[i] = d[i];
+  const int64_t blocks = (n_rows + 7) / 8;
+  if (blocks > 0x7fffffff) return KH_EINVAL;
+  const unsigned g = (unsigned)blocks;
+  if (D == 128) {
+    if (cb.n_c == 2) materialize_kernel<128, 2><<<g, 256, 0, stream>>>(P);
+    else materialize_kernel<128, 4><<<g, 256, 0, stream>>>(P);
+  } else {
+    if (cb.n_c == 2) materialize_kernel<256, 2><<<g, 256, 0, stream>>>(P);
+    else materialize_kernel<256, 4><<<g, 256, 0, stream>>>(P);
+  }
+  return cudaGetLastError() == cudaSuccess ? KH_OK : KH_ELAUNCH;
+}
+
+}  // namespace kh

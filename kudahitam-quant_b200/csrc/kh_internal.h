@@ -1,0 +1,102 @@
+// kh_internal.h -- host-side interfaces between the C-ABI layer (kh_api.cu)
+// and the kernel translation units.  Not part of the public ABI.
+#pragma once
+
+#include <cuda.h>
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "kudahitam.h"
+
+namespace kh {
+
+constexpr int kMaxSegments = 64;
+
+// Codebook kinds the compress kernels specialise on.
+enum CodebookKind : int {
+  kCbSym2 = 0,  // 2 levels, c0 == -c1 exactly (the Lloyd-Max bits=1 codebook)
+  kCbGen2 = 1,  // 2 levels, arbitrary sorted values
+  kCbGen4 = 2,  // 4 levels (bits=2 codebook), sorted ascending
+};
+
+// Per-call constants baked into every launch (passed by value).
+struct Codebook {
+  int kind;        // CodebookKind
+  int n_c;         // 2 or 4
+  float c[4];      // centroids, ascending
+  float mid[3];    // decision midpoints (c[i] + c[i+1]) / 2, float
+  float sel[2];    // kCbGen2: mid[0] - c[0], mid[0] - c[1]
+};
+
+struct CompressSegHost {
+  const void* x;
+  int64_t n_rows;
+  int64_t row_stride;  // elements
+  uint32_t* code;
+  uint32_t* res;
+  float* norms;
+  float* rnorms;
+};
+
+struct CompressRequest {
+  int dtype;  // kh_dtype
+  int head_dim;
+  int residual;
+  Codebook cb;
+  uint32_t dflip[256];  // per element: 0 or 0x80000000 (sign flip for d=-1)
+  int n_seg;
+  CompressSegHost seg[kMaxSegments];
+};
+
+// Launch the fused compression kernel.  Arguments are already validated.
+kh_status launch_compress(const CompressRequest& req, cudaStream_t stream);
+
+// Materialise reference-layout tensors from a packed cache.
+kh_status launch_materialize(const uint32_t* code, const uint32_t* res,
+                             const float* norms, int64_t n_rows, int D,
+                             const float* d, const Codebook& cb, uint8_t* idx,
+                             float* kmse, int8_t* signs, cudaStream_t stream);
+
+kh_status launch_fwht(float* x, int64_t n_rows, int D, cudaStream_t stream);
+
+kh_status launch_score(const float* q, int64_t n_groups, int n_q, int D,
+                       const uint32_t* code, const uint32_t* res,
+                       const float* norms, const float* rnorms,
+                       int64_t seq_len, const float* d, const Codebook& cb,
+                       float* out, cudaStream_t stream);
+
+struct DecodeRequest {
+  const float* q;
+  int64_t n_groups;
+  int D;
+  const uint32_t *k_code, *k_res, *v_code, *v_res;
+  const float *k_norms, *k_rnorms, *v_norms, *v_rnorms;
+  int64_t seq_len, seq_begin, seq_end;
+  float dk[256];
+  Codebook cb;
+  float sm_scale;
+  int n_splits;
+  float* partials;
+  int64_t part_stride, part_offset;
+};
+
+kh_status launch_decode_partial(const DecodeRequest& r, cudaStream_t stream);
+kh_status launch_decode_combine(const float* partials, int64_t n_groups,
+                                int n_parts, int D, const float* dv,
+                                float* out, cudaStream_t stream);
+
+// Device address of the sticky error word on the current device.
+uint32_t* device_error_ptr();
+
+// Number of SMs of the current device (cached per device).
+int sm_count();
+
+// Resolve cuTensorMapEncodeTiled through the runtime (no -lcuda needed).
+CUresult encode_tensor_map_2d(CUtensorMap* map, CUtensorMapDataType dt,
+                              void* base, uint64_t inner, uint64_t rows,
+                              uint64_t row_stride_bytes, uint32_t box_inner,
+                              uint32_t box_rows, CUtensorMapSwizzle swz);
+
+inline int dtype_size(int dtype) { return dtype == KH_F32 ? 4 : 2; }
+
+}  // namespace kh

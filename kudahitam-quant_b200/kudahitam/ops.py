@@ -1,0 +1,316 @@
+"""Torch-facing operators over the C ABI.
+
+Each op takes CUDA tensors, allocates its outputs with PyTorch's caching
+allocator, and launches on the tensor's device and its current stream.  There
+is no CPU path: CPU inputs raise ``ValueError`` and a missing engine raises
+``NativeLibraryError``.
+"""
+from __future__ import annotations
+
+import ctypes
+import math
+from dataclasses import dataclass
+from typing import Optional, Sequence
+
+import torch
+
+from . import _lib
+
+_DTYPE_CODE = {torch.float32: _lib.KH_F32, torch.float16: _lib.KH_F16,
+               torch.bfloat16: _lib.KH_BF16}
+
+HEAD_DIMS = (128, 256)
+
+
+def _vp(t: Optional[torch.Tensor]) -> Optional[ctypes.c_void_p]:
+    return None if t is None else ctypes.c_void_p(t.data_ptr())
+
+
+def _host_f32(t) -> torch.Tensor:
+    """Contiguous float32 CPU copy (d vectors and centroids travel by value)."""
+    t = torch.as_tensor(t)
+    return t.detach().to(device="cpu", dtype=torch.float32).contiguous()
+
+
+def _stream(device: torch.device) -> ctypes.c_void_p:
+    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+
+
+def _require_cuda(*ts: Optional[torch.Tensor]) -> torch.device:
+    dev = None
+    for t in ts:
+        if t is None:
+            continue
+        if not t.is_cuda:
+            raise ValueError("kudahitam ops run on CUDA tensors only (no CPU path)")
+        if dev is None:
+            dev = t.device
+        elif t.device != dev:
+            raise ValueError(f"tensors on different devices: {dev} vs {t.device}")
+    return dev
+
+
+def _rows(x: torch.Tensor) -> tuple[torch.Tensor, int]:
+    """[N, D] view with unit inner stride and a 16-byte row pitch (copies
+    only when the layout does not allow it)."""
+    D = x.shape[-1]
+    x2 = x.reshape(-1, D)
+    elt = x2.element_size()
+    ok = (x2.stride(-1) == 1 and x2.data_ptr() % 16 == 0
+          and (x2.shape[0] <= 1 or (x2.stride(0) * elt) % 16 == 0))
+    if not ok:
+        x2 = x2.contiguous()
+    stride = x2.stride(0) if x2.shape[0] > 1 else D
+    return x2, stride
+
+
+@dataclass
+class PackedKV:
+    """The packed cache of one tensor of N = prod(shape[:-1]) rows.
+
+    code   int32 [N, D/32] (bits=1) or [N, D/16] (bits=2), bit patterns of the
+           uint32 words described in include/kudahitam.h
+    res    int32 [N, D/32] residual sign plane, or None (1-bit mode)
+    norms  float32 [N]
+    rnorms float32 [N] or None
+    """
+    shape: tuple
+    bits: int
+    code: torch.Tensor
+    norms: torch.Tensor
+    res: Optional[torch.Tensor] = None
+    rnorms: Optional[torch.Tensor] = None
+
+    @property
+    def head_dim(self) -> int:
+        return int(self.shape[-1])
+
+    @property
+    def n_rows(self) -> int:
+        return int(self.norms.numel())
+
+    @property
+    def residual(self) -> bool:
+        return self.res is not None
+
+    @property
+    def device(self) -> torch.device:
+        return self.norms.device
+
+    def nbytes(self) -> int:
+        return sum(t.numel() * t.element_size() for t in
+                   (self.code, self.norms, self.res, self.rnorms) if t is not None)
+
+    def rows(self, start: int, stop: int) -> "PackedKV":
+        """Rows [start, stop) as a flat PackedKV (views, no copy)."""
+        sl = slice(start, stop)
+        return PackedKV((stop - start, self.head_dim), self.bits, self.code[sl],
+                        self.norms[sl], None if self.res is None else self.res[sl],
+                        None if self.rnorms is None else self.rnorms[sl])
+
+
+def empty_packed(shape, bits: int, residual: bool, device) -> PackedKV:
+    D = int(shape[-1])
+    n = math.prod(int(s) for s in shape[:-1])
+    words = D // 32 if bits == 1 else D // 16
+    return PackedKV(tuple(int(s) for s in shape), bits,
+                    torch.empty((n, words), dtype=torch.int32, device=device),
+                    torch.empty(n, dtype=torch.float32, device=device),
+                    torch.empty((n, D // 32), dtype=torch.int32, device=device) if residual else None,
+                    torch.empty(n, dtype=torch.float32, device=device) if residual else None)
+
+
+def _check_codebook(centroids: torch.Tensor) -> tuple[int, int]:
+    n_c = centroids.numel()
+    if n_c not in (2, 4):
+        raise ValueError(f"codebook must have 2 or 4 levels, got {n_c}")
+    return n_c, (1 if n_c == 2 else 2)
+
+
+def compress(x: torch.Tensor, d, centroids, residual: bool = True,
+             out: Optional[PackedKV] = None) -> PackedKV:
+    """Fused compression of the rows x[..., D] (fp32 / fp16 / bf16, D in
+    {128, 256}).  Replaces ``ultra_fused_full_fusion`` (KudaHitamCUDA.cu:197-231)."""
+    dev = _require_cuda(x)
+    if x.dtype not in _DTYPE_CODE:
+        raise TypeError(f"unsupported dtype {x.dtype}")
+    D = x.shape[-1]
+    if D not in HEAD_DIMS:
+        raise ValueError(f"head_dim must be 128 or 256, got {D}")
+    dh, ch = _host_f32(d), _host_f32(centroids)
+    n_c, bits = _check_codebook(ch)
+    x2, stride = _rows(x)
+    if out is None:
+        out = empty_packed(x.shape, bits, residual, dev)
+    with torch.cuda.device(dev):
+        _lib.call("kh_compress", _vp(x2), _DTYPE_CODE[x.dtype], x2.shape[0], D, stride,
+                  _vp(dh), _vp(ch), n_c, int(residual), _vp(out.code), _vp(out.res),
+                  _vp(out.norms), _vp(out.rnorms), _stream(dev))
+    return out
+
+
+def compress_many(xs: Sequence[torch.Tensor], d, centroids, residual: bool = True,
+                  outs: Optional[Sequence[PackedKV]] = None) -> list[PackedKV]:
+    """Compress several tensors (same dtype and head_dim) in one launch per
+    kh_max_segments() tensors."""
+    if not xs:
+        return []
+    dev = _require_cuda(*xs)
+    dt = xs[0].dtype
+    D = xs[0].shape[-1]
+    if any(t.dtype != dt or t.shape[-1] != D for t in xs):
+        raise ValueError("compress_many needs one dtype and one head_dim")
+    if dt not in _DTYPE_CODE or D not in HEAD_DIMS:
+        raise ValueError("unsupported dtype / head_dim")
+    dh, ch = _host_f32(d), _host_f32(centroids)
+    n_c, bits = _check_codebook(ch)
+    outs = list(outs) if outs is not None else [empty_packed(t.shape, bits, residual, dev)
+                                                for t in xs]
+    rows = [_rows(t) for t in xs]
+    maxseg = _lib.lib().kh_max_segments()
+    with torch.cuda.device(dev):
+        for i0 in range(0, len(xs), maxseg):
+            sl = range(i0, min(len(xs), i0 + maxseg))
+            n = len(sl)
+            P = ctypes.c_void_p * n
+            I = ctypes.c_int64 * n
+            args = [
+                P(*[rows[i][0].data_ptr() for i in sl]),
+                I(*[rows[i][0].shape[0] for i in sl]),
+                I(*[rows[i][1] for i in sl]),
+                P(*[outs[i].code.data_ptr() for i in sl]),
+                P(*[(outs[i].res.data_ptr() if residual else 0) for i in sl]),
+                P(*[outs[i].norms.data_ptr() for i in sl]),
+                P(*[(outs[i].rnorms.data_ptr() if residual else 0) for i in sl]),
+            ]
+            _lib.call("kh_compress_batched", n, *[ctypes.cast(a, ctypes.c_void_p) for a in args],
+                      _DTYPE_CODE[dt], D, _vp(dh), _vp(ch), n_c, int(residual), _stream(dev))
+    return outs
+
+
+def fwht_(x: torch.Tensor) -> torch.Tensor:
+    """In-place orthonormal FWHT of contiguous float32 rows (the reference's
+    ``cuda_ext.forward``, KudaHitamCUDA.cu:275-283)."""
+    dev = _require_cuda(x)
+    if x.dtype != torch.float32 or not x.is_contiguous():
+        raise ValueError("fwht_ needs a contiguous float32 tensor")
+    D = x.shape[-1]
+    with torch.cuda.device(dev):
+        _lib.call("kh_fwht_inplace", _vp(x), x.numel() // D if D else 0, D, _stream(dev))
+    return x
+
+
+def fwht(x: torch.Tensor) -> torch.Tensor:
+    """Orthonormal FWHT along the last dim (returns a new float32 tensor)."""
+    return fwht_(x.to(torch.float32).contiguous().clone())
+
+
+def materialize(p: PackedKV, d, centroids, idx: bool = True, kmse: bool = True,
+                signs: bool = True) -> dict:
+    """Reference-layout tensors from a packed cache: idx uint8 [N, D],
+    k_mse float32 [N, D], signs int8 [N, D]."""
+    dev = p.device
+    D, n = p.head_dim, p.n_rows
+    dh, ch = _host_f32(d), _host_f32(centroids)
+    n_c = ch.numel()
+    o_idx = torch.empty((n, D), dtype=torch.uint8, device=dev) if idx else None
+    o_k = torch.empty((n, D), dtype=torch.float32, device=dev) if kmse else None
+    o_s = torch.empty((n, D), dtype=torch.int8, device=dev) if (signs and p.res is not None) else None
+    with torch.cuda.device(dev):
+        _lib.call("kh_materialize", _vp(p.code), _vp(p.res), _vp(p.norms), n, D, _vp(dh),
+                  _vp(ch), n_c, _vp(o_idx), _vp(o_k), _vp(o_s), _stream(dev))
+    return {"idx": o_idx, "kmse": o_k, "signs": o_s}
+
+
+def score(q: torch.Tensor, p: PackedKV, d, centroids, seq_len: Optional[int] = None
+          ) -> torch.Tensor:
+    """Asymmetric scores of q [G, nq, D] against G groups of seq_len cached
+    rows each (rows of group g are rows [g*seq_len, (g+1)*seq_len) of p).
+    Returns float32 [G, nq, seq_len]."""
+    dev = _require_cuda(q, p.norms)
+    G, nq, D = q.shape
+    if D != p.head_dim:
+        raise ValueError("query head_dim does not match the cache")
+    S = p.n_rows // max(G, 1) if seq_len is None else int(seq_len)
+    if G * S != p.n_rows:
+        raise ValueError(f"{p.n_rows} cached rows do not split into {G} groups of {S}")
+    qf = q.to(torch.float32).contiguous()
+    dh, ch = _host_f32(d), _host_f32(centroids)
+    out = torch.empty((G, nq, S), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        _lib.call("kh_score", _vp(qf), G, nq, D, _vp(p.code), _vp(p.res), _vp(p.norms),
+                  _vp(p.rnorms), S, _vp(dh), _vp(ch), ch.numel(), _vp(out), _stream(dev))
+    return out
+
+
+def decode_workspace_bytes(n_groups: int, n_splits: int, head_dim: int) -> int:
+    return int(_lib.lib().kh_decode_workspace_bytes(n_groups, n_splits, head_dim))
+
+
+def default_splits(n_groups: int, seq_len: int, device) -> int:
+    """Enough (group, split) blocks to fill every SM a few times over."""
+    sms = torch.cuda.get_device_properties(device).multi_processor_count
+    want = max(1, (4 * sms + n_groups - 1) // max(n_groups, 1))
+    return int(max(1, min(want, seq_len // 256 if seq_len >= 256 else 1, 1024)))
+
+
+def decode_partial(q: torch.Tensor, k: PackedKV, v: PackedKV, dk, dv, centroids,
+                   sm_scale: float, n_splits: int, partials: torch.Tensor,
+                   part_stride: int, part_offset: int, seq_len: int,
+                   seq_begin: int = 0, seq_end: Optional[int] = None) -> torch.Tensor:
+    dev = _require_cuda(q, k.norms, v.norms, partials)
+    G, D = q.shape
+    seq_end = seq_len if seq_end is None else seq_end
+    if not (k.residual and v.residual):
+        raise ValueError("decode attention needs caches compressed with the residual plane")
+    qf = q.to(torch.float32).contiguous()
+    dkh, dvh, ch = _host_f32(dk), _host_f32(dv), _host_f32(centroids)
+    with torch.cuda.device(dev):
+        _lib.call("kh_decode_partial", _vp(qf), G, D, _vp(k.code), _vp(k.res), _vp(k.norms),
+                  _vp(k.rnorms), _vp(v.code), _vp(v.res), _vp(v.norms), _vp(v.rnorms),
+                  seq_len, seq_begin, seq_end, _vp(dkh), _vp(dvh), _vp(ch), ch.numel(),
+                  float(sm_scale), n_splits, _vp(partials), part_stride, part_offset,
+                  _stream(dev))
+    return partials
+
+
+def decode_combine(partials: torch.Tensor, n_parts: int, dv, out: torch.Tensor) -> torch.Tensor:
+    dev = _require_cuda(partials, out)
+    G, D = out.shape
+    dvh = _host_f32(dv)
+    with torch.cuda.device(dev):
+        _lib.call("kh_decode_combine", _vp(partials), G, n_parts, D, _vp(dvh), _vp(out),
+                  _stream(dev))
+    return out
+
+
+def decode_attention(q: torch.Tensor, k: PackedKV, v: PackedKV, dk, dv, centroids,
+                     sm_scale: Optional[float] = None, n_splits: Optional[int] = None,
+                     workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """softmax(score * sm_scale) . V_hat for one query per group.
+    q [G, D]; k / v hold G * S rows.  Returns float32 [G, D]."""
+    dev = _require_cuda(q, k.norms, v.norms)
+    G, D = q.shape
+    S = k.n_rows // max(G, 1)
+    if G * S != k.n_rows or v.n_rows != k.n_rows:
+        raise ValueError("K/V caches do not hold G * S rows")
+    if sm_scale is None:
+        sm_scale = 1.0 / math.sqrt(D)
+    if n_splits is None:
+        n_splits = default_splits(G, S, dev)
+    need = decode_workspace_bytes(G, n_splits, D)
+    if workspace is None or workspace.numel() * workspace.element_size() < need:
+        workspace = torch.empty(max(need // 4, 1), dtype=torch.float32, device=dev)
+    out = torch.empty((G, D), dtype=torch.float32, device=dev)
+    decode_partial(q, k, v, dk, dv, centroids, sm_scale, n_splits, workspace, n_splits, 0, S)
+    return decode_combine(workspace, n_splits, dv, out)
+
+
+def ultra_fused_full_fusion(x: torch.Tensor, d, centroids):
+    """Compatibility op with the reference kernel's outputs
+    (KudaHitamCUDA.cu:197-231): (idx uint8 [N, D], norms [N, 1],
+    k_mse float32 [N, D], r_norms [N, 1], signs int8 [N, D]).  Accepts
+    fp16 (like the reference) and also fp32 / bf16."""
+    p = compress(x, d, centroids, residual=True)
+    m = materialize(p, d, centroids)
+    return m["idx"], p.norms.view(-1, 1), m["kmse"], p.rnorms.view(-1, 1), m["signs"]

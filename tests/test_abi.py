@@ -1,0 +1,102 @@
+"""The C ABI: the library loads, exports exactly what include/kudahitam.h
+declares, and validates arguments without touching a GPU."""
+import ctypes
+import pathlib
+import re
+
+import pytest
+
+from kudahitam import _lib
+
+HEADER = pathlib.Path(__file__).resolve().parents[1] / "include" / "kudahitam.h"
+
+
+def declared() -> list[str]:
+    text = HEADER.read_text()
+    text = re.sub(r"/\*.*?\*/", "", text, flags=re.S)
+    return sorted(set(re.findall(r"\b(kh_[a-z0-9_]+)\s*\(", text)))
+
+
+def test_library_exports_every_declaration():
+    L = _lib.lib()
+    names = declared()
+    assert len(names) >= 14
+    for n in names:
+        assert hasattr(L, n), n
+        assert n in _lib.SIGNATURES, n
+    assert sorted(_lib.SIGNATURES) == names
+
+
+def test_status_strings_and_version():
+    L = _lib.lib()
+    assert L.kh_version() >= 100
+    assert L.kh_status_string(0) == b"ok"
+    assert b"aligned" in L.kh_status_string(_lib.KH_EALIGN)
+    assert L.kh_status_string(99) == b"unknown status"
+
+
+def _f(vals):
+    return (ctypes.c_float * len(vals))(*vals)
+
+
+D128 = _f([1.0, -1.0] * 64)
+C2 = _f([-0.07, 0.07])
+FAKE = ctypes.c_void_p(0x10000)  # never dereferenced: validation fails first
+
+
+@pytest.mark.parametrize("kw,status", [
+    (dict(head_dim=64), _lib.KH_EINVAL),
+    (dict(dtype=7), _lib.KH_EINVAL),
+    (dict(n_centroids=3), _lib.KH_EINVAL),
+    (dict(centroids=_f([0.07, -0.07])), _lib.KH_EINVAL),
+    (dict(d=_f([0.5] * 128)), _lib.KH_EINVAL),
+    (dict(residual=2), _lib.KH_EINVAL),
+    (dict(x=ctypes.c_void_p(0x10008)), _lib.KH_EALIGN),
+    (dict(row_stride=100), _lib.KH_EINVAL),
+    (dict(row_stride=132, dtype=_lib.KH_BF16), _lib.KH_EALIGN),
+    (dict(res=None), _lib.KH_EINVAL),
+    (dict(n_rows=-1), _lib.KH_EINVAL),
+    (dict(n_rows=1 << 31), _lib.KH_EINVAL),
+    (dict(n_rows=0), _lib.KH_OK),
+])
+def test_compress_validation(kw, status):
+    a = dict(x=FAKE, dtype=_lib.KH_F32, n_rows=10, head_dim=128, row_stride=128, d=D128,
+             centroids=C2, n_centroids=2, residual=1, code=FAKE, res=FAKE, norms=FAKE,
+             rnorms=FAKE)
+    a.update(kw)
+    st = _lib.lib().kh_compress(a["x"], a["dtype"], a["n_rows"], a["head_dim"], a["row_stride"],
+                                a["d"], a["centroids"], a["n_centroids"], a["residual"],
+                                a["code"], a["res"], a["norms"], a["rnorms"], None)
+    assert st == status
+
+
+def test_batched_validation():
+    L = _lib.lib()
+    assert L.kh_max_segments() == 64
+    assert L.kh_compress_batched(65, None, None, None, None, None, None, None, 0, 128, D128,
+                                 C2, 2, 1, None) == _lib.KH_EINVAL
+    assert L.kh_compress_batched(0, None, None, None, None, None, None, None, 0, 128, D128,
+                                 C2, 2, 1, None) == _lib.KH_OK
+
+
+def test_other_entry_points_validate():
+    L = _lib.lib()
+    assert L.kh_fwht_inplace(FAKE, 4, 100, None) == _lib.KH_EINVAL
+    assert L.kh_fwht_inplace(FAKE, 0, 128, None) == _lib.KH_OK
+    assert L.kh_materialize(FAKE, None, FAKE, 4, 96, D128, C2, 2, None, None, None,
+                            None) == _lib.KH_EINVAL
+    assert L.kh_materialize(FAKE, None, FAKE, 4, 128, D128, C2, 2, None, None, FAKE,
+                            None) == _lib.KH_EINVAL  # signs need res_bits
+    assert L.kh_score(FAKE, 2, 1, 128, FAKE, FAKE, FAKE, None, 16, D128, C2, 2, FAKE,
+                      None) == _lib.KH_EINVAL  # res_bits without r_norms
+    assert L.kh_decode_workspace_bytes(10, 4, 128) == 10 * 4 * 130 * 4
+    assert L.kh_decode_workspace_bytes(10, 0, 128) == -1
+    assert L.kh_decode_partial(FAKE, 2, 128, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE,
+                               100, 50, 10, D128, D128, C2, 2, 0.1, 2, FAKE, 2, 0,
+                               None) == _lib.KH_EINVAL  # seq_end < seq_begin
+    assert L.kh_decode_partial(FAKE, 2, 128, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE,
+                               100, 0, 100, D128, D128, _f([-0.1, -0.05, 0.05, 0.1]), 4, 0.1,
+                               2, FAKE, 2, 0, None) == _lib.KH_ENOTSUP
+    assert L.kh_decode_attn(FAKE, 2, 128, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 100,
+                            D128, D128, C2, 2, 0.1, 4, FAKE, 16, FAKE,
+                            None) == _lib.KH_EINVAL  # workspace too small

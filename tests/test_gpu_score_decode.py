@@ -1,0 +1,182 @@
+"""Scores and decode attention read from the packed cache, against the
+oracle (the reference's score function, KudaHitamQuant_full.py:373-377) and
+the reference-generated golden scores.  Tolerance: normwise per group
+max|est - ref| / max|ref| <= 1e-3 (asserted tighter where the arithmetic
+allows)."""
+import math
+
+import numpy as np
+import pytest
+import torch
+
+import khtest as K
+from kudahitam import KudahitamCompressorV2, fwht, load_cuda_ext, lloyd_max, ops, rademacher
+from oracle import oracle as O
+
+pytestmark = pytest.mark.gpu
+
+
+@pytest.mark.parametrize("case", ["d128_fp32_b1", "d128_fp32_b2", "d256_fp16_b1",
+                                  "d256_fp16_b2"])
+def test_scores_match_reference_golden(case):
+    g = K.golden(f"compress_{case}.npz")
+    B, H, S, D = g["x"].shape
+    bits = 1 if len(g["c"]) == 2 else 2
+    comp = KudahitamCompressorV2(D, bits, seed=7)
+    out = comp.compress(torch.from_numpy(g["x"]).cuda())
+    sc = comp.asymmetric_attention_scores(torch.from_numpy(g["q"]).cuda(), out)
+    assert sc.shape == g["scores"].shape and sc.dtype == torch.float32
+    got = sc.cpu().numpy().reshape(B * H, -1)
+    ref = g["scores"].reshape(B * H, -1)
+    for gi in range(B * H):
+        assert K.normwise(got[gi], ref[gi]) < 1e-4
+
+
+@pytest.mark.parametrize("D", [128, 256])
+@pytest.mark.parametrize("bits", [1, 2])
+@pytest.mark.parametrize("residual", [True, False])
+def test_scores_match_oracle(D, bits, residual):
+    if bits == 2 and not residual:
+        pytest.skip("1-bit mode uses the 2-level codebook")
+    G, S, nq = 6, 333, 3
+    d = rademacher(D, 3).numpy()
+    c = lloyd_max(bits, D).numpy()
+    x = K.synth((1, G, S, D), dtype=torch.bfloat16, seed=9)
+    q = torch.randn(G, nq, D, generator=torch.Generator().manual_seed(1))
+    p = ops.compress(x.cuda(), d, c, residual=residual)
+    got = ops.score(q.cuda(), p, d, c, seq_len=S).cpu().numpy()
+    ref = O.compress_v8(x, d, c)
+    want = O.score(q.numpy(), ref["kmse"].reshape(G, S, D),
+                   ref["signs"].reshape(G, S, D) if residual else None,
+                   ref["rnorms"].reshape(G, S) if residual else None, d)
+    for gi in range(G):
+        assert K.normwise(got[gi], want[gi]) < 1e-4
+
+
+def test_gqa_scores_share_kv_heads():
+    D, S = 128, 200
+    comp = KudahitamCompressorV2(D, 1, seed=0)
+    k = torch.randn(2, 2, S, D, device="cuda", dtype=torch.float16)
+    ck = comp.compress(k)
+    q = torch.randn(2, 8, 1, D, device="cuda")   # 4 query heads per KV head
+    sc = comp.asymmetric_attention_scores(q, ck)
+    assert sc.shape == (2, 8, 1, S)
+    for h in range(8):
+        ck1 = comp.compress(k[:, h // 4:h // 4 + 1].contiguous())
+        one = comp.asymmetric_attention_scores(q[:, h:h + 1], ck1)
+        assert torch.allclose(sc[:, h:h + 1], one, rtol=0, atol=1e-5)
+
+
+def test_fwht_matches_oracle_and_reference_forward():
+    for D in (2, 8, 64, 128, 256, 1024):
+        x = torch.randn(37, D)
+        got = fwht(x.cuda()).cpu().numpy()
+        assert np.allclose(got, O.fwht_forward(x.numpy()), rtol=1e-5, atol=1e-6)
+    ext = load_cuda_ext()
+    y = torch.randn(5, 128, device="cuda")
+    y0 = y.clone()
+    ext.forward(y)
+    assert torch.allclose(y, torch.tensor(O.fwht_forward(y0.cpu().numpy()), device="cuda"),
+                          atol=1e-6)
+
+
+@pytest.mark.parametrize("D", [128, 256])
+@pytest.mark.parametrize("bits", [1, 2])
+def test_materialize_and_compat_op(D, bits):
+    d = rademacher(D, 8).numpy()
+    c = lloyd_max(bits, D).numpy()
+    x = K.synth((1, 2, 50, D), dtype=torch.float16, seed=4)
+    idx, norms, kmse, rn, signs = load_cuda_ext().ultra_fused_full_fusion(
+        x.cuda().view(-1, D), torch.tensor(d).cuda(), torch.tensor(c).cuda())
+    n = 100
+    assert idx.shape == (n, D) and norms.shape == (n, 1) and kmse.shape == (n, D)
+    assert rn.shape == (n, 1) and signs.shape == (n, D) and signs.dtype == torch.int8
+    ref = O.compress_v8(x, d, c)
+    y = K.projected(x.float().numpy().reshape(n, D), d)
+    m = K.idx_mask(y, c)
+    assert np.array_equal(idx.cpu().numpy()[m], ref["idx"][m])
+    rm = K.res_mask(y, ref["idx"].astype(np.int64), c)
+    assert np.array_equal(signs.cpu().numpy()[rm], ref["signs"][rm])
+    assert K.normwise(kmse.cpu().numpy(), ref["kmse"]) < 1e-5
+    assert K.rel_err(rn.cpu().numpy()[:, 0], ref["rnorms"]) < 1e-4
+
+
+def _caches(G, S, D, seed):
+    dk = rademacher(D, 10).numpy()
+    dv = rademacher(D, 11).numpy()
+    c = lloyd_max(1, D).numpy()
+    k = K.synth((1, G, S, D), dtype=torch.bfloat16, seed=seed)
+    v = K.synth((1, G, S, D), dtype=torch.bfloat16, seed=seed + 1)
+    return dk, dv, c, k, v
+
+
+@pytest.mark.parametrize("D", [128, 256])
+@pytest.mark.parametrize("S", [1, 7, 300, 1000])
+def test_decode_attention_matches_oracle(D, S):
+    G = 5
+    dk, dv, c, k, v = _caches(G, S, D, seed=S)
+    q = torch.randn(G, D, generator=torch.Generator().manual_seed(S)).to(torch.bfloat16)
+    pk = ops.compress(k.cuda(), dk, c)
+    pv = ops.compress(v.cuda(), dv, c)
+    sm = 1.0 / math.sqrt(D)
+    rk = O.compress_v8(k, dk, c)
+    rv = O.compress_v8(v, dv, c)
+    want = O.decode(q.float().numpy(), rk["kmse"].reshape(G, S, D), rk["signs"].reshape(G, S, D),
+                    rk["rnorms"].reshape(G, S), rv["kmse"].reshape(G, S, D),
+                    rv["signs"].reshape(G, S, D), rv["rnorms"].reshape(G, S), dk, dv, sm)
+    for n_splits in (1, 3, 16):
+        got = ops.decode_attention(q.cuda(), pk, pv, dk, dv, c, sm, n_splits=n_splits)
+        got = got.cpu().numpy()
+        for gi in range(G):
+            assert K.normwise(got[gi], want[gi]) < 1e-3, (n_splits, gi)
+
+
+def test_decode_split_invariance_and_empty_splits():
+    D, G, S = 128, 3, 5
+    dk, dv, c, k, v = _caches(G, S, D, seed=1)
+    q = torch.randn(G, D, device="cuda")
+    pk = ops.compress(k.cuda(), dk, c)
+    pv = ops.compress(v.cuda(), dv, c)
+    base = ops.decode_attention(q, pk, pv, dk, dv, c, n_splits=1)
+    for n in (2, 5, 8, 64):  # 64 splits over 5 rows: most splits are empty
+        got = ops.decode_attention(q, pk, pv, dk, dv, c, n_splits=n)
+        assert torch.allclose(got, base, rtol=1e-5, atol=1e-6), n
+
+
+def test_decode_seq_sharded_emulated_on_one_gpu():
+    """The multi-GPU combine, with the ranks' slots filled by one process:
+    partial records of every S-shard in their own slots, merged once."""
+    D, G, S, world, n_splits = 128, 4, 1000, 4, 2
+    dk, dv, c, k, v = _caches(G, S, D, seed=3)
+    q = torch.randn(G, D, device="cuda")
+    kc, vc = k.cuda().view(G, S, D), v.cuda().view(G, S, D)
+    parts = world * n_splits
+    buf = torch.zeros(G, parts, D + 2, device="cuda")
+    from kudahitam.dist import shard_range
+    for r in range(world):
+        a, b = shard_range(S, world, r)
+        pk = ops.compress(kc[:, a:b].contiguous(), dk, c)
+        pv = ops.compress(vc[:, a:b].contiguous(), dv, c)
+        ops.decode_partial(q, pk, pv, dk, dv, c, 1 / math.sqrt(D), n_splits, buf,
+                           part_stride=parts, part_offset=r * n_splits, seq_len=b - a)
+    got = ops.decode_combine(buf, parts, dv, torch.empty(G, D, device="cuda"))
+    pk = ops.compress(kc, dk, c)
+    pv = ops.compress(vc, dv, c)
+    want = ops.decode_attention(q, pk, pv, dk, dv, c, 1 / math.sqrt(D), n_splits=8)
+    assert torch.allclose(got, want, rtol=1e-4, atol=1e-5)
+
+
+def test_compressor_decode_api():
+    D = 128
+    ck = KudahitamCompressorV2(D, 1, seed=10)
+    cv = KudahitamCompressorV2(D, 1, seed=11)
+    k = torch.randn(2, 4, 500, D, device="cuda", dtype=torch.bfloat16)
+    v = torch.randn(2, 4, 500, D, device="cuda", dtype=torch.bfloat16)
+    q = torch.randn(2, 4, D, device="cuda", dtype=torch.bfloat16)
+    out = ck.decode_attention(q, ck.compress(k), cv.compress(v), v_compressor=cv)
+    assert out.shape == (2, 4, D)
+    # close to exact attention on the uncompressed cache
+    att = torch.softmax((q.float().unsqueeze(2) @ k.float().transpose(-1, -2)) / math.sqrt(D), -1)
+    exact = (att @ v.float()).squeeze(2)
+    cos = torch.nn.functional.cosine_similarity(out.flatten(), exact.flatten(), dim=0)
+    assert cos > 0.9

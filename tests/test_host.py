@@ -1,0 +1,65 @@
+"""Host-side logic of the Python layer (no GPU)."""
+import numpy as np
+import pytest
+import torch
+
+from kudahitam import KudahitamCompressorV2, lloyd_max, ops
+from kudahitam.dist import shard_range
+
+
+def test_shard_range_partitions():
+    for n in (0, 1, 7, 1024, 1023):
+        for world in (1, 2, 3, 8):
+            spans = [shard_range(n, world, r) for r in range(world)]
+            assert spans[0][0] == 0 and spans[-1][1] == n
+            for (a, b), (c, _) in zip(spans, spans[1:]):
+                assert b == c
+            sizes = [b - a for a, b in spans]
+            assert max(sizes) - min(sizes) <= 1
+    with pytest.raises(ValueError):
+        shard_range(4, 2, 2)
+
+
+def test_compressor_signature_and_rejections():
+    c = KudahitamCompressorV2(128, 1, seed=3)  # reference defaults
+    assert c.d.shape == (128,) and set(c.d.unique().tolist()) <= {-1.0, 1.0}
+    assert torch.equal(c.centroids, lloyd_max(1, 128))
+    KudahitamCompressorV2(256, 2, 0, use_fractional=True, use_dynamic_codebook=True,
+                          use_spectral=True, use_spaced=True, use_ultra=True)
+    with pytest.raises(NotImplementedError):
+        KudahitamCompressorV2(128, 1, 0, protected_dim_count=8)
+    with pytest.raises(NotImplementedError):
+        KudahitamCompressorV2(128, 1, 0, is_domain_layer=True)
+    KudahitamCompressorV2(128, 1, 0, is_domain_layer=True, use_outlier=False)
+    with pytest.raises(NotImplementedError):
+        KudahitamCompressorV2(128, 1, 0, use_vwh=True)
+    with pytest.raises(ValueError):
+        KudahitamCompressorV2(96, 1, 0)
+    with pytest.raises(ValueError):
+        KudahitamCompressorV2(128, 2, 0, residual=False)
+
+
+def test_no_cpu_path():
+    c = KudahitamCompressorV2(128, 1, seed=0)
+    with pytest.raises(ValueError, match="CUDA"):
+        c.compress(torch.randn(1, 2, 8, 128))
+    with pytest.raises(ValueError, match="CUDA"):
+        ops.fwht(torch.randn(4, 128))
+
+
+def test_packed_layout_shapes():
+    p = ops.empty_packed((2, 3, 5, 128), bits=1, residual=True, device="cpu")
+    assert p.code.shape == (30, 4) and p.res.shape == (30, 4)
+    assert p.nbytes() == 30 * (16 + 16 + 4 + 4)
+    p2 = ops.empty_packed((7, 256), bits=2, residual=False, device="cpu")
+    assert p2.code.shape == (7, 16) and p2.res is None and p2.rnorms is None
+    sub = p.rows(5, 10)
+    assert sub.n_rows == 5 and sub.code.data_ptr() == p.code[5].data_ptr()
+
+
+def test_lloyd_max_other_dims_sorted_symmetric():
+    for D in (16, 64, 512):
+        for bits in (1, 2, 3):
+            c = lloyd_max(bits, D).numpy()
+            assert np.all(np.diff(c) > 0)
+            assert np.allclose(c, -c[::-1], atol=1e-9)
