@@ -72,58 +72,58 @@ def synth_kv(seed: int, device) -> tuple[torch.Tensor, torch.Tensor]:
 
 
 class ClockSampler:
-    """nvidia-smi clock / throttle sampling during the timed region."""
+    """SM clock and clock-event (throttle) reasons sampled through NVML every
+    50 ms during the timed region (read-only queries)."""
 
-    Q = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
-         "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
-         "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
+               "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4}
 
     def __init__(self, index: int):
         self.index = index
-        self.proc = None
-        self.lines: list[str] = []
+        self.sm: list[float] = []
+        self.max_mhz = None
+        self.mask = 0
+        self.err = None
+        self._stop = threading.Event()
 
     def __enter__(self):
         try:
-            self.proc = subprocess.Popen(
-                ["nvidia-smi", f"--id={self.index}", f"--query-gpu={self.Q}",
-                 "--format=csv,noheader,nounits", "-lms", "100"],
-                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
-            self.t = threading.Thread(target=self._read, daemon=True)
-            self.t.start()
-        except (OSError, FileNotFoundError):
-            self.proc = None
+            import pynvml as N
+            N.nvmlInit()
+            self._N = N
+            self._h = N.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = float(N.nvmlDeviceGetMaxClockInfo(self._h, N.NVML_CLOCK_SM))
+            self._t = threading.Thread(target=self._run, daemon=True)
+            self._t.start()
+        except Exception as e:  # NVML missing: report, do not fail the bench
+            self.err = repr(e)
+            self._N = None
         return self
 
-    def _read(self):
-        for line in self.proc.stdout:
-            self.lines.append(line.strip())
+    def _run(self):
+        N = self._N
+        while not self._stop.is_set():
+            try:
+                self.sm.append(float(N.nvmlDeviceGetClockInfo(self._h, N.NVML_CLOCK_SM)))
+                self.mask |= int(N.nvmlDeviceGetCurrentClocksEventReasons(self._h))
+            except Exception as e:
+                self.err = repr(e)
+                return
+            self._stop.wait(0.05)
 
     def __exit__(self, *exc):
-        if self.proc is not None:
-            self.proc.terminate()
-            try:
-                self.proc.wait(timeout=5)
-            except subprocess.TimeoutExpired:
-                self.proc.kill()
+        self._stop.set()
+        if self._N is not None:
+            self._t.join(timeout=2)
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], None, set()
-        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
-        for ln in self.lines:
-            f = [x.strip() for x in ln.split(",")]
-            if len(f) < 9:
-                continue
-            try:
-                sm.append(float(f[1]))
-                mx = float(f[2])
-            except ValueError:
-                continue
-            for nm, v in zip(names, f[5:9]):
-                if v.lower().startswith("active"):
-                    reasons.add(nm)
-        return {"sm_mhz": statistics.median(sm) if sm else None, "sm_max_mhz": mx,
-                "reasons": sorted(reasons), "samples": len(sm)}
+        out = {"sm_mhz": statistics.median(self.sm) if self.sm else None,
+               "sm_max_mhz": self.max_mhz,
+               "reasons": sorted(k for k, b in self.REASONS.items() if self.mask & b),
+               "samples": len(self.sm)}
+        if self.err:
+            out["error"] = self.err
+        return out
 
 
 def dist_setup(args):
@@ -229,6 +229,11 @@ def run_engine(args, world, rank, local):
     torch.cuda.set_device(dev)
     peak, peak_kind = peaks()
 
+    if args.only == "decode":
+        dec = decode_bench(dev, args)
+        if rank == 0:
+            print(json.dumps({"decode": dec}), flush=True)
+        return
     k, v = synth_kv(2 + 1000 * rank, dev)
     d = rademacher(D, 1)
     c = lloyd_max(1, D)
@@ -313,7 +318,7 @@ def run_engine(args, world, rank, local):
            "ms_per_step": e2e_ms / e2e_steps}
     del hk, hv, gk, gv
 
-    dec = decode_bench(dev, args)
+    dec = decode_bench(dev, args) if args.only == "all" else None
 
     line = {"metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
@@ -373,7 +378,15 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["engine", "reference"], default="engine")
     ap.add_argument("--no-cpu-baseline", action="store_true")
+    ap.add_argument("--only", choices=["all", "compress", "decode"], default="all",
+                    help="run one part (small cases for profiler captures)")
+    ap.add_argument("--seq", type=int, default=None,
+                    help="override S of the compression workload (profiling only)")
     args = ap.parse_args()
+    if args.seq:
+        global S, ROWS_PER_TENSOR
+        S = args.seq
+        ROWS_PER_TENSOR = B * H * S
     if args.impl == "reference":
         world = int(os.environ.get("WORLD_SIZE", "1"))
         rank = int(os.environ.get("RANK", "0"))

@@ -59,7 +59,9 @@ def _rows(x: torch.Tensor) -> tuple[torch.Tensor, int]:
     ok = (x2.stride(-1) == 1 and x2.data_ptr() % 16 == 0
           and (x2.shape[0] <= 1 or (x2.stride(0) * elt) % 16 == 0))
     if not ok:
-        x2 = x2.contiguous()
+        # a fresh allocation is 256-byte aligned (contiguous() would return a
+        # misaligned tensor unchanged)
+        x2 = torch.empty(x2.shape, dtype=x2.dtype, device=x2.device).copy_(x2)
     stride = x2.stride(0) if x2.shape[0] > 1 else D
     return x2, stride
 

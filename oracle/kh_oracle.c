@@ -55,6 +55,12 @@ static void stage(float* r, int D, int h) {
 }
 
 void khx_fwht_v8(float* r, int D) {
+  /* the reference kernels need D >= 8 (D/8 lanes per row); smaller rows get
+   * the natural stage order */
+  if (D < 8) {
+    for (int h = 1; h < D; h <<= 1) stage(r, D, h);
+    return;
+  }
   stage(r, D, 1);
   stage(r, D, 2);
   for (int h = 8; h < D; h <<= 1) stage(r, D, h);

@@ -110,22 +110,35 @@ def test_edge_rows():
         check_against_oracle(x, p, d, c)
 
 
-def test_strided_and_unaligned_inputs():
+def _dc(seed=5, D=128):
+    return rademacher(D, seed).numpy(), lloyd_max(1, D).numpy()
+
+
+def test_row_pitch_wider_than_head_dim():
     D = 128
-    d = rademacher(D, 5).numpy()
-    c = lloyd_max(1, D).numpy()
+    d, c = _dc()
     base = torch.randn(64, D + 8, dtype=torch.float16, device="cuda")
-    x = base[:, :D]                         # row stride D+8 elements (272 B)
+    x = base[:, :D]                         # row pitch D+8 elements (272 B), read in place
     p = ops.compress(x, d, c)
     check_against_oracle(x.cpu(), p, d, c)
+
+
+def test_unaligned_base_is_copied():
+    D = 128
+    d, c = _dc()
     flat = torch.randn(64 * D + 1, dtype=torch.bfloat16, device="cuda")
-    xu = flat[1:].view(64, D)               # 2-byte offset: copied internally
-    p2 = ops.compress(xu, d, c)
-    check_against_oracle(xu.cpu(), p2, d, c)
+    xu = flat[1:].view(64, D)               # 2-byte offset
+    p = ops.compress(xu, d, c)
+    check_against_oracle(xu.cpu(), p, d, c)
+
+
+def test_non_uniform_rows_are_copied():
+    D = 128
+    d, c = _dc()
     big = torch.randn(2, 4, 40, D, device="cuda")
-    xs = big[:, :, 5:30]                    # non-uniform row pitch
-    p3 = ops.compress(xs, d, c)
-    check_against_oracle(xs.cpu(), p3, d, c)
+    xs = big[:, :, 5:30]
+    p = ops.compress(xs, d, c)
+    check_against_oracle(xs.cpu(), p, d, c)
 
 
 def test_batched_equals_single():
