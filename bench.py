@@ -273,7 +273,9 @@ def run_engine(args, world, rank, local):
             "traffic": (NCU_TRAFFIC_BYTES_PER_ROW * rows_launch
                         if NCU_TRAFFIC_BYTES_PER_ROW else None),
             "algorithmic_bytes": rows_launch * ALG_BYTES_PER_ROW,
-            "kernel": "compress_simt_kernel<__half,256,Sym2,RES>"}
+            "kernel": ("compress_simt_kernel<__half,256,Sym2,RES>"
+                       if os.environ.get("KUDAHITAM_COMPRESS_PATH") == "simt"
+                       else "compress_tc_kernel<__half,256,Sym2,RES>")}
 
     # e2e through the public API with host buffers
     comp = KudahitamCompressorV2(D, 1, seed=1)

@@ -17,6 +17,7 @@
 // after the top butterfly stage).  Each warp runs its own STAGES-deep TMA
 // ring, so loads of the next tiles overlap the arithmetic of this one.
 #include <algorithm>
+#include <cstdlib>
 #include <cstring>
 #include <mutex>
 #include <type_traits>
@@ -336,9 +337,17 @@ kh_status dispatch_t(const CompressRequest& req, cudaStream_t s) {
 
 }  // namespace
 
-kh_status launch_compress(const CompressRequest& req, cudaStream_t stream) {
+kh_status launch_compress_simt(const CompressRequest& req, cudaStream_t stream) {
   if (req.n_seg <= 2) return dispatch_t<2>(req, stream);
   return dispatch_t<kMaxSegments>(req, stream);
+}
+
+kh_status launch_compress(const CompressRequest& req, cudaStream_t stream) {
+  const bool sixteen = req.dtype == KH_F16 || req.dtype == KH_BF16;
+  const char* env = getenv("KUDAHITAM_COMPRESS_PATH");
+  const bool force_simt = env && strcmp(env, "simt") == 0;
+  if (sixteen && !force_simt) return launch_compress_tc(req, stream);
+  return launch_compress_simt(req, stream);
 }
 
 }  // namespace kh

@@ -49,7 +49,12 @@ struct CompressRequest {
 };
 
 // Launch the fused compression kernel.  Arguments are already validated.
+// Picks the datapath: the tensor-core kernel for fp16 / bf16 rows, the SIMT
+// kernel for fp32.  Environment KUDAHITAM_COMPRESS_PATH=simt sends 16-bit
+// inputs to the SIMT kernel too (used to test and compare both datapaths).
 kh_status launch_compress(const CompressRequest& req, cudaStream_t stream);
+kh_status launch_compress_simt(const CompressRequest& req, cudaStream_t stream);
+kh_status launch_compress_tc(const CompressRequest& req, cudaStream_t stream);
 
 // Materialise reference-layout tensors from a packed cache.
 kh_status launch_materialize(const uint32_t* code, const uint32_t* res,

@@ -45,10 +45,17 @@ def check_against_oracle(x_cpu: torch.Tensor, p: ops.PackedKV, d, c, residual=Tr
     return ref
 
 
+@pytest.fixture(params=["simt", "tensor"])
+def path(request, monkeypatch):
+    """Datapath of the 16-bit compressor (fp32 always takes the SIMT one)."""
+    monkeypatch.setenv("KUDAHITAM_COMPRESS_PATH", request.param)
+    return request.param
+
+
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("D", [128, 256])
 @pytest.mark.parametrize("bits", [1, 2])
-def test_compress_matches_oracle(dtype, D, bits):
+def test_compress_matches_oracle(dtype, D, bits, path):
     d = rademacher(D, 1).numpy()
     c = lloyd_max(bits, D).numpy()
     x = K.synth((2, 3, 171, D), dtype=dtype, seed=D + bits)
@@ -59,7 +66,7 @@ def test_compress_matches_oracle(dtype, D, bits):
 
 @pytest.mark.parametrize("dtype", DTYPES)
 @pytest.mark.parametrize("D", [128, 256])
-def test_one_bit_mode(dtype, D):
+def test_one_bit_mode(dtype, D, path):
     d = rademacher(D, 2).numpy()
     c = lloyd_max(1, D).numpy()
     x = K.synth((1, 2, 77, D), dtype=dtype, seed=3)
@@ -72,7 +79,7 @@ def test_one_bit_mode(dtype, D):
 
 @pytest.mark.parametrize("n", [1, 2, 3, 15, 16, 17, 31, 32, 33, 63, 65, 129, 1000])
 @pytest.mark.parametrize("D", [128, 256])
-def test_tails(n, D):
+def test_tails(n, D, path):
     d = rademacher(D, 4).numpy()
     c = lloyd_max(1, D).numpy()
     x = torch.randn(n, D, generator=torch.Generator().manual_seed(n)).to(torch.bfloat16)
@@ -87,7 +94,7 @@ def test_tails(n, D):
     check_against_oracle(x, p, d, c)
 
 
-def test_edge_rows():
+def test_edge_rows(path):
     D = 128
     d = rademacher(D, 0).numpy()
     for bits in (1, 2):
@@ -114,7 +121,7 @@ def _dc(seed=5, D=128):
     return rademacher(D, seed).numpy(), lloyd_max(1, D).numpy()
 
 
-def test_row_pitch_wider_than_head_dim():
+def test_row_pitch_wider_than_head_dim(path):
     D = 128
     d, c = _dc()
     base = torch.randn(64, D + 8, dtype=torch.float16, device="cuda")
@@ -141,7 +148,7 @@ def test_non_uniform_rows_are_copied():
     check_against_oracle(xs.cpu(), p, d, c)
 
 
-def test_batched_equals_single():
+def test_batched_equals_single(path):
     D = 128
     d = rademacher(D, 6).numpy()
     c = lloyd_max(1, D).numpy()
@@ -190,7 +197,7 @@ def test_matches_reference_golden(case):
     assert out["rank"] == 4 and out["shape"] == (B, H, S, D) and out["p_indices"] is None
 
 
-def test_full_size_fp16_d256_properties():
+def test_full_size_fp16_d256_properties(path):
     """40000-token fp16 D=256 K tensor (the 2-bit-mode workload): sampled rows
     against the oracle, and on every row the residual identity
     sign(H(d (.) (x - k_mse))) == residual bits, r_norm == ||x - k_mse||."""
