@@ -182,6 +182,32 @@ int kh_decode_attn(const float* q, int64_t n_groups, int head_dim,
                    void* workspace, int64_t workspace_bytes, float* out,
                    void* stream);
 
+/*
+ * kh_decode_attn_static -- kh_decode_attn without a workspace argument, for
+ * callers that cannot allocate device memory when they call: for example a
+ * server that has reserved all device memory in its own pool and forbids
+ * further allocations, or a C/FFI caller that only holds the buffers it was
+ * given.  No counterpart in the reference (it has no decode step at all).
+ * The split-K scratch comes from one array of KH_DECODE_STATIC_SCRATCH_BYTES
+ * compiled into the library, held on every GPU that loads it until exit.
+ * Requests needing more than that return KH_EINVAL (see
+ * kh_decode_workspace_bytes).  Calls on the same device share the array:
+ * calls whose GPU work overlaps race, so order them.  The first call on a
+ * device resolves the array's address (cudaGetSymbolAddress) and should come
+ * before any stream capture.  Allocates nothing (no cudaMalloc / cudaFree).
+ */
+#define KH_DECODE_STATIC_SCRATCH_BYTES (4 * 1024 * 1024)
+
+int kh_decode_attn_static(const float* q, int64_t n_groups, int head_dim,
+                          const uint32_t* k_code, const uint32_t* k_res,
+                          const float* k_norms, const float* k_rnorms,
+                          const uint32_t* v_code, const uint32_t* v_res,
+                          const float* v_norms, const float* v_rnorms,
+                          int64_t seq_len, const float* d_k_host,
+                          const float* d_v_host, const float* centroids_host,
+                          int n_centroids, float sm_scale, int n_splits,
+                          float* out, void* stream);
+
 #ifdef __cplusplus
 }
 #endif

@@ -44,7 +44,13 @@ SIGNATURES = {
     "kh_decode_attn": (_c_i, [_vp, _c_i64, _c_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                               _c_i64, _vp, _vp, _vp, _c_i, _c_f, _c_i, _vp, _c_i64, _vp,
                               _vp]),
+    "kh_decode_attn_static": (_c_i, [_vp, _c_i64, _c_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
+                                     _vp, _c_i64, _vp, _vp, _vp, _c_i, _c_f, _c_i, _vp,
+                                     _vp]),
 }
+
+# Size of the library's fixed scratch array used by kh_decode_attn_static.
+DECODE_STATIC_SCRATCH_BYTES = 4 * 1024 * 1024
 
 
 class NativeLibraryError(RuntimeError):
