@@ -116,18 +116,52 @@ struct alignas(64) TcParams {
 template <int D>
 struct TcCfg {
   static constexpr int kM = 128;                 // rows per tile
-  static constexpr int kKB = D / 64;             // 128-byte K-blocks per row
-  static constexpr int kBoxBytes = kM * 128;     // one K-block of a tile
-  static constexpr int kStageBytes = kKB * kBoxBytes;
-  static constexpr int kStages = (D == 128) ? 5 : 2;
-  static constexpr int kNB = D / 128;            // 128x128 B matrices
+  static constexpr int kNB = D / 128;            // 128-column chunks per tile
+  static constexpr int kBoxBytes = kM * 128;     // one 64-column K-block of a chunk
+  static constexpr int kChunkBytes = 2 * kBoxBytes;  // 128 rows x 128 columns, 32 KB
+  static constexpr int kStages = (D == 128) ? 5 : 4;  // chunk ring depth
   static constexpr int kBMatBytes = 2 * kBoxBytes;
   static constexpr int kAccCols = D;             // tensor-memory columns per tile
   static constexpr uint32_t kTmemCols = 2 * kAccCols;
   static constexpr int kThreads = 320;
-  static constexpr int kBarOff = kStages * kStageBytes + kNB * kBMatBytes;
-  static constexpr int kSmem = 1024 + kBarOff + (2 * kStages + 4) * 8 + 16;
+  static constexpr int kBarOff = kStages * kChunkBytes + kNB * kBMatBytes;
+  // barriers, the tensor-memory slot, then (D=256) the partner exchange
+  static constexpr int kXchOff = kBarOff + (2 * kStages + 4) * 8 + 16;
+  static constexpr int kSmem = 1024 + kXchOff + (D == 256 ? 4 * 128 * 4 : 0);
+  static_assert(kSmem <= 232448, "exceeds the 227 KB of shared memory a CTA can use");
 };
+
+__device__ __forceinline__ void named_bar_sync(int id, int n) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
+}
+
+// Store this row's packed words w[0..n) at dst (16-byte vectors when possible).
+template <int N>
+__device__ __forceinline__ void store_words(uint32_t* dst, const uint32_t* w) {
+  if constexpr (N % 4 == 0) {
+#pragma unroll
+    for (int k = 0; k < N / 4; ++k)
+      reinterpret_cast<uint4*>(dst)[k] = make_uint4(w[4 * k], w[4 * k + 1], w[4 * k + 2], w[4 * k + 3]);
+  } else {
+#pragma unroll
+    for (int k = 0; k < N / 2; ++k)
+      reinterpret_cast<uint2*>(dst)[k] = make_uint2(w[2 * k], w[2 * k + 1]);
+  }
+}
+
+// Quantise NG groups of 32 values: the interleaved fast path for the
+// symmetric codebook, the per-group generic code otherwise.
+template <int CK, bool RES, int NG, class P>
+__device__ __forceinline__ void quant_groups(const float (&u)[NG][32], float rs, const P& prm,
+                                             uint32_t* code, uint32_t* resw, float2& acc) {
+  if constexpr (CK == kCbSym2) {
+    quant_sym2_groups<NG, RES>(u, rs, prm.cb.c[1], code, resw, acc);
+  } else {
+    using Q = Quant<CK, RES>;
+#pragma unroll
+    for (int g = 0; g < NG; ++g) Q::run(u[g], rs, prm, &code[g * Q::kCodeWords], resw[g], acc);
+  }
+}
 
 template <typename T, int D, int CK, bool RES, int MAXSEG>
 __global__ void __launch_bounds__(320, 1)
@@ -137,23 +171,25 @@ __global__ void __launch_bounds__(320, 1)
   constexpr bool kBF16 = std::is_same<T, __nv_bfloat16>::value;
   constexpr uint32_t kIdesc = make_idesc(kBF16, 128, 128);
   constexpr uint16_t kOne = kBF16 ? 0x3F80 : 0x3C00;
+  constexpr int kCW = Q::kCodeWords;  // code words per 32 elements
 
   extern __shared__ uint8_t smem_raw[];
   const uint32_t raw = smem_u32(smem_raw);
   const uint32_t base = (raw + 1023u) & ~1023u;
   uint8_t* g = smem_raw + (base - raw);
   uint8_t* stages = g;
-  uint8_t* bmat = g + C::kStages * C::kStageBytes;
+  uint8_t* bmat = g + C::kStages * C::kChunkBytes;
   uint64_t* full = reinterpret_cast<uint64_t*>(g + C::kBarOff);
   uint64_t* empty = full + C::kStages;
   uint64_t* tfull = empty + C::kStages;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
+  float* xch = reinterpret_cast<float*>(g + C::kXchOff);  // D=256: [2 WG][2][128]
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
 
-  // ---- B = diag(d) H_128 per 128-block, K-major, 128B-swizzled ----------
+  // ---- B = diag(d) H_128 per 128-column chunk, K-major, 128B-swizzled -----
   for (int i = threadIdx.x; i < C::kNB * 2 * 128 * 8; i += C::kThreads) {
     const int mat = i / 2048, rem = i % 2048;
     const int kb = rem / 1024, n = (rem / 8) % 128, c = rem % 8;
@@ -180,7 +216,7 @@ __global__ void __launch_bounds__(320, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], 4);
+      mbar_init(&tempty[b], D == 128 ? 4 : 8);
     }
     fence_mbar_init();
   }
@@ -205,137 +241,158 @@ __global__ void __launch_bounds__(320, 1)
     // ------------------------------------------------------ TMA producer
     if (lane == 0) {
       const uint64_t policy = l2_policy_evict_first();
-      int i = 0;
-      for (int64_t t = blockIdx.x; t < total; t += gridDim.x, ++i) {
-        const int s = i % C::kStages;
-        const uint32_t ph = (uint32_t)((i / C::kStages) & 1);
-        if (!mbar_wait(&empty[s], ph ^ 1u, P.err)) break;
+      int c = 0;  // chunk counter
+      bool ok = true;
+      for (int64_t t = blockIdx.x; t < total && ok; t += gridDim.x) {
         const int sg = seg_of(t);
         const int32_t row0 = (int32_t)((t - P.tile_begin[sg]) * C::kM);
-        mbar_arrive_expect_tx(&full[s], C::kStageBytes);
-#pragma unroll
-        for (int kb = 0; kb < C::kKB; ++kb)
-          tma_load_2d(stages + s * C::kStageBytes + kb * C::kBoxBytes, &P.tmap[sg],
-                      kb * 64, row0, &full[s], policy);
+#pragma unroll 1
+        for (int h = 0; h < C::kNB; ++h, ++c) {
+          const int s = c % C::kStages;
+          const uint32_t ph = (uint32_t)((c / C::kStages) & 1);
+          if (!mbar_wait(&empty[s], ph ^ 1u, P.err)) { ok = false; break; }
+          mbar_arrive_expect_tx(&full[s], C::kChunkBytes);
+          uint8_t* dst = stages + s * C::kChunkBytes;
+          tma_load_2d(dst, &P.tmap[sg], h * 128, row0, &full[s], policy);
+          tma_load_2d(dst + C::kBoxBytes, &P.tmap[sg], h * 128 + 64, row0, &full[s], policy);
+        }
       }
     }
   } else if (warp == 1) {
     // ------------------------------------------------------ MMA issuer
     if (lane == 0) {
-      int i = 0;
-      for (int64_t t = blockIdx.x; t < total; t += gridDim.x, ++i) {
-        const int s = i % C::kStages;
-        const uint32_t ph = (uint32_t)((i / C::kStages) & 1);
+      int i = 0, c = 0;
+      bool ok = true;
+      const uint32_t b0 = smem_u32(bmat);
+      for (int64_t t = blockIdx.x; t < total && ok; t += gridDim.x, ++i) {
         const int b = i & 1;
         const uint32_t jb = (uint32_t)((i >> 1) & 1);
-        if (!mbar_wait(&full[s], ph, P.err)) break;
         if (!mbar_wait(&tempty[b], jb ^ 1u, P.err)) break;
         tc_fence_after();
-        const uint32_t a0 = smem_u32(stages + s * C::kStageBytes);
-        const uint32_t b0 = smem_u32(bmat);
-#pragma unroll
-        for (int half = 0; half < C::kNB; ++half) {
-          const uint32_t dt = tmem + b * C::kAccCols + half * 128;
+#pragma unroll 1
+        for (int h = 0; h < C::kNB; ++h, ++c) {
+          const int s = c % C::kStages;
+          const uint32_t ph = (uint32_t)((c / C::kStages) & 1);
+          if (!mbar_wait(&full[s], ph, P.err)) { ok = false; break; }
+          tc_fence_after();
+          const uint32_t a0 = smem_u32(stages + s * C::kChunkBytes);
+          const uint32_t dt = tmem + b * C::kAccCols + h * 128;
 #pragma unroll
           for (int kb = 0; kb < 2; ++kb) {
-            const uint64_t ad = sw128_desc(a0 + (half * 2 + kb) * C::kBoxBytes);
-            const uint64_t bd = sw128_desc(b0 + half * C::kBMatBytes + kb * C::kBoxBytes);
+            const uint64_t ad = sw128_desc(a0 + kb * C::kBoxBytes);
+            const uint64_t bd = sw128_desc(b0 + h * C::kBMatBytes + kb * C::kBoxBytes);
 #pragma unroll
             for (int kk = 0; kk < 4; ++kk)  // K = 16 per MMA: 32 B along the row
               umma_f16(dt, ad + 2 * kk, bd + 2 * kk, kIdesc, (kb | kk) != 0);
           }
+          umma_commit(&empty[s]);  // frees the chunk stage once these MMAs finish
         }
-        umma_commit(&empty[s]);
-        umma_commit(&tfull[b]);
+        if (ok) umma_commit(&tfull[b]);
       }
     }
   } else {
     // ------------------------------------------------------ epilogue
-    const int wg = (warp - 2) >> 2;  // accumulator buffer this warpgroup drains
+    const int wg = (warp - 2) >> 2;  // warpgroup 0 or 1
     const int q = warp & 3;          // tensor-memory lane quarter of this warp
+    const int r = 32 * q + lane;     // row within the tile
     int i = 0;
     for (int64_t t = blockIdx.x; t < total; t += gridDim.x, ++i) {
-      if ((i & 1) != wg) continue;
+      if constexpr (D == 128) {
+        if ((i & 1) != wg) continue;  // warpgroups alternate tiles
+      }
+      const int b = i & 1;
       const uint32_t jb = (uint32_t)((i >> 1) & 1);
       // warp-uniform outcome: tcgen05.ld below is a warp-collective
-      const bool ok = __all_sync(0xffffffffu, mbar_wait(&tfull[wg], jb, P.err));
+      const bool ok = __all_sync(0xffffffffu, mbar_wait(&tfull[b], jb, P.err));
       if (!ok) break;
       tc_fence_after();
       const int sg = seg_of(t);
-      const int64_t row = (t - P.tile_begin[sg]) * C::kM + 32 * q + lane;
-      const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + wg * C::kAccCols;
+      const int64_t row = (t - P.tile_begin[sg]) * C::kM + r;
+      const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + b * C::kAccCols;
 
-      float v[32];
-      float2 ss2 = make_float2(0.f, 0.f);
+      float u[4][32];
+      float2 s2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+      if constexpr (D == 128) {
 #pragma unroll
-      for (int c = 0; c < C::kAccCols / 32; ++c) {
-        tmem_ld32(ta + 32 * c, v);
-        tmem_wait_ld();
+        for (int gq = 0; gq < 4; ++gq) tmem_ld32(ta + 32 * gq, u[gq]);
+      } else {
+        // this warpgroup's half of the pairs: a = acc0[64 wg ..], b = acc1[64 wg ..]
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const float2 p = make_float2(v[e], v[e + 1]);
-          ss2 = __ffma2_rn(p, p, ss2);
+        for (int gq = 0; gq < 2; ++gq) {
+          tmem_ld32(ta + 64 * wg + 32 * gq, u[gq]);
+          tmem_ld32(ta + 128 + 64 * wg + 32 * gq, u[2 + gq]);
         }
       }
-      const float ss = ss2.x + ss2.y;  // = 128 ||x||^2
+      tmem_wait_ld();
+      // accumulator in registers: hand the buffer back to the MMA issuer
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[b]);
+
+#pragma unroll
+      for (int gq = 0; gq < 4; ++gq)
+#pragma unroll
+        for (int e = 0; e < 32; e += 2) {
+          const float2 p = make_float2(u[gq][e], u[gq][e + 1]);
+          s2[gq & 1] = __ffma2_rn(p, p, s2[gq & 1]);
+        }
+      float ss = (s2[0].x + s2[0].y) + (s2[1].x + s2[1].y);
+      if constexpr (D == 256) {
+        // pairs (a, b) -> (a + b, a - b) = (u_lo, u_hi); exchange the partial
+        // sum of a^2 + b^2 with the other warpgroup (same row)
+        const float2 neg1 = make_float2(-1.f, -1.f);
+#pragma unroll
+        for (int gq = 0; gq < 2; ++gq)
+#pragma unroll
+          for (int e = 0; e < 32; e += 2) {
+            const float2 a = make_float2(u[gq][e], u[gq][e + 1]);
+            const float2 bb = make_float2(u[2 + gq][e], u[2 + gq][e + 1]);
+            const float2 lo = __fadd2_rn(a, bb);
+            const float2 hi = __ffma2_rn(bb, neg1, a);
+            u[gq][e] = lo.x; u[gq][e + 1] = lo.y;
+            u[2 + gq][e] = hi.x; u[2 + gq][e + 1] = hi.y;
+          }
+        xch[wg * 256 + r] = ss;
+        named_bar_sync(1, 256);
+        ss = xch[r] + xch[256 + r];
+      }
+      // ss = 128 ||x||^2 for both head dims
       const float norm = ss > 0.f ? sqrtf(ss * (1.0f / 128.0f)) : 1e-8f;
       const float rs = 1.0f / (norm * (D == 128 ? 11.313708498984761f : 16.0f));
 
-      uint32_t code[(D / 32) * Q::kCodeWords];
-      uint32_t resw[D / 32];
+      uint32_t code[4 * kCW];
+      uint32_t resw[4];
       float2 acc = make_float2(0.f, 0.f);
-      if constexpr (D == 128) {
-#pragma unroll
-        for (int gq = 0; gq < 4; ++gq) {
-          tmem_ld32(ta + 32 * gq, v);
-          tmem_wait_ld();
-          Q::run(v, rs, P, &code[gq * Q::kCodeWords], resw[gq], acc);
-        }
-      } else {
-        const float2 neg1 = make_float2(-1.f, -1.f);
-#pragma unroll
-        for (int gq = 0; gq < 4; ++gq) {
-          float w[32];
-          tmem_ld32(ta + 32 * gq, v);
-          tmem_ld32(ta + 128 + 32 * gq, w);
-          tmem_wait_ld();
-#pragma unroll
-          for (int e = 0; e < 32; e += 2) {
-            const float2 a = make_float2(v[e], v[e + 1]);
-            const float2 bb = make_float2(w[e], w[e + 1]);
-            const float2 lo = __fadd2_rn(a, bb);
-            const float2 hi = __ffma2_rn(bb, neg1, a);
-            v[e] = lo.x; v[e + 1] = lo.y;
-            w[e] = hi.x; w[e + 1] = hi.y;
-          }
-          Q::run(v, rs, P, &code[gq * Q::kCodeWords], resw[gq], acc);
-          Q::run(w, rs, P, &code[(4 + gq) * Q::kCodeWords], resw[4 + gq], acc);
-        }
-      }
-      // accumulator fully read: hand the buffer back to the MMA issuer
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[wg]);
-
-      float rn = 0.f;
-      if (RES) {
-        const float a = acc.x + acc.y;
-        rn = a > 0.f ? norm * sqrtf(a) : 1e-8f;
-      }
-      if (row < P.n_rows[sg]) {
-        constexpr int kCW = (D / 32) * Q::kCodeWords;
-        uint4* cdst = reinterpret_cast<uint4*>(P.code[sg] + row * kCW);
-#pragma unroll
-        for (int k = 0; k < kCW / 4; ++k)
-          cdst[k] = make_uint4(code[4 * k], code[4 * k + 1], code[4 * k + 2], code[4 * k + 3]);
+      quant_groups<CK, RES, 4>(u, rs, P, code, resw, acc);
+      float a = acc.x + acc.y;
+      if constexpr (D == 256) {
         if (RES) {
-          uint4* rdst = reinterpret_cast<uint4*>(P.res[sg] + row * (D / 32));
-#pragma unroll
-          for (int k = 0; k < D / 128; ++k)
-            rdst[k] = make_uint4(resw[4 * k], resw[4 * k + 1], resw[4 * k + 2], resw[4 * k + 3]);
-          P.rnorms[sg][row] = rn;
+          xch[512 + wg * 128 + r] = a;
+          named_bar_sync(1, 256);
+          a = xch[512 + r] + xch[512 + 128 + r];
         }
-        P.norms[sg][row] = norm;
+      }
+      const float rn = a > 0.f ? norm * sqrtf(a) : 1e-8f;
+
+      if (row < P.n_rows[sg]) {
+        constexpr int kRowCW = (D / 32) * kCW;
+        uint32_t* crow = P.code[sg] + row * kRowCW;
+        if constexpr (D == 128) {
+          store_words<4 * kCW>(crow, code);
+          if (RES) store_words<4>(P.res[sg] + row * 4, resw);
+        } else {
+          // groups held: u_lo 64wg.. (words 2wg, 2wg+1), u_hi (words 4+2wg, 5+2wg)
+          store_words<2 * kCW>(crow + 2 * wg * kCW, code);
+          store_words<2 * kCW>(crow + (4 + 2 * wg) * kCW, code + 2 * kCW);
+          if (RES) {
+            store_words<2>(P.res[sg] + row * 8 + 2 * wg, resw);
+            store_words<2>(P.res[sg] + row * 8 + 4 + 2 * wg, resw + 2);
+          }
+        }
+        if (D == 128 || wg == 0) {
+          P.norms[sg][row] = norm;
+          if (RES) P.rnorms[sg][row] = rn;
+        }
       }
     }
   }

@@ -169,4 +169,44 @@ struct Quant<kCbGen4, RES> {
   }
 };
 
+// NG groups of 32 transformed values, symmetric 2-level codebook, with the
+// 2*NG bit-packing chains interleaved (a single chain of 32 dependent funnel
+// shifts per word stalls on latency).  Residual bit via
+//   v = y - c[idx] >= 0  <=>  idx XOR [|y| < c1]     (except |y| == c1 exactly)
+// and sum (y - c[idx])^2 = sum (|y| - c1)^2.
+template <int NG, bool RES>
+__device__ __forceinline__ void quant_sym2_groups(const float (&u)[NG][32], float rs,
+                                                  float c1, uint32_t* code,
+                                                  uint32_t* resw, float2& acc) {
+  const float2 nrs = make_float2(-rs, -rs);
+  const float2 zero = make_float2(0.f, 0.f);
+  uint32_t cw[NG], sw[NG];
+#pragma unroll
+  for (int g = 0; g < NG; ++g) cw[g] = sw[g] = 0u;
+  float2 a2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+  for (int k = 30; k >= 0; k -= 2) {
+#pragma unroll
+    for (int g = 0; g < NG; ++g) {
+      const float2 q = __ffma2_rn(make_float2(u[g][k], u[g][k + 1]), nrs, zero);
+      cw[g] = push_sign(cw[g], q.y);
+      cw[g] = push_sign(cw[g], q.x);
+      if (RES) {
+        const float t0 = __fmaf_rn(fabsf(u[g][k]), rs, -c1);
+        const float t1 = __fmaf_rn(fabsf(u[g][k + 1]), rs, -c1);
+        sw[g] = push_sign(sw[g], t1);
+        sw[g] = push_sign(sw[g], t0);
+        const float2 t = make_float2(t0, t1);
+        a2[g & 1] = __ffma2_rn(t, t, a2[g & 1]);
+      }
+    }
+  }
+#pragma unroll
+  for (int g = 0; g < NG; ++g) {
+    code[g] = cw[g];
+    if (RES) resw[g] = cw[g] ^ sw[g];
+  }
+  acc = __fadd2_rn(acc, __fadd2_rn(a2[0], a2[1]));
+}
+
 }  // namespace kh
