@@ -13,6 +13,11 @@
 // Accumulation stays in the rotated domain; one FWHT per group in the
 // combine step.  A partial record is (m, l, acc[0..D-1]).
 #include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
+#include <type_traits>
+#include <utility>
 
 #include "kh_common.cuh"
 #include "kh_internal.h"
@@ -186,6 +191,328 @@ __global__ void __launch_bounds__(D)
   out[g * D + t] = L > 0.f ? sh[t] * P.dk[t] / L : 0.f;
 }
 
+
+// ---------------------------------------------------------------------------
+// Decode v2: table-driven.  Both planes of a row are read as bytes.
+//
+// K side: per CTA (one query) a table holds, for every byte position p of a
+// plane and byte value v, the partial sum  sum_{k<8, bit k of v} q~[8p+k];
+// a row's masked sums M1, M2 are 2 * D/8 table lookups.
+// V side: instead of touching D accumulators per row, each row adds its
+// softmax weight into a histogram per byte position, H_p[byte] += w; after a
+// chunk of rows the histograms are folded into the D accumulators
+// (acc[8p+b] = sum over v with bit b set of H_p[v]).
+//
+// Bank-conflict-free addressing: a table / histogram entry (slot j, value v)
+// lives at float index 32 v + j, i.e. in bank j.  Lane l of a warp visits
+// byte position p = (k + l) mod P at step k (P = D/8 positions), in copy
+// c = l / P of the table (32 / P copies), slot j = p + P c: the 32 lanes of
+// a warp always touch 32 distinct banks.  A lane reads its row's bytes in
+// that rotated order by loading the plane's words rotated by
+// (l mod P) / 4 and funnel-shifting by 8 (l mod 4) bits.
+// Calls f(std::integral_constant<int, I>) for I = 0 .. N-1, fully unrolled.
+template <class F, int... I>
+__device__ __forceinline__ void static_for_impl(F&& f, std::integer_sequence<int, I...>) {
+  (f(std::integral_constant<int, I>{}), ...);
+}
+template <int N, class F>
+__device__ __forceinline__ void static_for(F&& f) {
+  static_for_impl(f, std::make_integer_sequence<int, N>{});
+}
+
+template <int D>
+struct V2Cfg {
+  static constexpr int kP = D / 8;          // byte positions per plane
+  static constexpr int kW = D / 32;         // words per plane
+  static constexpr int kThreads = 256;      // thread = row in both passes
+  static constexpr int kRPT = 8;            // rows per thread per chunk (registers)
+  static constexpr int kChunk = kRPT * kThreads;
+  static constexpr int kTab = 256 * 32;     // entries per K table / V histogram plane
+  // lut | hist (int32 fixed point, 2 planes) | q~ | reduction scratch | folded sums [4][D]
+  static constexpr int kSmem = (3 * kTab + D + 64 + 4 * D) * 4;
+};
+
+// Rotated view of one row plane: byte k of the result = plane byte
+// (k + r) mod P, r = lane mod P.
+template <int D>
+__device__ __forceinline__ void load_rotated(const uint32_t* __restrict__ plane, int wr,
+                                             int bs, uint32_t (&rot)[D / 32]) {
+  constexpr int kW = D / 32;
+  uint32_t w[kW];
+  static_for<kW>([&](auto ic) {
+    constexpr int i = decltype(ic)::value;
+    w[i] = __ldg(plane + ((i + wr) & (kW - 1)));
+  });
+  static_for<kW>([&](auto ic) {
+    constexpr int i = decltype(ic)::value;
+    rot[i] = __funnelshift_r(w[i], w[(i + 1) % kW], bs);
+  });
+}
+
+// byte k of a rotated plane, zero-extended
+template <int K>
+__device__ __forceinline__ uint32_t byte_of(const uint32_t* rot) {
+  return __byte_perm(rot[K >> 2], 0u, 0x4440u + (K & 3));
+}
+
+template <int NT>
+__device__ __forceinline__ float block_sum(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = 0.f;
+#pragma unroll
+  for (int i = 0; i < NT / 32; ++i) r += red[i];
+  return r;
+}
+
+template <int NT>
+__device__ __forceinline__ float block_max(float v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
+  __syncthreads();
+  float r = red[0];
+#pragma unroll
+  for (int i = 1; i < NT / 32; ++i) r = fmaxf(r, red[i]);
+  return r;
+}
+
+template <int D>
+struct RowK {
+  uint32_t c[D / 32], r[D / 32];
+  float n, rn;
+};
+
+template <int D>
+__global__ void __launch_bounds__(256)
+    decode_v2_kernel(const __grid_constant__ DecodeParams P) {
+  using C = V2Cfg<D>;
+  constexpr int kP = C::kP;
+  constexpr int kW = C::kW;
+  constexpr int NT = C::kThreads;
+  extern __shared__ float sm[];
+  float* lut = sm;                                         // [256][32]
+  int* hist = reinterpret_cast<int*>(sm + C::kTab);        // [2][256][32], fixed point
+  float* qt = sm + 3 * C::kTab;                            // [D]
+  float* red = qt + D;                                     // [64]
+  int* fsum = reinterpret_cast<int*>(red + 64);            // [plane * copies][D]
+
+  const int t = threadIdx.x;
+  const int lane = t & 31;
+  const int64_t g = blockIdx.y;
+  const int split = blockIdx.x;
+  const int64_t len = P.seq_end - P.seq_begin;
+  const int64_t s0 = P.seq_begin + len * split / P.n_splits;
+  const int64_t s1 = P.seq_begin + len * (split + 1) / P.n_splits;
+  const float inv_sqrt_d = 1.0f / sqrtf((float)D);
+  const float qjl = 0.7978845608028654f / (float)D;  // sqrt(2/pi) / D
+  const float dc = P.c1 - P.c0;
+
+  // q~ = H(q (.) d) / sqrt(D)
+  for (int i = t; i < D; i += NT) qt[i] = P.q[g * D + i] * P.dk[i];
+  __syncthreads();
+  for (int h = 1; h < D; h <<= 1) {
+    for (int b = t; b < D / 2; b += NT) {
+      const int lo = (b / h) * 2 * h + (b % h);
+      const float a = qt[lo], c = qt[lo + h];
+      qt[lo] = a + c;
+      qt[lo + h] = a - c;
+    }
+    __syncthreads();
+  }
+  float qpart = 0.f;
+  for (int i = t; i < D; i += NT) {
+    qt[i] *= inv_sqrt_d;
+    qpart += qt[i];
+  }
+  const float Q = block_sum<NT>(qpart, red);
+
+  // K table (every copy) and zeroed histograms
+  for (int e = t; e < kP * 256; e += NT) {
+    const int pos = e % kP, v = e / kP;
+    float sum = 0.f;
+#pragma unroll
+    for (int k = 0; k < 8; ++k) sum += ((v >> k) & 1) ? qt[8 * pos + k] : 0.f;
+#pragma unroll
+    for (int c = 0; c < 32 / kP; ++c) lut[v * 32 + pos + kP * c] = sum;
+  }
+  for (int e = t; e < 2 * C::kTab; e += NT) hist[e] = 0;
+  __syncthreads();
+
+  // lane-constant addressing: slot(k) = ((k + lane) mod P) + P (lane / P)
+  const int rr = lane % kP;
+  const int wr = rr >> 2, bs = 8 * (rr & 3);
+  const int copy_off = kP * (lane / kP);
+  const char* lutb = reinterpret_cast<const char*>(lut);
+  char* h1b = reinterpret_cast<char*>(hist);
+  char* h2b = reinterpret_cast<char*>(hist + C::kTab);
+  int slot4[kP];  // byte offset of slot(k) in a table / histogram row
+  static_for<kP>([&](auto kc) {
+    constexpr int k = decltype(kc)::value;
+    slot4[k] = 4 * (((k + lane) % kP) + copy_off);
+  });
+
+  float m_run = -INFINITY, l_run = 0.f, c_run = 0.f;
+  // accumulators of the elements this thread folds: element t (D <= NT)
+  float acc = 0.f;
+
+  constexpr int R = C::kRPT;
+  for (int64_t c0 = s0; c0 < s1; c0 += C::kChunk) {
+    const int n = (int)min((int64_t)C::kChunk, s1 - c0);
+    const int64_t row0 = g * P.seq_len + c0;
+    // this thread's rows of the chunk: t + r * NT, r < R
+    float lg[R];
+    // ---------------- pass 1: scores -> logits (two rows in flight)
+    float mloc = -INFINITY;
+    static_for<R / 2>([&](auto rc) {
+      constexpr int r0 = 2 * decltype(rc)::value;
+      RowK<D> a[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int ii = t + (r0 + u) * NT;
+        const int64_t row = row0 + (ii < n ? ii : 0);
+        load_rotated<D>(P.k_code + row * kW, wr, bs, a[u].c);
+        load_rotated<D>(P.k_res + row * kW, wr, bs, a[u].r);
+        a[u].n = __ldg(P.k_norms + row);
+        a[u].rn = __ldg(P.k_rnorms + row);
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        float m1 = 0.f, m2 = 0.f;
+        const RowK<D>& ar = a[u];
+        static_for<kP>([&](auto kc) {
+          constexpr int k = decltype(kc)::value;
+          const uint32_t b1 = __byte_perm(ar.c[k >> 2], 0u, 0x4440u + (k & 3));
+          const uint32_t b2 = __byte_perm(ar.r[k >> 2], 0u, 0x4440u + (k & 3));
+          m1 += *reinterpret_cast<const float*>(lutb + b1 * 128 + slot4[k]);
+          m2 += *reinterpret_cast<const float*>(lutb + b2 * 128 + slot4[k]);
+        });
+        const float score = ar.n * (P.c0 * Q + dc * m1) + inv_sqrt_d * (2.f * m2 - Q) * ar.rn;
+        const bool ok = t + (r0 + u) * NT < n;
+        lg[r0 + u] = ok ? score * P.sm_scale : -INFINITY;
+        mloc = fmaxf(mloc, lg[r0 + u]);
+      }
+    });
+    const float m_c = block_max<NT>(mloc, red);
+    const float m_new = fmaxf(m_run, m_c);
+    const float alpha = expf(m_run - m_new);  // rescales earlier chunks (0 on the first)
+    m_run = m_new;
+
+    // ---------------- pass 2a: softmax weights of this thread's rows
+    float w1[R], w2[R];
+    float lsum = 0.f, wmax = 0.f;
+#pragma unroll
+    for (int r = 0; r < R; ++r) {
+      const int ii = t + r * NT;
+      const bool ok = ii < n;
+      const int64_t row = row0 + (ok ? ii : 0);
+      const float p = ok ? expf(lg[r] - m_new) : 0.f;
+      const float va = __ldg(P.v_norms + row) * inv_sqrt_d;
+      const float vb = __ldg(P.v_rnorms + row) * qjl;
+      lsum += p;
+      w1[r] = p * va * dc;
+      w2[r] = 2.f * p * vb;
+      wmax = fmaxf(wmax, fmaxf(w1[r], w2[r]));
+    }
+    const float l_c = block_sum<NT>(lsum, red);
+    const float w_max = block_max<NT>(wmax, red);
+    // Fixed point: the bins of one (plane, copy) sum a subset of the chunk's
+    // rows, so a bin stays below n * w_max * scale_inv <= 2^30.  The constant
+    // term sum_s p (a c0 - b) = -sum_s (w1 + w2) / 2 (c0 = -c1) is built from
+    // the same quantised weights, so a row rounded to zero drops out of every
+    // output element alike instead of biasing their sum.
+    const float scale_inv = w_max > 0.f ? 1073741824.0f / (w_max * (float)n) : 0.f;
+    const float scale = w_max > 0.f ? (w_max * (float)n) / 1073741824.0f : 0.f;
+    float csum = 0.f;  // constant term in units of the quantum
+
+    // ---------------- pass 2b: scatter the V bytes into the histograms
+    static_for<R / 2>([&](auto rc) {
+      constexpr int r0 = 2 * decltype(rc)::value;
+      RowK<D> a[2];
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const int ii = t + (r0 + u) * NT;
+        const int64_t row = row0 + (ii < n ? ii : 0);
+        load_rotated<D>(P.v_code + row * kW, wr, bs, a[u].c);
+        load_rotated<D>(P.v_res + row * kW, wr, bs, a[u].r);
+      }
+#pragma unroll
+      for (int u = 0; u < 2; ++u) {
+        const RowK<D>& ar = a[u];
+        const int f1 = __float2int_rn(w1[r0 + u] * scale_inv);  // 0 for rows past n
+        const int f2 = __float2int_rn(w2[r0 + u] * scale_inv);
+        csum += (float)f1 * (P.c0 / dc) - 0.5f * (float)f2;
+        static_for<kP>([&](auto kc) {
+          constexpr int k = decltype(kc)::value;
+          const uint32_t b1 = __byte_perm(ar.c[k >> 2], 0u, 0x4440u + (k & 3));
+          const uint32_t b2 = __byte_perm(ar.r[k >> 2], 0u, 0x4440u + (k & 3));
+          atomicAdd(reinterpret_cast<int*>(h1b + b1 * 128 + slot4[k]), f1);
+          atomicAdd(reinterpret_cast<int*>(h2b + b2 * 128 + slot4[k]), f2);
+        });
+      }
+    });
+
+    const float c_c = block_sum<NT>(csum, red) * scale;  // also fences the histograms
+    // ---------------- fold: acc[8 pos + b] = sum over bins v with bit b set.
+    // Thread t takes (plane, slot) = t / 4 and bins [64 q, 64 q + 64), q = t % 4:
+    // each bin is read once; bits 0..5 of v are compile-time, bits 6..7 are q.
+    {
+      const int combo = t >> 2, q = t & 3;
+      const int pl = combo >> 5, slot = combo & 31;
+      const int* hb = hist + pl * C::kTab + slot;
+      int sb[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      int tot = 0;
+      static_for<64>([&](auto jc) {
+        constexpr int j = decltype(jc)::value;
+        const int h = hb[(64 * q + j) * 32];
+        tot += h;
+        if (j & 1) sb[0] += h;
+        if (j & 2) sb[1] += h;
+        if (j & 4) sb[2] += h;
+        if (j & 8) sb[3] += h;
+        if (j & 16) sb[4] += h;
+        if (j & 32) sb[5] += h;
+      });
+      sb[6] = (q & 1) ? tot : 0;
+      sb[7] = (q & 2) ? tot : 0;
+#pragma unroll
+      for (int bb = 0; bb < 8; ++bb) {
+        sb[bb] += __shfl_xor_sync(0xffffffffu, sb[bb], 1);
+        sb[bb] += __shfl_xor_sync(0xffffffffu, sb[bb], 2);
+      }
+      if (q == 0) {
+        // slot = pos + P * copy; element 8 pos + b of plane pl, copy class pl * copies + copy
+        const int pos = slot % kP, cp = slot / kP;
+#pragma unroll
+        for (int bb = 0; bb < 8; ++bb) fsum[(pl * (32 / kP) + cp) * D + 8 * pos + bb] = sb[bb];
+      }
+    }
+    __syncthreads();
+    if (t < D) {
+      float a = 0.f;
+#pragma unroll
+      for (int k = 0; k < 2 * (32 / kP); ++k) a += (float)fsum[k * D + t];
+      acc = acc * alpha + a * scale;
+    }
+    l_run = l_run * alpha + l_c;
+    c_run = c_run * alpha + c_c;
+    __syncthreads();
+    for (int e = t; e < 2 * C::kTab; e += NT) hist[e] = 0;
+    __syncthreads();
+  }
+
+  float* rec = P.partials + (g * P.part_stride + P.part_offset + split) * (D + 2);
+  if (t < D) rec[2 + t] = c_run + acc;
+  if (t == 0) {
+    rec[0] = m_run;
+    rec[1] = l_run;
+  }
+}
+
 }  // namespace
 
 kh_status launch_decode_partial(const DecodeRequest& r, cudaStream_t stream) {
@@ -204,8 +531,25 @@ kh_status launch_decode_partial(const DecodeRequest& r, cudaStream_t stream) {
   P.c1 = r.cb.c[1];
   for (int i = 0; i < r.D; ++i) P.dk[i] = r.dk[i];
   const dim3 grid((unsigned)r.n_splits, (unsigned)r.n_groups);
-  if (r.D == 128) decode_partial_kernel<128><<<grid, 128, 0, stream>>>(P);
-  else decode_partial_kernel<256><<<grid, 256, 0, stream>>>(P);
+  const char* env = getenv("KUDAHITAM_DECODE_PATH");
+  if (env && strcmp(env, "v1") == 0) {
+    if (r.D == 128) decode_partial_kernel<128><<<grid, 128, 0, stream>>>(P);
+    else decode_partial_kernel<256><<<grid, 256, 0, stream>>>(P);
+  } else if (r.D == 128) {
+    static std::once_flag once;
+    std::call_once(once, [] {
+      cudaFuncSetAttribute(decode_v2_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           V2Cfg<128>::kSmem);
+    });
+    decode_v2_kernel<128><<<grid, V2Cfg<128>::kThreads, V2Cfg<128>::kSmem, stream>>>(P);
+  } else {
+    static std::once_flag once;
+    std::call_once(once, [] {
+      cudaFuncSetAttribute(decode_v2_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                           V2Cfg<256>::kSmem);
+    });
+    decode_v2_kernel<256><<<grid, V2Cfg<256>::kThreads, V2Cfg<256>::kSmem, stream>>>(P);
+  }
   return cudaGetLastError() == cudaSuccess ? KH_OK : KH_ELAUNCH;
 }
 

@@ -250,10 +250,11 @@ def decode_workspace_bytes(n_groups: int, n_splits: int, head_dim: int) -> int:
 
 
 def default_splits(n_groups: int, seq_len: int, device) -> int:
-    """Enough (group, split) blocks to fill every SM a few times over."""
+    """About 8 waves of (group, split) blocks at 2 blocks per SM, with at
+    least 1024 rows per split."""
     sms = torch.cuda.get_device_properties(device).multi_processor_count
-    want = max(1, (4 * sms + n_groups - 1) // max(n_groups, 1))
-    return int(max(1, min(want, seq_len // 256 if seq_len >= 256 else 1, 1024)))
+    want = max(1, round(16 * sms / max(n_groups, 1)))
+    return int(max(1, min(want, seq_len // 1024 if seq_len >= 1024 else 1, 1024)))
 
 
 def decode_partial(q: torch.Tensor, k: PackedKV, v: PackedKV, dk, dv, centroids,

@@ -119,6 +119,13 @@ def test_materialize_and_compat_op(D, bits):
     assert K.rel_err(rn.cpu().numpy()[:, 0], ref["rnorms"]) < 1e-4
 
 
+@pytest.fixture(params=["v2", "v1"])
+def decode_path(request, monkeypatch):
+    """Decode kernel: the table-driven one (default) or the direct one."""
+    monkeypatch.setenv("KUDAHITAM_DECODE_PATH", request.param)
+    return request.param
+
+
 def _caches(G, S, D, seed):
     dk = rademacher(D, 10).numpy()
     dv = rademacher(D, 11).numpy()
@@ -129,8 +136,8 @@ def _caches(G, S, D, seed):
 
 
 @pytest.mark.parametrize("D", [128, 256])
-@pytest.mark.parametrize("S", [1, 7, 300, 1000])
-def test_decode_attention_matches_oracle(D, S):
+@pytest.mark.parametrize("S", [1, 7, 300, 1000, 5000])
+def test_decode_attention_matches_oracle(D, S, decode_path):
     G = 5
     dk, dv, c, k, v = _caches(G, S, D, seed=S)
     q = torch.randn(G, D, generator=torch.Generator().manual_seed(S)).to(torch.bfloat16)
@@ -149,7 +156,7 @@ def test_decode_attention_matches_oracle(D, S):
             assert K.normwise(got[gi], want[gi]) < 1e-3, (n_splits, gi)
 
 
-def test_decode_split_invariance_and_empty_splits():
+def test_decode_split_invariance_and_empty_splits(decode_path):
     D, G, S = 128, 3, 5
     dk, dv, c, k, v = _caches(G, S, D, seed=1)
     q = torch.randn(G, D, device="cuda")
@@ -161,7 +168,7 @@ def test_decode_split_invariance_and_empty_splits():
         assert torch.allclose(got, base, rtol=1e-4, atol=1e-6), n  # split-K reassociation
 
 
-def test_decode_seq_sharded_emulated_on_one_gpu():
+def test_decode_seq_sharded_emulated_on_one_gpu(decode_path):
     """The multi-GPU combine, with the ranks' slots filled by one process:
     partial records of every S-shard in their own slots, merged once."""
     D, G, S, world, n_splits = 128, 4, 1000, 4, 2
