@@ -72,18 +72,22 @@ def synth_kv(seed: int, device) -> tuple[torch.Tensor, torch.Tensor]:
 
 
 class ClockSampler:
-    """SM clock and clock-event (throttle) reasons sampled through NVML every
-    50 ms during the timed region (read-only queries)."""
+    """SM clock and clock-event (throttle) reasons, sampled through NVML
+    (read-only queries) every 5 ms from a host thread.  Samples carry host
+    timestamps so that the ones taken inside the timed region can be told
+    apart from those of the adjacent loaded loops (warm-up and per-launch
+    timing of the same kernel)."""
 
     REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
                "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4}
 
-    def __init__(self, index: int):
+    def __init__(self, index: int, period_s: float = 0.005):
         self.index = index
-        self.sm: list[float] = []
+        self.period = period_s
+        self.samples: list[tuple[float, float, int]] = []  # (t, MHz, reasons mask)
         self.max_mhz = None
-        self.mask = 0
         self.err = None
+        self.region = None
         self._stop = threading.Event()
 
     def __enter__(self):
@@ -104,12 +108,16 @@ class ClockSampler:
         N = self._N
         while not self._stop.is_set():
             try:
-                self.sm.append(float(N.nvmlDeviceGetClockInfo(self._h, N.NVML_CLOCK_SM)))
-                self.mask |= int(N.nvmlDeviceGetCurrentClocksEventReasons(self._h))
+                mhz = float(N.nvmlDeviceGetClockInfo(self._h, N.NVML_CLOCK_SM))
+                mask = int(N.nvmlDeviceGetCurrentClocksEventReasons(self._h))
+                self.samples.append((time.perf_counter(), mhz, mask))
             except Exception as e:
                 self.err = repr(e)
                 return
-            self._stop.wait(0.05)
+            self._stop.wait(self.period)
+
+    def mark_region(self, t0: float, t1: float) -> None:
+        self.region = (t0, t1)
 
     def __exit__(self, *exc):
         self._stop.set()
@@ -117,10 +125,19 @@ class ClockSampler:
             self._t.join(timeout=2)
 
     def summary(self) -> dict:
-        out = {"sm_mhz": statistics.median(self.sm) if self.sm else None,
+        inside = [s for s in self.samples
+                  if self.region and self.region[0] <= s[0] <= self.region[1]]
+        use = inside if len(inside) >= 3 else self.samples
+        mask = 0
+        for s in self.samples:
+            mask |= s[2]
+        out = {"sm_mhz": statistics.median(s[1] for s in use) if use else None,
                "sm_max_mhz": self.max_mhz,
-               "reasons": sorted(k for k, b in self.REASONS.items() if self.mask & b),
-               "samples": len(self.sm)}
+               "reasons": sorted(k for k, b in self.REASONS.items() if mask & b),
+               "samples": len(use), "samples_in_timed_region": len(inside),
+               "window": ("timed region" if use is inside else
+                          "timed region + adjacent warm-up and per-launch loops of "
+                          "the same kernel (timed region shorter than 3 samples)")}
         if self.err:
             out["error"] = self.err
         return out
@@ -230,7 +247,7 @@ def run_engine(args, world, rank, local):
     peak, peak_kind = peaks()
 
     if args.only == "decode":
-        dec = decode_bench(dev, args)
+        dec = decode_bench(dev, args, world, rank)
         if rank == 0:
             print(json.dumps({"decode": dec}), flush=True)
         return
@@ -243,12 +260,13 @@ def run_engine(args, world, rank, local):
     def step():
         ops.compress_many([k, v], d, c, residual=True, outs=outs)
 
-    for _ in range(max(args.warmup, 3)):
-        step()
-    torch.cuda.synchronize()
-    barrier(world)
-    torch.cuda.synchronize()
     with ClockSampler(local) as clk:
+        for _ in range(max(args.warmup, 3)):
+            step()
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        h0 = time.perf_counter()
         t0 = torch.cuda.Event(enable_timing=True)
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record(stream)
@@ -256,15 +274,20 @@ def run_engine(args, world, rank, local):
             step()
         t1.record(stream)
         torch.cuda.synchronize()
+        clk.mark_region(h0, time.perf_counter())
         barrier(world)
         torch.cuda.synchronize()
-    ms_local = t0.elapsed_time(t1)
-    ms = max_over_ranks(ms_local, world)
-    rows_all = 2 * ROWS_PER_TENSOR * world * args.steps
-    value = rows_all / (ms / 1e3)
+        ms_local = t0.elapsed_time(t1)
+        ms = max_over_ranks(ms_local, world)
+        rows_all = 2 * ROWS_PER_TENSOR * world * args.steps
+        value = rows_all / (ms / 1e3)
 
-    # dominant kernel, per-launch times
-    per = time_loop(step, max(args.steps, 5), stream)
+        # dominant kernel, per-launch times (at least ~0.3 s of launches so the
+        # clock record has samples under this load)
+        n_launch = max(args.steps, 5)
+        if args.only == "all":
+            n_launch = max(n_launch, int(0.3 / max(ms_local / args.steps / 1e3, 1e-6)))
+        per = time_loop(step, min(n_launch, 5000), stream)
     launch_ms = statistics.median(per)
     rows_launch = 2 * ROWS_PER_TENSOR
     achieved = rows_launch * ALG_BYTES_PER_ROW / (launch_ms / 1e3) / 1e9
@@ -273,6 +296,7 @@ def run_engine(args, world, rank, local):
             "traffic": (NCU_TRAFFIC_BYTES_PER_ROW * rows_launch
                         if NCU_TRAFFIC_BYTES_PER_ROW else None),
             "algorithmic_bytes": rows_launch * ALG_BYTES_PER_ROW,
+            "launch_ms_median": launch_ms, "launches_timed": len(per),
             "kernel": ("compress_simt_kernel<__half,256,Sym2,RES>"
                        if os.environ.get("KUDAHITAM_COMPRESS_PATH") == "simt"
                        else "compress_tc_kernel<__half,256,Sym2,RES>")}
@@ -320,7 +344,7 @@ def run_engine(args, world, rank, local):
            "ms_per_step": e2e_ms / e2e_steps}
     del hk, hv, gk, gv
 
-    dec = decode_bench(dev, args) if args.only == "all" else None
+    dec = decode_bench(dev, args, world, rank) if args.only == "all" else None
 
     line = {"metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
@@ -336,47 +360,66 @@ def run_engine(args, world, rank, local):
         print(json.dumps(line), flush=True)
 
 
-def decode_bench(dev, args) -> dict:
+def decode_bench(dev, args, world: int = 1, rank: int = 0) -> dict:
+    """Decode step over the 40k-token compressed cache.  With N ranks the
+    sequence is sharded (S/N rows per group on each rank) and the split-K
+    records are combined with one NCCL all-reduce; the time is the max over
+    ranks (strong scaling: the total S is fixed)."""
+    from kudahitam import dist as khdist
     from kudahitam import ops
     from kudahitam.codebook import lloyd_max, rademacher
     G = DEC_B * DEC_H
-    g = torch.Generator(device=dev).manual_seed(5)
+    a, b = khdist.shard_range(DEC_S, world, rank)
+    S_loc = b - a
+    g = torch.Generator(device=dev).manual_seed(5 + 7919 * rank)
     dk, dv = rademacher(DEC_D, 10), rademacher(DEC_D, 11)
     c = lloyd_max(1, DEC_D)
-    pk = ops.empty_packed((G, DEC_S, DEC_D), 1, True, dev)
-    pv = ops.empty_packed((G, DEC_S, DEC_D), 1, True, dev)
+    pk = ops.empty_packed((G, S_loc, DEC_D), 1, True, dev)
+    pv = ops.empty_packed((G, S_loc, DEC_D), 1, True, dev)
     for p, dd in ((pk, dk), (pv, dv)):
         for i in range(0, G, 64):
-            x = torch.randn(64, DEC_S, DEC_D, device=dev, generator=g).to(torch.bfloat16)
-            ops.compress(x, dd, c, out=p.rows(i * DEC_S, (i + 64) * DEC_S))
+            x = torch.randn(64, S_loc, DEC_D, device=dev, generator=g).to(torch.bfloat16)
+            ops.compress(x, dd, c, out=p.rows(i * S_loc, (i + 64) * S_loc))
     q = torch.randn(G, DEC_D, generator=torch.Generator().manual_seed(4)).to(torch.bfloat16).to(dev)
-    n_splits = ops.default_splits(G, DEC_S, dev)
-    ws = torch.empty(ops.decode_workspace_bytes(G, n_splits, DEC_D) // 4, device=dev)
-    out = torch.empty(G, DEC_D, device=dev)
+    n_splits = ops.default_splits(G, S_loc, dev)
     stream = torch.cuda.current_stream(dev)
     qf = q.float()
+    sm = 1 / math.sqrt(DEC_D)
+    if world == 1:
+        ws = torch.empty(ops.decode_workspace_bytes(G, n_splits, DEC_D) // 4, device=dev)
+        out = torch.empty(G, DEC_D, device=dev)
 
-    def step():
-        ops.decode_partial(qf, pk, pv, dk, dv, c, 1 / math.sqrt(DEC_D), n_splits, ws, n_splits,
-                           0, DEC_S)
-        ops.decode_combine(ws, n_splits, dv, out)
+        def step():
+            ops.decode_partial(qf, pk, pv, dk, dv, c, sm, n_splits, ws, n_splits, 0, S_loc)
+            ops.decode_combine(ws, n_splits, dv, out)
+    else:
+        buf = torch.empty(G * world * n_splits * (DEC_D + 2), device=dev)
+
+        def step():
+            khdist.decode_attention_seq_sharded(qf, pk, pv, dk, dv, c, sm, n_splits,
+                                                partials=buf)
 
     for _ in range(3):
         step()
+    torch.cuda.synchronize()
+    barrier(world)
     per = time_loop(step, max(5, min(args.steps, 20)), stream)
-    ms = statistics.median(per)
-    bytes_step = G * DEC_S * DEC_BYTES_PER_ROW
+    ms = max_over_ranks(statistics.median(per), world)
+    bytes_step = G * DEC_S * DEC_BYTES_PER_ROW  # whole job
     peak, _ = peaks()
-    return {"config": "q bf16 [32,16,128]; K and V 2-bit-mode packed, S=40000",
+    return {"config": "q bf16 [32,16,128]; K and V 2-bit-mode packed, S=40000"
+                      + (f", sequence-sharded over {world} GPUs + one NCCL all-reduce"
+                         if world > 1 else ""),
             "us_per_step": ms * 1e3, "us_per_token": ms * 1e3 / DEC_B,
-            "n_splits": n_splits, "gbs": bytes_step / (ms / 1e3) / 1e9,
-            "frac_of_measured_hbm": bytes_step / (ms / 1e3) / 1e9 / peak}
+            "n_splits": n_splits, "scaling": "strong" if world > 1 else None,
+            "gbs": bytes_step / (ms / 1e3) / 1e9,
+            "frac_of_measured_hbm_per_gpu": bytes_step / world / (ms / 1e3) / 1e9 / peak}
 
 
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
-    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--steps", type=int, default=400)
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["engine", "reference"], default="engine")
     ap.add_argument("--no-cpu-baseline", action="store_true")

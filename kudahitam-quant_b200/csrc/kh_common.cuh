@@ -1,7 +1,7 @@
 // kh_common.cuh -- shared device helpers for the sm_100a kernels.
 //
 // Inline-PTX wrappers for mbarriers and TMA (cp.async.bulk.tensor), written
-// from the PTX ISA.  No TMA load here uses .multicast::cluster.
+// from the PTX ISA.  Every TMA load here is a plain per-CTA load.
 #pragma once
 
 #include <cuda.h>

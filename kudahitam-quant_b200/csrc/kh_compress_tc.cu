@@ -15,7 +15,7 @@
 //   warps 2..9  two epilogue warpgroups; warpgroup g drains accumulator buffer
 //               g (tiles alternate), thread = tensor-memory lane = row
 // All mbarrier waits are bounded (kh::mbar_wait); a timeout records an error
-// bit and every role leaves its loop.  No TMA load uses cluster multicast.
+// bit and every role leaves its loop.  Every TMA load is a plain per-CTA load.
 #include <algorithm>
 #include <cstring>
 #include <mutex>

@@ -535,20 +535,24 @@ kh_status launch_decode_partial(const DecodeRequest& r, cudaStream_t stream) {
   if (env && strcmp(env, "v1") == 0) {
     if (r.D == 128) decode_partial_kernel<128><<<grid, 128, 0, stream>>>(P);
     else decode_partial_kernel<256><<<grid, 256, 0, stream>>>(P);
-  } else if (r.D == 128) {
-    static std::once_flag once;
-    std::call_once(once, [] {
-      cudaFuncSetAttribute(decode_v2_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           V2Cfg<128>::kSmem);
-    });
-    decode_v2_kernel<128><<<grid, V2Cfg<128>::kThreads, V2Cfg<128>::kSmem, stream>>>(P);
   } else {
-    static std::once_flag once;
-    std::call_once(once, [] {
-      cudaFuncSetAttribute(decode_v2_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                           V2Cfg<256>::kSmem);
-    });
-    decode_v2_kernel<256><<<grid, V2Cfg<256>::kThreads, V2Cfg<256>::kSmem, stream>>>(P);
+    // the shared-memory opt-in is a per-device function attribute
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return KH_ECUDA;
+    static std::once_flag once128[64], once256[64];
+    if (r.D == 128) {
+      std::call_once(once128[dev & 63], [] {
+        cudaFuncSetAttribute(decode_v2_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             V2Cfg<128>::kSmem);
+      });
+      decode_v2_kernel<128><<<grid, V2Cfg<128>::kThreads, V2Cfg<128>::kSmem, stream>>>(P);
+    } else {
+      std::call_once(once256[dev & 63], [] {
+        cudaFuncSetAttribute(decode_v2_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             V2Cfg<256>::kSmem);
+      });
+      decode_v2_kernel<256><<<grid, V2Cfg<256>::kThreads, V2Cfg<256>::kSmem, stream>>>(P);
+    }
   }
   return cudaGetLastError() == cudaSuccess ? KH_OK : KH_ELAUNCH;
 }
