@@ -136,6 +136,38 @@ int kh_score(const float* q, int64_t n_groups, int n_q, int head_dim,
              float* out, void* stream);
 
 /*
+ * kh_score_packed_compat -- the reference's packed-cache scorer with its own
+ * argument layout and arithmetic.  Replaces fused_asymmetric_attention
+ * (fused_asymmetric_attention_packed_cuda / _kernel, KudaHitamCUDA.cu:695-797,
+ * called from KudaHitamQuant_full-reasoning.py:411 and :563):
+ *   q~   = H(q_h (.) d) / sqrt(D)   (unnormalised Hadamard, strides 1,2,4,..)
+ *   sum1 = sum_i q~_i * (centroids[i][v_i] * k_norm)
+ *   sum2 = sum_i q_i * signs_i      (unrotated q, raw signs values)
+ *   out  = sum1 + k_norm * scale * sum2 * r_norm
+ * v_i = bit (i & 7) of byte (i >> 3) of the row's 32 packed bytes; when
+ * 0 <= layer_id < 8 and bit layer_id of active_mask is set, v_i = nibble
+ * (i & 1) of byte (i >> 1) of the row's 128 packed bytes.  Same summation
+ * order as the reference kernel (per-lane fused multiply-adds over
+ * i = lane, lane + 32, ..., then a butterfly reduction).
+ *   q         device fp16 [n_heads][D]
+ *   k_packed  device uint8 [n_heads][seq_len][32 or 128], 4-byte aligned
+ *   signs     device fp16 [n_heads][seq_len][D]
+ *   d         device float [D]
+ *   k_norms, r_norms  device float [n_heads][seq_len]
+ *   centroids device float [D][16]
+ *   out       device float [n_heads][seq_len]
+ * Unlike the other entry points, d and centroids are DEVICE arrays here, as
+ * in the reference binding.  D is a power of two in [32, 256].
+ */
+int kh_score_packed_compat(const void* q, int64_t n_heads, int head_dim,
+                           int64_t seq_len, const uint8_t* k_packed,
+                           const void* signs, const float* d,
+                           const float* k_norms, const float* r_norms,
+                           const float* centroids, int layer_id,
+                           int active_mask, float scale, float* out,
+                           void* stream);
+
+/*
  * Decode attention over a compressed K/V cache (split-K / flash-decoding).
  * Not present in the reference, which stops at the scores
  * (KudaHitamQuant_full.py:373-386); softmax(score * sm_scale) . V_hat with

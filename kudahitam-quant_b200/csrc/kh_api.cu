@@ -287,6 +287,30 @@ int kh_score(const float* q, int64_t n_groups, int n_q, int head_dim,
                       static_cast<cudaStream_t>(stream));
 }
 
+int kh_score_packed_compat(const void* q, int64_t n_heads, int head_dim,
+                           int64_t seq_len, const uint8_t* k_packed,
+                           const void* signs, const float* d,
+                           const float* k_norms, const float* r_norms,
+                           const float* centroids, int layer_id,
+                           int active_mask, float scale, float* out,
+                           void* stream) {
+  if (n_heads < 0 || seq_len < 0 || layer_id < 0) return KH_EINVAL;
+  if (head_dim != 32 && head_dim != 64 && head_dim != 128 && head_dim != 256)
+    return KH_EINVAL;
+  if (n_heads >= 65536) return KH_EINVAL;  // grid.y limit
+  if (n_heads == 0 || seq_len == 0) return KH_OK;
+  if (!q || !k_packed || !signs || !d || !k_norms || !r_norms || !centroids || !out)
+    return KH_EINVAL;
+  if (!aligned4(k_packed) || !aligned4(d) || !aligned4(k_norms) || !aligned4(r_norms) ||
+      !aligned4(centroids) || !aligned4(out) ||
+      reinterpret_cast<uintptr_t>(q) % 2 != 0 || reinterpret_cast<uintptr_t>(signs) % 2 != 0)
+    return KH_EALIGN;
+  const int nibble = (layer_id < 8 && ((active_mask & 0xff) >> layer_id) & 1) ? 1 : 0;
+  return launch_score_packed_compat(q, n_heads, head_dim, seq_len, k_packed, signs, d,
+                                    k_norms, r_norms, centroids, nibble, scale, out,
+                                    static_cast<cudaStream_t>(stream));
+}
+
 int64_t kh_decode_workspace_bytes(int64_t n_groups, int n_splits,
                                   int head_dim) {
   if (n_groups < 0 || n_splits < 1 || !valid_head_dim(head_dim)) return -1;

@@ -513,6 +513,337 @@ __global__ void __launch_bounds__(256)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Decode v3: segment-exact softmax, one-instruction table addressing.
+//
+// A split's rows are processed in segments of up to kSeg rows:
+//   phase 1  K scores through the byte table -> logits (log2 units) kept in
+//            shared memory for the whole segment; block max;
+//   phase 2a sums of p and of the V weights (fixed-point range);
+//   phase 2b V bytes scattered into int32 histograms with the segment's
+//            fixed-point scale 2^30 / sum(weights) (any bin <= 2^30 + n/2);
+//   fold     histograms -> D accumulators, rescaled online across segments.
+// Table and histograms share one array of 256 rows (one per byte value) of
+// 64 32-bit entries: the K table uses entries 0..31 during phase 1, the two V
+// histograms entries 0..31 (code plane) and 32..63 (residual plane) during
+// phase 2.  Row v starts at byte 256 v, so one byte-permute of (plane word,
+// lane slot offset) yields the byte address 256 v + 4 slot, and the residual
+// histogram is the same address + 128 (an immediate).  Slots follow the
+// conflict-free rotation described for v2.  The next rows' plane words are
+// loaded while the current rows are scored / scattered.
+template <int D>
+struct V3Cfg {
+  static constexpr int kP = D / 8;
+  static constexpr int kW = D / 32;
+  static constexpr int kCopies = 32 / kP;
+  static constexpr int kThreads = 256;
+  static constexpr int kSeg = 8192;
+  static constexpr int kBatch = D == 128 ? 2 : 1;  // rows per thread in flight
+  // tab [256][64] | logits [kSeg] | fold partials [2][4][32][8] | q~ [D] |
+  // nibble tables [2][kP][16] | reduction scratch [64]
+  static constexpr int kTabWords = 256 * 64;
+  static constexpr int kSmem =
+      (kTabWords + kSeg + 2048 + D + 2 * kP * 16 + 64) * 4;
+};
+
+// byte-permute selector: result = slot_off + (byte b of x) * 256
+template <int B>
+__device__ __forceinline__ uint32_t tab_addr(uint32_t x, uint32_t slot_off) {
+  return __byte_perm(x, slot_off, 0x5504u | (B << 4));
+}
+
+template <int D>
+__device__ __forceinline__ void load_k_row(const DecodeParams& P, int64_t row, int wr, int bs,
+                                           RowK<D>& a) {
+  constexpr int kW = D / 32;
+  load_rotated<D>(P.k_code + row * kW, wr, bs, a.c);
+  load_rotated<D>(P.k_res + row * kW, wr, bs, a.r);
+  a.n = __ldg(P.k_norms + row);
+  a.rn = __ldg(P.k_rnorms + row);
+}
+
+template <int D>
+__device__ __forceinline__ void load_v_row(const DecodeParams& P, int64_t row, int wr, int bs,
+                                           RowK<D>& a) {
+  constexpr int kW = D / 32;
+  load_rotated<D>(P.v_code + row * kW, wr, bs, a.c);
+  load_rotated<D>(P.v_res + row * kW, wr, bs, a.r);
+}
+
+template <int NT>
+__device__ __forceinline__ float2 block_sum2(float2 v, float* red) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1) {
+    v.x += __shfl_xor_sync(0xffffffffu, v.x, o);
+    v.y += __shfl_xor_sync(0xffffffffu, v.y, o);
+  }
+  __syncthreads();
+  if ((threadIdx.x & 31) == 0) {
+    red[2 * (threadIdx.x >> 5)] = v.x;
+    red[2 * (threadIdx.x >> 5) + 1] = v.y;
+  }
+  __syncthreads();
+  float2 r = make_float2(0.f, 0.f);
+#pragma unroll
+  for (int i = 0; i < NT / 32; ++i) {
+    r.x += red[2 * i];
+    r.y += red[2 * i + 1];
+  }
+  return r;
+}
+
+template <int D>
+__global__ void __launch_bounds__(256, 2)
+    decode_v3_kernel(const __grid_constant__ DecodeParams P) {
+  using C = V3Cfg<D>;
+  constexpr int kP = C::kP;
+  constexpr int NT = C::kThreads;
+  constexpr int B = C::kBatch;
+  constexpr float kLog2e = 1.4426950408889634f;
+  constexpr float kLn2 = 0.6931471805599453f;
+  extern __shared__ __align__(16) unsigned char smem_raw[];
+  unsigned char* tabb = smem_raw;                                    // [256][64] words
+  float* lg = reinterpret_cast<float*>(smem_raw) + C::kTabWords;    // [kSeg]
+  int* part = reinterpret_cast<int*>(lg + C::kSeg);                 // [2][4][32][8]
+  float* qt = reinterpret_cast<float*>(part + 2048);                // [D]
+  float* nib = qt + D;                                               // [2][kP][16]
+  float* red = nib + 2 * kP * 16;                                    // [64]
+
+  const int t = threadIdx.x;
+  const int lane = t & 31;
+  const int64_t g = blockIdx.y;
+  const int split = blockIdx.x;
+  const int64_t len = P.seq_end - P.seq_begin;
+  const int64_t s0 = P.seq_begin + len * split / P.n_splits;
+  const int64_t s1 = P.seq_begin + len * (split + 1) / P.n_splits;
+  const float inv_sqrt_d = 1.0f / sqrtf((float)D);
+  const float qjl = 0.7978845608028654f / (float)D;  // sqrt(2/pi) / D
+  const float dc = P.c1 - P.c0;
+  const float lscale = P.sm_scale * kLog2e;
+  const float c0dc = P.c0 / dc;
+
+  // q~ = H(q (.) d) / sqrt(D) and its nibble partial-sum tables
+  for (int i = t; i < D; i += NT) qt[i] = P.q[g * D + i] * P.dk[i];
+  __syncthreads();
+  for (int h = 1; h < D; h <<= 1) {
+    for (int b = t; b < D / 2; b += NT) {
+      const int lo = (b / h) * 2 * h + (b % h);
+      const float a = qt[lo], c = qt[lo + h];
+      qt[lo] = a + c;
+      qt[lo + h] = a - c;
+    }
+    __syncthreads();
+  }
+  float qpart = 0.f;
+  for (int i = t; i < D; i += NT) {
+    qt[i] *= inv_sqrt_d;
+    qpart += qt[i];
+  }
+  const float Q = block_sum<NT>(qpart, red);  // (its barriers also publish qt)
+  for (int e = t; e < 2 * kP * 16; e += NT) {
+    const int hi = e / (kP * 16), pos = (e / 16) % kP, nv = e & 15;
+    float s = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) s += ((nv >> k) & 1) ? qt[8 * pos + 4 * hi + k] : 0.f;
+    nib[e] = s;
+  }
+  __syncthreads();
+
+  // lane constants: byte k of a rotated plane is plane byte (k + rr) mod kP,
+  // looked up in slot ((k + lane) mod kP) + kP (lane / kP)
+  const int rr = lane % kP;
+  const int wr = rr >> 2, bs = 8 * (rr & 3);
+  uint32_t slot4[kP];
+  static_for<kP>([&](auto kc) {
+    constexpr int k = decltype(kc)::value;
+    slot4[k] = 4u * (uint32_t)(((k + lane) % kP) + kP * (lane / kP));
+  });
+
+  float m_run = -INFINITY, l_run = 0.f, c_run = 0.f, acc = 0.f;
+
+  for (int64_t c0 = s0; c0 < s1; c0 += C::kSeg) {
+    const int n = (int)min((int64_t)C::kSeg, s1 - c0);
+    const int64_t row0 = g * P.seq_len + c0;
+    const int nb = (n + NT * B - 1) / (NT * B);  // batches of B rows per thread
+
+    // K table into entries 0..31 of every row: T[v][slot] = sum of q~ over
+    // the set bits of v at the slot's byte position
+    for (int e = t; e < 256 * 32; e += NT) {
+      const int v = e >> 5, slot = e & 31, pos = slot % kP;
+      reinterpret_cast<float*>(tabb)[v * 64 + slot] =
+          nib[pos * 16 + (v & 15)] + nib[kP * 16 + pos * 16 + (v >> 4)];
+    }
+    __syncthreads();
+
+    // ---------------- phase 1: logits (log2 units) of the segment
+    float mloc = -INFINITY;
+    {
+      RowK<D> a[2][B];
+      auto load_batch = [&](RowK<D>(&dst)[B], int bi) {
+#pragma unroll
+        for (int u = 0; u < B; ++u) {
+          const int ii = t + (bi * B + u) * NT;
+          load_k_row<D>(P, row0 + (ii < n ? ii : 0), wr, bs, dst[u]);
+        }
+      };
+      auto score_batch = [&](const RowK<D>(&src)[B], int bi) {
+#pragma unroll
+        for (int u = 0; u < B; ++u) {
+          float2 m = make_float2(0.f, 0.f);
+          static_for<kP>([&](auto kc) {
+            constexpr int k = decltype(kc)::value;
+            const float x1 = *reinterpret_cast<const float*>(
+                tabb + tab_addr<k & 3>(src[u].c[k >> 2], slot4[k]));
+            const float x2 = *reinterpret_cast<const float*>(
+                tabb + tab_addr<k & 3>(src[u].r[k >> 2], slot4[k]));
+            m = __fadd2_rn(m, make_float2(x1, x2));
+          });
+          const float score = src[u].n * (P.c0 * Q + dc * m.x) +
+                              inv_sqrt_d * (2.f * m.y - Q) * src[u].rn;
+          const int ii = t + (bi * B + u) * NT;
+          if (ii < n) {
+            const float l2 = score * lscale;
+            lg[ii] = l2;
+            mloc = fmaxf(mloc, l2);
+          }
+        }
+      };
+      load_batch(a[0], 0);
+      for (int bi = 0; bi < nb; bi += 2) {
+        load_batch(a[1], bi + 1);
+        score_batch(a[0], bi);
+        if (bi + 1 < nb) {
+          load_batch(a[0], bi + 2);
+          score_batch(a[1], bi + 1);
+        }
+      }
+    }
+    const float m_seg = block_max<NT>(mloc, red);  // also: phase-1 table reads done
+    const float m_new = fmaxf(m_run, m_seg);
+    const float alpha = exp2f(m_run - m_new);  // 0 on the first segment
+    m_run = m_new;
+
+    // zero both histograms (all 64 entries of every row)
+    {
+      int4* z = reinterpret_cast<int4*>(tabb);
+      for (int e = t; e < C::kTabWords / 4; e += NT) z[e] = make_int4(0, 0, 0, 0);
+    }
+
+    // ---------------- phase 2a: sum of p and of the V weights
+    float2 sums = make_float2(0.f, 0.f);
+#pragma unroll 4
+    for (int ii = t; ii < n; ii += NT) {
+      const float p = exp2f(lg[ii] - m_new);
+      const int64_t row = row0 + ii;
+      const float w = p * (__ldg(P.v_norms + row) * inv_sqrt_d * dc +
+                           2.f * __ldg(P.v_rnorms + row) * qjl);
+      sums.x += p;
+      sums.y += w;
+    }
+    const float2 tot = block_sum2<NT>(sums, red);  // barriers also order the zeroing
+    const float l_c = tot.x;
+    const float scale_inv = tot.y > 0.f ? 1073741824.0f / tot.y : 0.f;
+    const float scale = tot.y / 1073741824.0f;
+
+    // ---------------- phase 2b: scatter V bytes with fixed-point weights
+    float csum = 0.f;  // constant term in quanta
+    const float k1 = inv_sqrt_d * dc * scale_inv, k2 = 2.f * qjl * scale_inv;
+    {
+      RowK<D> a[2][B];
+      auto load_batch = [&](RowK<D>(&dst)[B], int bi) {
+#pragma unroll
+        for (int u = 0; u < B; ++u) {
+          const int ii = t + (bi * B + u) * NT;
+          const int64_t row = row0 + (ii < n ? ii : 0);
+          load_v_row<D>(P, row, wr, bs, dst[u]);
+          dst[u].n = __ldg(P.v_norms + row);
+          dst[u].rn = __ldg(P.v_rnorms + row);
+        }
+      };
+      auto scatter_batch = [&](const RowK<D>(&src)[B], int bi) {
+#pragma unroll
+        for (int u = 0; u < B; ++u) {
+          const int ii = t + (bi * B + u) * NT;
+          const bool ok = ii < n;
+          const float p = ok ? exp2f(lg[ok ? ii : 0] - m_new) : 0.f;
+          const int f1 = __float2int_rn(p * src[u].n * k1);
+          const int f2 = __float2int_rn(p * src[u].rn * k2);
+          csum += (float)f1 * c0dc - 0.5f * (float)f2;
+          static_for<kP>([&](auto kc) {
+            constexpr int k = decltype(kc)::value;
+            atomicAdd(reinterpret_cast<int*>(tabb + tab_addr<k & 3>(src[u].c[k >> 2], slot4[k])),
+                      f1);
+            atomicAdd(reinterpret_cast<int*>(tabb + 128 +
+                                             tab_addr<k & 3>(src[u].r[k >> 2], slot4[k])),
+                      f2);
+          });
+        }
+      };
+      load_batch(a[0], 0);
+      for (int bi = 0; bi < nb; bi += 2) {
+        load_batch(a[1], bi + 1);
+        scatter_batch(a[0], bi);
+        if (bi + 1 < nb) {
+          load_batch(a[0], bi + 2);
+          scatter_batch(a[1], bi + 1);
+        }
+      }
+    }
+    const float c_c = block_sum<NT>(csum, red) * scale;  // also fences the histograms
+
+    // ---------------- fold: thread (plane, quarter, slot) sums its 64 bins
+    // per bit of the byte value; bits 6, 7 of v are the quarter's bits
+    {
+      const int slot = t & 31, pl = (t >> 5) & 1, q = t >> 6;
+      const int* hb = reinterpret_cast<const int*>(tabb) + 32 * pl + slot;
+      int sb[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      int tt = 0;
+      static_for<64>([&](auto jc) {
+        constexpr int j = decltype(jc)::value;
+        const int h = hb[(64 * q + j) * 64];
+        tt += h;
+        if (j & 1) sb[0] += h;
+        if (j & 2) sb[1] += h;
+        if (j & 4) sb[2] += h;
+        if (j & 8) sb[3] += h;
+        if (j & 16) sb[4] += h;
+        if (j & 32) sb[5] += h;
+      });
+      sb[6] = (q & 1) ? tt : 0;
+      sb[7] = (q & 2) ? tt : 0;
+      int4* pp = reinterpret_cast<int4*>(part + ((pl * 4 + q) * 32 + slot) * 8);
+      pp[0] = make_int4(sb[0], sb[1], sb[2], sb[3]);
+      pp[1] = make_int4(sb[4], sb[5], sb[6], sb[7]);
+    }
+    __syncthreads();
+    if (t < D) {
+      const int pos = t >> 3, bb = t & 7;
+      float a = 0.f;
+#pragma unroll
+      for (int pl = 0; pl < 2; ++pl) {
+        int s = 0;  // one plane: a subset sum of one histogram, < 2^31
+#pragma unroll
+        for (int q = 0; q < 4; ++q)
+#pragma unroll
+          for (int cp = 0; cp < C::kCopies; ++cp)
+            s += part[((pl * 4 + q) * 32 + pos + kP * cp) * 8 + bb];
+        a += (float)s;
+      }
+      acc = acc * alpha + a * scale;
+    }
+    l_run = l_run * alpha + l_c;
+    c_run = c_run * alpha + c_c;
+    __syncthreads();  // fold reads done before the next segment's table
+  }
+
+  float* rec = P.partials + (g * P.part_stride + P.part_offset + split) * (D + 2);
+  if (t < D) rec[2 + t] = c_run + acc;
+  if (t == 0) {
+    rec[0] = m_run * kLn2;  // natural-log units for the combine step
+    rec[1] = l_run;
+  }
+}
+
 }  // namespace
 
 kh_status launch_decode_partial(const DecodeRequest& r, cudaStream_t stream) {
@@ -532,26 +863,27 @@ kh_status launch_decode_partial(const DecodeRequest& r, cudaStream_t stream) {
   for (int i = 0; i < r.D; ++i) P.dk[i] = r.dk[i];
   const dim3 grid((unsigned)r.n_splits, (unsigned)r.n_groups);
   const char* env = getenv("KUDAHITAM_DECODE_PATH");
-  if (env && strcmp(env, "v1") == 0) {
+  const int path = (env && strcmp(env, "v1") == 0) ? 1 : (env && strcmp(env, "v2") == 0) ? 2 : 3;
+  if (path == 1) {
     if (r.D == 128) decode_partial_kernel<128><<<grid, 128, 0, stream>>>(P);
     else decode_partial_kernel<256><<<grid, 256, 0, stream>>>(P);
   } else {
     // the shared-memory opt-in is a per-device function attribute
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return KH_ECUDA;
-    static std::once_flag once128[64], once256[64];
-    if (r.D == 128) {
-      std::call_once(once128[dev & 63], [] {
-        cudaFuncSetAttribute(decode_v2_kernel<128>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             V2Cfg<128>::kSmem);
+    static std::once_flag once[4][64];
+    auto launch = [&](auto kern, int slot, int smem, int threads) {
+      std::call_once(once[slot][dev & 63], [&] {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       });
-      decode_v2_kernel<128><<<grid, V2Cfg<128>::kThreads, V2Cfg<128>::kSmem, stream>>>(P);
+      kern<<<grid, threads, smem, stream>>>(P);
+    };
+    if (path == 2) {
+      if (r.D == 128) launch(decode_v2_kernel<128>, 0, V2Cfg<128>::kSmem, V2Cfg<128>::kThreads);
+      else launch(decode_v2_kernel<256>, 1, V2Cfg<256>::kSmem, V2Cfg<256>::kThreads);
     } else {
-      std::call_once(once256[dev & 63], [] {
-        cudaFuncSetAttribute(decode_v2_kernel<256>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                             V2Cfg<256>::kSmem);
-      });
-      decode_v2_kernel<256><<<grid, V2Cfg<256>::kThreads, V2Cfg<256>::kSmem, stream>>>(P);
+      if (r.D == 128) launch(decode_v3_kernel<128>, 2, V3Cfg<128>::kSmem, V3Cfg<128>::kThreads);
+      else launch(decode_v3_kernel<256>, 3, V3Cfg<256>::kSmem, V3Cfg<256>::kThreads);
     }
   }
   return cudaGetLastError() == cudaSuccess ? KH_OK : KH_ELAUNCH;

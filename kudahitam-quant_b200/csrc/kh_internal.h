@@ -64,6 +64,12 @@ kh_status launch_materialize(const uint32_t* code, const uint32_t* res,
 
 kh_status launch_fwht(float* x, int64_t n_rows, int D, cudaStream_t stream);
 
+kh_status launch_score_packed_compat(const void* q, int64_t n_heads, int D, int64_t seq_len,
+                                     const uint8_t* k_packed, const void* signs,
+                                     const float* d, const float* k_norms,
+                                     const float* r_norms, const float* centroids,
+                                     int nibble, float scale, float* out,
+                                     cudaStream_t stream);
 kh_status launch_score(const float* q, int64_t n_groups, int n_q, int D,
                        const uint32_t* code, const uint32_t* res,
                        const float* norms, const float* rnorms,

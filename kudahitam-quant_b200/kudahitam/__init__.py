@@ -29,11 +29,13 @@ fwht_ = ops.fwht_
 
 def load_cuda_ext():
     """The reference's extension handle (KudaHitamQuant_full.py:43-98): an
-    object with ``forward`` (in-place orthonormal FWHT of [N, D] float32 rows)
-    and ``ultra_fused_full_fusion`` (the fused compressor with the reference
-    kernel's five outputs).  Raises NativeLibraryError when the engine is not
+    object with ``forward`` (in-place orthonormal FWHT of [N, D] float32 rows),
+    ``ultra_fused_full_fusion`` (the fused compressor with the reference
+    kernel's five outputs) and ``fused_asymmetric_attention`` (the packed-byte
+    scorer, KudaHitamCUDA.cu:695-797).  Raises NativeLibraryError when the engine is not
     built, instead of returning None."""
     from . import _lib
     _lib.lib()
     return types.SimpleNamespace(forward=ops.fwht_,
-                                 ultra_fused_full_fusion=ops.ultra_fused_full_fusion)
+                                 ultra_fused_full_fusion=ops.ultra_fused_full_fusion,
+                                 fused_asymmetric_attention=ops.fused_asymmetric_attention)

@@ -317,3 +317,40 @@ def ultra_fused_full_fusion(x: torch.Tensor, d, centroids):
     p = compress(x, d, centroids, residual=True)
     m = materialize(p, d, centroids)
     return m["idx"], p.norms.view(-1, 1), m["kmse"], p.rnorms.view(-1, 1), m["signs"]
+
+
+def fused_asymmetric_attention(q: torch.Tensor, k_packed: torch.Tensor, signs: torch.Tensor,
+                               d_vec: torch.Tensor, k_norms: torch.Tensor,
+                               r_norms: torch.Tensor, centroids: torch.Tensor,
+                               layer_id: int, active_mask: int, scale: float) -> torch.Tensor:
+    """The reference's packed-cache scorer, same arguments and result
+    (fused_asymmetric_attention, KudaHitamCUDA.cu:774-797): q fp16 [H, D],
+    k_packed uint8 [H, S, 32 or 128], signs fp16 [H, S, D], d_vec float32
+    [D], k_norms / r_norms float32 [H, S], centroids float32 [D, 16].
+    Returns float32 [H, S]:  sum_i q~_i c[i][v_i] k_norm + k_norm * scale *
+    (q . signs) * r_norm  with q~ = H(q (.) d)/sqrt(D).  Inputs of another
+    dtype are converted; non-contiguous inputs are copied."""
+    dev = _require_cuda(q, k_packed, signs, d_vec, k_norms, r_norms, centroids)
+    H, D = q.shape
+    S = k_norms.shape[1]
+    nib = 0 <= layer_id < 8 and ((int(active_mask) & 0xFF) >> layer_id) & 1
+    bpt = 128 if nib else 32
+    if k_packed.shape[0] != H or k_packed.shape[1] != S or k_packed.shape[-1] != bpt:
+        raise ValueError(f"k_packed must be [H, S, {bpt}] for this layer")
+    if signs.shape != (H, S, D) or r_norms.shape != (H, S) or centroids.shape != (D, 16):
+        raise ValueError("signs [H, S, D], r_norms [H, S] and centroids [D, 16] expected")
+
+    def prep(t, dt):
+        t = t.to(dt)
+        return t.contiguous() if t.data_ptr() % 16 == 0 else torch.empty_like(t).copy_(t)
+
+    qh, sg = prep(q, torch.float16), prep(signs, torch.float16)
+    kp = prep(k_packed, torch.uint8)
+    dv, kn, rn, cb = (prep(t, torch.float32) for t in (d_vec, k_norms, r_norms, centroids))
+    out = torch.empty((H, S), dtype=torch.float32, device=dev)
+    with torch.cuda.device(dev):
+        _lib.call("kh_score_packed_compat", _vp(qh), H, D, S, _vp(kp), _vp(sg), _vp(dv),
+                  _vp(kn), _vp(rn), _vp(cb), int(layer_id), int(active_mask) & 0xFF,
+                  float(scale), _vp(out), _stream(dev))
+    return out
+

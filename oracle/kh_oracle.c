@@ -10,6 +10,10 @@
  *   score    : KudahitamCompressorV2.asymmetric_attention_scores,
  *              KudaHitamQuant_full.py:373-377 (with fwht() = the GPU
  *              `forward` kernel, i.e. orthonormal)
+ *   compat   : fused_asymmetric_attention_packed_kernel,
+ *              KudaHitamCUDA.cu:695-772 (packed-byte scorer); no golden
+ *              vectors exist for it (the reference kernel needs a GPU and its
+ *              callers need the HBBA encoder), so its parity is unpinned
  *
  * Arithmetic follows the kernel in fp32 and in its order: the same
  * butterfly stage order, the same segmented shuffle-tree reductions, the
@@ -258,6 +262,66 @@ void khx_decode(const float* q, int64_t G, int D, const float* k_kmse,
     }
     for (int e = 0; e < D; ++e) out[g * D + e] = L > 0 ? (float)(acc[e] / L) : 0.0f;
     free(logits);
+  }
+}
+
+/*
+ * Packed-byte scorer of the reference, KudaHitamCUDA.cu:695-772, in its
+ * order: q~ = H(q (.) d) with butterfly strides 1, 2, 4, ... (:723-733),
+ * times 1/sqrtf(D) (:734); lane l of the row's warp accumulates elements
+ * l, l+32, ... with one fused multiply-add each (k_recon = c[i][v] * k_norm
+ * rounded first, :758-761); a butterfly xor reduction over the 32 lanes
+ * (:765-768); out = fma(k_norm * scale * sum2, r_norm, sum1) (:771).
+ * v = bit (i & 7) of byte (i >> 3) (nibble = 0), or nibble (i & 1) of byte
+ * (i >> 1) (nibble = 1).  q fp16 [H][D]; k_packed [H][S][bpt]; signs fp16
+ * [H][S][D]; k_norms, r_norms [H][S]; centroids [D][16]; out [H][S].
+ */
+void khx_compat_score(const _Float16* q, int64_t H, int D, int64_t S,
+                      const uint8_t* k_packed, int nibble, const _Float16* signs,
+                      const float* d, const float* k_norms, const float* r_norms,
+                      const float* centroids, float scale, float* out) {
+  const int bpt = nibble ? 128 : 32;
+  const float inv = 1.0f / sqrtf((float)D);
+#ifdef _OPENMP
+#pragma omp parallel for schedule(static)
+#endif
+  for (int64_t h = 0; h < H; ++h) {
+    float sq[256], qp[256];
+    for (int i = 0; i < D; ++i) {
+      sq[i] = (float)q[h * D + i];
+      qp[i] = sq[i] * d[i];
+    }
+    for (int len = 1; len < D; len <<= 1) stage(qp, D, len);
+    for (int i = 0; i < D; ++i) qp[i] *= inv;
+    for (int64_t s = 0; s < S; ++s) {
+      const int64_t row = h * S + s;
+      const uint8_t* kp = k_packed + row * bpt;
+      const _Float16* sg = signs + row * D;
+      const float kn = k_norms[row];
+      float l1[32], l2[32];
+      for (int lane = 0; lane < 32; ++lane) {
+        float s1 = 0.f, s2 = 0.f;
+        for (int i = lane; i < D; i += 32) {
+          const int v = nibble ? (kp[i >> 1] >> ((i & 1) ? 4 : 0)) & 15 : (kp[i >> 3] >> (i & 7)) & 1;
+          const float k_recon = centroids[i * 16 + v] * kn;
+          s1 = fmaf(qp[i], k_recon, s1);
+          s2 = fmaf(sq[i], (float)sg[i], s2);
+        }
+        l1[lane] = s1;
+        l2[lane] = s2;
+      }
+      for (int o = 16; o > 0; o >>= 1) {
+        float n1[32], n2[32];
+        for (int lane = 0; lane < 32; ++lane) {
+          n1[lane] = l1[lane] + l1[lane ^ o];
+          n2[lane] = l2[lane] + l2[lane ^ o];
+        }
+        memcpy(l1, n1, sizeof(l1));
+        memcpy(l2, n2, sizeof(l2));
+      }
+      const float t2 = kn * scale * l2[0];
+      out[row] = fmaf(t2, r_norms[row], l1[0]);
+    }
   }
 }
 

@@ -50,6 +50,9 @@ def lib():
                                 _vp, ctypes.c_int64, _vp, _vp]
         L.khx_decode.argtypes = [_vp, ctypes.c_int64, ctypes.c_int, _vp, _vp, _vp, _vp, _vp,
                                  _vp, ctypes.c_int64, _vp, _vp, ctypes.c_float, _vp]
+        L.khx_compat_score.argtypes = [_vp, ctypes.c_int64, ctypes.c_int, ctypes.c_int64, _vp,
+                                       ctypes.c_int, _vp, _vp, _vp, _vp, _vp, ctypes.c_float,
+                                       _vp]
         L.khx_num_threads.restype = ctypes.c_int
         _lib = L
     return _lib
@@ -190,6 +193,23 @@ def decode(q, k_kmse, k_signs, k_rnorms, v_kmse, v_signs, v_rnorms, dk, dv,
     out = np.empty((G, D), np.float32)
     lib().khx_decode(_ptr(q), G, D, *[_ptr(a) for a in arrs[:6]], S, _ptr(arrs[6]),
                      _ptr(arrs[7]), float(sm_scale), _ptr(out))
+    return out
+
+
+def compat_score(q, k_packed, signs, d, k_norms, r_norms, centroids, nibble: bool,
+                 scale: float) -> np.ndarray:
+    """The reference's packed-byte scorer (KudaHitamCUDA.cu:695-772).
+    q fp16 [H, D]; k_packed uint8 [H, S, 32 or 128]; signs fp16 [H, S, D];
+    k_norms, r_norms [H, S]; centroids [D, 16].  Returns float32 [H, S]."""
+    q = np.ascontiguousarray(q, dtype=np.float16)
+    H, D = q.shape
+    kp = np.ascontiguousarray(k_packed, dtype=np.uint8)
+    S = kp.shape[1]
+    sg = np.ascontiguousarray(signs, dtype=np.float16)
+    arrs = [np.ascontiguousarray(a, dtype=np.float32) for a in (d, k_norms, r_norms, centroids)]
+    out = np.empty((H, S), np.float32)
+    lib().khx_compat_score(_ptr(q), H, D, S, _ptr(kp), int(bool(nibble)), _ptr(sg),
+                           *[_ptr(a) for a in arrs], float(scale), _ptr(out))
     return out
 
 

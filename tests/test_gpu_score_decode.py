@@ -119,9 +119,10 @@ def test_materialize_and_compat_op(D, bits):
     assert K.rel_err(rn.cpu().numpy()[:, 0], ref["rnorms"]) < 1e-4
 
 
-@pytest.fixture(params=["v2", "v1"])
+@pytest.fixture(params=["v3", "v2", "v1"])
 def decode_path(request, monkeypatch):
-    """Decode kernel: the table-driven one (default) or the direct one."""
+    """Decode kernel: segment-exact table-driven (default), chunked
+    table-driven, or the direct one."""
     monkeypatch.setenv("KUDAHITAM_DECODE_PATH", request.param)
     return request.param
 
@@ -150,6 +151,29 @@ def test_decode_attention_matches_oracle(D, S, decode_path):
                     rk["rnorms"].reshape(G, S), rv["kmse"].reshape(G, S, D),
                     rv["signs"].reshape(G, S, D), rv["rnorms"].reshape(G, S), dk, dv, sm)
     for n_splits in (1, 3, 16):
+        got = ops.decode_attention(q.cuda(), pk, pv, dk, dv, c, sm, n_splits=n_splits)
+        got = got.cpu().numpy()
+        for gi in range(G):
+            assert K.normwise(got[gi], want[gi]) < 1e-3, (n_splits, gi)
+
+
+@pytest.mark.parametrize("sm_mult", [1.0, 12.0])
+def test_decode_long_splits_and_peaked_softmax(sm_mult, decode_path):
+    """Splits longer than one 8192-row segment (online rescaling across
+    segments) and a sharply peaked softmax (fixed-point weights dominated by
+    a few rows)."""
+    D, G, S = 128, 2, 20000
+    dk, dv, c, k, v = _caches(G, S, D, seed=11)
+    q = torch.randn(G, D, generator=torch.Generator().manual_seed(2)).to(torch.bfloat16)
+    sm = sm_mult / math.sqrt(D)
+    pk = ops.compress(k.cuda(), dk, c)
+    pv = ops.compress(v.cuda(), dv, c)
+    rk = O.compress_v8(k, dk, c)
+    rv = O.compress_v8(v, dv, c)
+    want = O.decode(q.float().numpy(), rk["kmse"].reshape(G, S, D), rk["signs"].reshape(G, S, D),
+                    rk["rnorms"].reshape(G, S), rv["kmse"].reshape(G, S, D),
+                    rv["signs"].reshape(G, S, D), rv["rnorms"].reshape(G, S), dk, dv, sm)
+    for n_splits in (1, 2):
         got = ops.decode_attention(q.cuda(), pk, pv, dk, dv, c, sm, n_splits=n_splits)
         got = got.cpu().numpy()
         for gi in range(G):
