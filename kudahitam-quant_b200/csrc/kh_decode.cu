@@ -518,8 +518,9 @@ __global__ void __launch_bounds__(256)
 //
 // A split's rows are processed in segments of up to kSeg rows:
 //   phase 1  K scores through the byte table -> logits (log2 units) kept in
-//            shared memory for the whole segment; block max;
-//   phase 2a sums of p and of the V weights (fixed-point range);
+//            shared memory for the whole segment; per-thread online sums of
+//            p and of the V weights (for the fixed-point range); block max
+//            and block sums;
 //   phase 2b V bytes scattered into int32 histograms with the segment's
 //            fixed-point scale 2^30 / sum(weights) (any bin <= 2^30 + n/2);
 //   fold     histograms -> D accumulators, rescaled online across segments.
@@ -530,15 +531,26 @@ __global__ void __launch_bounds__(256)
 // lane slot offset) yields the byte address 256 v + 4 slot, and the residual
 // histogram is the same address + 128 (an immediate).  Slots follow the
 // conflict-free rotation described for v2.  The next rows' plane words are
-// loaded while the current rows are scored / scattered.
+// loaded while the current rows are scored / scattered.  (Bulk L2
+// prefetches of the rows a few batches ahead were measured slower.)
+// Build-time tuning knobs of decode v3 (defaults are the measured best).
+#ifndef KH_DECODE_WIDE_LOADS
+#define KH_DECODE_WIDE_LOADS 1
+#endif
+#ifndef KH_DECODE_SEG
+#define KH_DECODE_SEG 8192
+#endif
+#ifndef KH_DECODE_BATCH128
+#define KH_DECODE_BATCH128 2
+#endif
+
 template <int D>
 struct V3Cfg {
   static constexpr int kP = D / 8;
-  static constexpr int kW = D / 32;
   static constexpr int kCopies = 32 / kP;
   static constexpr int kThreads = 256;
-  static constexpr int kSeg = 8192;
-  static constexpr int kBatch = D == 128 ? 2 : 1;  // rows per thread in flight
+  static constexpr int kSeg = KH_DECODE_SEG;
+  static constexpr int kBatch = D == 128 ? KH_DECODE_BATCH128 : 1;  // rows per thread in flight
   // tab [256][64] | logits [kSeg] | fold partials [2][4][32][8] | q~ [D] |
   // nibble tables [2][kP][16] | reduction scratch [64]
   static constexpr int kTabWords = 256 * 64;
@@ -546,28 +558,67 @@ struct V3Cfg {
       (kTabWords + kSeg + 2048 + D + 2 * kP * 16 + 64) * 4;
 };
 
-// byte-permute selector: result = slot_off + (byte b of x) * 256
+// Byte address 256 * (byte B of x) + (byte B of slots): one byte-permute.
+// slots packs four lane slot offsets (each 4 * slot < 128) one per byte;
+// result bytes 2 and 3 replicate the (zero) sign bit of the slot byte.
+// (prmt.b32 generic mode: a selector nibble with its msb set replicates the
+// sign bit of the selected byte.)
 template <int B>
-__device__ __forceinline__ uint32_t tab_addr(uint32_t x, uint32_t slot_off) {
-  return __byte_perm(x, slot_off, 0x5504u | (B << 4));
+__device__ __forceinline__ uint32_t tab_addr(uint32_t x, uint32_t slots) {
+  constexpr uint32_t ys = 4u + B;  // selector of byte B of `slots`
+  constexpr uint32_t sel = ((8u | ys) << 12) | ((8u | ys) << 8) | (B << 4) | ys;
+  uint32_t r;
+  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(x), "r"(slots), "n"(sel));
+  return r;
+}
+
+template <int D>
+struct RowKV {
+  uint32_t c[D / 32], r[D / 32];
+  float n, rn, vn, vrn;
+};
+
+// v3 plane load.  D = 128: one 16-byte load per row (4 L1 wavefronts per
+// warp instead of 16 for four rotated 4-byte loads), rotated in registers:
+// words by wr (two select stages), then bytes by bs (funnel shifts).
+// D = 256: rotated 4-byte loads as in v2.
+template <int D>
+__device__ __forceinline__ void load_rotated_v3(const uint32_t* __restrict__ plane, int wr,
+                                                int bs, uint32_t (&rot)[D / 32]) {
+  if constexpr (D == 128 && KH_DECODE_WIDE_LOADS) {
+    const uint4 v = __ldg(reinterpret_cast<const uint4*>(plane));
+    const bool h = wr & 2, o = wr & 1;
+    const uint32_t y0 = h ? v.z : v.x, y1 = h ? v.w : v.y;
+    const uint32_t y2 = h ? v.x : v.z, y3 = h ? v.y : v.w;
+    const uint32_t z0 = o ? y1 : y0, z1 = o ? y2 : y1;
+    const uint32_t z2 = o ? y3 : y2, z3 = o ? y0 : y3;
+    rot[0] = __funnelshift_r(z0, z1, bs);
+    rot[1] = __funnelshift_r(z1, z2, bs);
+    rot[2] = __funnelshift_r(z2, z3, bs);
+    rot[3] = __funnelshift_r(z3, z0, bs);
+  } else {
+    load_rotated<D>(plane, wr, bs, rot);
+  }
 }
 
 template <int D>
 __device__ __forceinline__ void load_k_row(const DecodeParams& P, int64_t row, int wr, int bs,
-                                           RowK<D>& a) {
+                                           RowKV<D>& a) {
   constexpr int kW = D / 32;
-  load_rotated<D>(P.k_code + row * kW, wr, bs, a.c);
-  load_rotated<D>(P.k_res + row * kW, wr, bs, a.r);
+  load_rotated_v3<D>(P.k_code + row * kW, wr, bs, a.c);
+  load_rotated_v3<D>(P.k_res + row * kW, wr, bs, a.r);
   a.n = __ldg(P.k_norms + row);
   a.rn = __ldg(P.k_rnorms + row);
+  a.vn = __ldg(P.v_norms + row);
+  a.vrn = __ldg(P.v_rnorms + row);
 }
 
 template <int D>
 __device__ __forceinline__ void load_v_row(const DecodeParams& P, int64_t row, int wr, int bs,
                                            RowK<D>& a) {
   constexpr int kW = D / 32;
-  load_rotated<D>(P.v_code + row * kW, wr, bs, a.c);
-  load_rotated<D>(P.v_res + row * kW, wr, bs, a.r);
+  load_rotated_v3<D>(P.v_code + row * kW, wr, bs, a.c);
+  load_rotated_v3<D>(P.v_res + row * kW, wr, bs, a.r);
 }
 
 template <int NT>
@@ -621,6 +672,7 @@ __global__ void __launch_bounds__(256, 2)
   const float dc = P.c1 - P.c0;
   const float lscale = P.sm_scale * kLog2e;
   const float c0dc = P.c0 / dc;
+  const float wa = inv_sqrt_d * dc, wb = 2.f * qjl;  // V weight = p (wa |v| + wb r_norm)
 
   // q~ = H(q (.) d) / sqrt(D) and its nibble partial-sum tables
   for (int i = t; i < D; i += NT) qt[i] = P.q[g * D + i] * P.dk[i];
@@ -640,8 +692,8 @@ __global__ void __launch_bounds__(256, 2)
     qpart += qt[i];
   }
   const float Q = block_sum<NT>(qpart, red);  // (its barriers also publish qt)
-  for (int e = t; e < 2 * kP * 16; e += NT) {
-    const int hi = e / (kP * 16), pos = (e / 16) % kP, nv = e & 15;
+  for (int e = t; e < 2 * kP * 16; e += NT) {  // layout [hi][nibble][pos]
+    const int hi = e / (kP * 16), nv = (e / kP) & 15, pos = e % kP;
     float s = 0.f;
 #pragma unroll
     for (int k = 0; k < 4; ++k) s += ((nv >> k) & 1) ? qt[8 * pos + 4 * hi + k] : 0.f;
@@ -653,10 +705,14 @@ __global__ void __launch_bounds__(256, 2)
   // looked up in slot ((k + lane) mod kP) + kP (lane / kP)
   const int rr = lane % kP;
   const int wr = rr >> 2, bs = 8 * (rr & 3);
-  uint32_t slot4[kP];
-  static_for<kP>([&](auto kc) {
-    constexpr int k = decltype(kc)::value;
-    slot4[k] = 4u * (uint32_t)(((k + lane) % kP) + kP * (lane / kP));
+  uint32_t slot4[kP / 4];  // byte (k & 3) of slot4[k >> 2] = 4 * slot(k)
+  static_for<kP / 4>([&](auto mc) {
+    constexpr int m = decltype(mc)::value;
+    uint32_t w = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      w |= (4u * (uint32_t)(((4 * m + j + lane) % kP) + kP * (lane / kP))) << (8 * j);
+    slot4[m] = w;
   });
 
   float m_run = -INFINITY, l_run = 0.f, c_run = 0.f, acc = 0.f;
@@ -671,41 +727,55 @@ __global__ void __launch_bounds__(256, 2)
     for (int e = t; e < 256 * 32; e += NT) {
       const int v = e >> 5, slot = e & 31, pos = slot % kP;
       reinterpret_cast<float*>(tabb)[v * 64 + slot] =
-          nib[pos * 16 + (v & 15)] + nib[kP * 16 + pos * 16 + (v >> 4)];
+          nib[(v & 15) * kP + pos] + nib[kP * 16 + (v >> 4) * kP + pos];
     }
     __syncthreads();
 
-    // ---------------- phase 1: logits (log2 units) of the segment
-    float mloc = -INFINITY;
+    // ---------------- phase 1: logits (log2 units) of the segment, online
+    // per-thread sums of p and of the V weights relative to the running max mt
+    float mt = -INFINITY;
+    float2 sums = make_float2(0.f, 0.f);
     {
-      RowK<D> a[2][B];
-      auto load_batch = [&](RowK<D>(&dst)[B], int bi) {
+      RowKV<D> a[2][B];
+      auto load_batch = [&](RowKV<D>(&dst)[B], int bi) {
 #pragma unroll
         for (int u = 0; u < B; ++u) {
           const int ii = t + (bi * B + u) * NT;
           load_k_row<D>(P, row0 + (ii < n ? ii : 0), wr, bs, dst[u]);
         }
       };
-      auto score_batch = [&](const RowK<D>(&src)[B], int bi) {
+      auto score_batch = [&](const RowKV<D>(&src)[B], int bi) {
+        float l2[B];
+        float mb = mt;
 #pragma unroll
         for (int u = 0; u < B; ++u) {
           float2 m = make_float2(0.f, 0.f);
           static_for<kP>([&](auto kc) {
             constexpr int k = decltype(kc)::value;
             const float x1 = *reinterpret_cast<const float*>(
-                tabb + tab_addr<k & 3>(src[u].c[k >> 2], slot4[k]));
+                tabb + tab_addr<k & 3>(src[u].c[k >> 2], slot4[k >> 2]));
             const float x2 = *reinterpret_cast<const float*>(
-                tabb + tab_addr<k & 3>(src[u].r[k >> 2], slot4[k]));
+                tabb + tab_addr<k & 3>(src[u].r[k >> 2], slot4[k >> 2]));
             m = __fadd2_rn(m, make_float2(x1, x2));
           });
           const float score = src[u].n * (P.c0 * Q + dc * m.x) +
                               inv_sqrt_d * (2.f * m.y - Q) * src[u].rn;
           const int ii = t + (bi * B + u) * NT;
-          if (ii < n) {
-            const float l2 = score * lscale;
-            lg[ii] = l2;
-            mloc = fmaxf(mloc, l2);
+          l2[u] = ii < n ? score * lscale : -INFINITY;
+          if (ii < n) lg[ii] = l2[u];
+          mb = fmaxf(mb, l2[u]);
+        }
+        if (mb > -INFINITY) {
+          const float sc = exp2f(mt - mb);  // 0 while mt is -inf
+          sums.x *= sc;
+          sums.y *= sc;
+#pragma unroll
+          for (int u = 0; u < B; ++u) {
+            const float p = exp2f(l2[u] - mb);  // 0 for rows past n
+            sums.x += p;
+            sums.y += p * (src[u].vn * wa + src[u].vrn * wb);
           }
+          mt = mb;
         }
       };
       load_batch(a[0], 0);
@@ -718,7 +788,7 @@ __global__ void __launch_bounds__(256, 2)
         }
       }
     }
-    const float m_seg = block_max<NT>(mloc, red);  // also: phase-1 table reads done
+    const float m_seg = block_max<NT>(mt, red);  // also: phase-1 table reads done
     const float m_new = fmaxf(m_run, m_seg);
     const float alpha = exp2f(m_run - m_new);  // 0 on the first segment
     m_run = m_new;
@@ -728,17 +798,10 @@ __global__ void __launch_bounds__(256, 2)
       int4* z = reinterpret_cast<int4*>(tabb);
       for (int e = t; e < C::kTabWords / 4; e += NT) z[e] = make_int4(0, 0, 0, 0);
     }
-
-    // ---------------- phase 2a: sum of p and of the V weights
-    float2 sums = make_float2(0.f, 0.f);
-#pragma unroll 4
-    for (int ii = t; ii < n; ii += NT) {
-      const float p = exp2f(lg[ii] - m_new);
-      const int64_t row = row0 + ii;
-      const float w = p * (__ldg(P.v_norms + row) * inv_sqrt_d * dc +
-                           2.f * __ldg(P.v_rnorms + row) * qjl);
-      sums.x += p;
-      sums.y += w;
+    {
+      const float r = mt > -INFINITY ? exp2f(mt - m_new) : 0.f;
+      sums.x *= r;
+      sums.y *= r;
     }
     const float2 tot = block_sum2<NT>(sums, red);  // barriers also order the zeroing
     const float l_c = tot.x;
@@ -747,7 +810,7 @@ __global__ void __launch_bounds__(256, 2)
 
     // ---------------- phase 2b: scatter V bytes with fixed-point weights
     float csum = 0.f;  // constant term in quanta
-    const float k1 = inv_sqrt_d * dc * scale_inv, k2 = 2.f * qjl * scale_inv;
+    const float k1 = wa * scale_inv, k2 = wb * scale_inv;
     {
       RowK<D> a[2][B];
       auto load_batch = [&](RowK<D>(&dst)[B], int bi) {
@@ -771,10 +834,10 @@ __global__ void __launch_bounds__(256, 2)
           csum += (float)f1 * c0dc - 0.5f * (float)f2;
           static_for<kP>([&](auto kc) {
             constexpr int k = decltype(kc)::value;
-            atomicAdd(reinterpret_cast<int*>(tabb + tab_addr<k & 3>(src[u].c[k >> 2], slot4[k])),
+            atomicAdd(reinterpret_cast<int*>(tabb + tab_addr<k & 3>(src[u].c[k >> 2], slot4[k >> 2])),
                       f1);
             atomicAdd(reinterpret_cast<int*>(tabb + 128 +
-                                             tab_addr<k & 3>(src[u].r[k >> 2], slot4[k])),
+                                             tab_addr<k & 3>(src[u].r[k >> 2], slot4[k >> 2])),
                       f2);
           });
         }
