@@ -168,6 +168,28 @@ int kh_score_packed_compat(const void* q, int64_t n_heads, int head_dim,
                            void* stream);
 
 /*
+ * kh_decode_partial_gqa -- kh_decode_partial for grouped-query attention:
+ * n_q query heads share each cache group (H_q = n_q * H_kv).  q is
+ * [n_groups][n_q][D]; partial records (and the combine step's n_groups
+ * argument and output) cover n_groups * n_q query rows, query row
+ * g * n_q + j reading cache group g.  The cache is not expanded: the n_q
+ * CTAs of a group read the same rows (from L2 after the first).  No
+ * counterpart in the reference, which expands K and V to the query heads
+ * before scoring (KudaHitamQuant_full-reasoning.py:389-403).
+ * kh_decode_partial is this call with n_q = 1.
+ */
+int kh_decode_partial_gqa(const float* q, int64_t n_groups, int n_q, int head_dim,
+                          const uint32_t* k_code, const uint32_t* k_res,
+                          const float* k_norms, const float* k_rnorms,
+                          const uint32_t* v_code, const uint32_t* v_res,
+                          const float* v_norms, const float* v_rnorms,
+                          int64_t seq_len, int64_t seq_begin, int64_t seq_end,
+                          const float* d_k_host, const float* d_v_host,
+                          const float* centroids_host, int n_centroids,
+                          float sm_scale, int n_splits, float* partials,
+                          int64_t part_stride, int64_t part_offset, void* stream);
+
+/*
  * Decode attention over a compressed K/V cache (split-K / flash-decoding).
  * Not present in the reference, which stops at the scores
  * (KudaHitamQuant_full.py:373-386); softmax(score * sm_scale) . V_hat with

@@ -317,19 +317,19 @@ int64_t kh_decode_workspace_bytes(int64_t n_groups, int n_splits,
   return n_groups * (int64_t)n_splits * (head_dim + 2) * (int64_t)sizeof(float);
 }
 
-int kh_decode_partial(const float* q, int64_t n_groups, int head_dim,
-                      const uint32_t* k_code, const uint32_t* k_res,
-                      const float* k_norms, const float* k_rnorms,
-                      const uint32_t* v_code, const uint32_t* v_res,
-                      const float* v_norms, const float* v_rnorms,
-                      int64_t seq_len, int64_t seq_begin, int64_t seq_end,
-                      const float* d_k_host, const float* d_v_host,
-                      const float* centroids_host, int n_centroids,
-                      float sm_scale, int n_splits, float* partials,
-                      int64_t part_stride, int64_t part_offset, void* stream) {
+int kh_decode_partial_gqa(const float* q, int64_t n_groups, int n_q, int head_dim,
+                          const uint32_t* k_code, const uint32_t* k_res,
+                          const float* k_norms, const float* k_rnorms,
+                          const uint32_t* v_code, const uint32_t* v_res,
+                          const float* v_norms, const float* v_rnorms,
+                          int64_t seq_len, int64_t seq_begin, int64_t seq_end,
+                          const float* d_k_host, const float* d_v_host,
+                          const float* centroids_host, int n_centroids,
+                          float sm_scale, int n_splits, float* partials,
+                          int64_t part_stride, int64_t part_offset, void* stream) {
   (void)d_v_host;  // V's diagonal is applied by the combine step
-  if (n_groups < 0 || n_groups >= 65536 || !valid_head_dim(head_dim))
-    return KH_EINVAL;
+  if (n_groups < 0 || n_q < 1 || !valid_head_dim(head_dim)) return KH_EINVAL;
+  if (n_groups * (int64_t)n_q >= 65536) return KH_EINVAL;  // grid.y limit
   if (n_splits < 1 || n_splits > 65535) return KH_EINVAL;
   if (seq_len < 0 || seq_begin < 0 || seq_end < seq_begin || seq_end > seq_len)
     return KH_EINVAL;
@@ -358,10 +358,27 @@ int kh_decode_partial(const float* q, int64_t n_groups, int head_dim,
   r.seq_len = seq_len; r.seq_begin = seq_begin; r.seq_end = seq_end;
   r.sm_scale = sm_scale;
   r.n_splits = n_splits;
+  r.n_q = n_q;
   r.partials = partials;
   r.part_stride = part_stride;
   r.part_offset = part_offset;
   return launch_decode_partial(r, static_cast<cudaStream_t>(stream));
+}
+
+int kh_decode_partial(const float* q, int64_t n_groups, int head_dim,
+                      const uint32_t* k_code, const uint32_t* k_res,
+                      const float* k_norms, const float* k_rnorms,
+                      const uint32_t* v_code, const uint32_t* v_res,
+                      const float* v_norms, const float* v_rnorms,
+                      int64_t seq_len, int64_t seq_begin, int64_t seq_end,
+                      const float* d_k_host, const float* d_v_host,
+                      const float* centroids_host, int n_centroids,
+                      float sm_scale, int n_splits, float* partials,
+                      int64_t part_stride, int64_t part_offset, void* stream) {
+  return kh_decode_partial_gqa(q, n_groups, 1, head_dim, k_code, k_res, k_norms, k_rnorms,
+                               v_code, v_res, v_norms, v_rnorms, seq_len, seq_begin, seq_end,
+                               d_k_host, d_v_host, centroids_host, n_centroids, sm_scale,
+                               n_splits, partials, part_stride, part_offset, stream);
 }
 
 int kh_decode_combine(const float* partials, int64_t n_groups, int n_parts,

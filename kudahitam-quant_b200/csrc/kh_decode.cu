@@ -33,6 +33,7 @@ struct alignas(16) DecodeParams {
   int64_t seq_len, seq_begin, seq_end, part_stride, part_offset;
   float sm_scale;
   int n_splits;
+  int n_q;  // queries per cache group (grouped-query attention); blockIdx.y = query row
   float c0, c1;
   float dk[256];
 };
@@ -64,7 +65,8 @@ __global__ void __launch_bounds__(D)
   __shared__ float red[32];
 
   const int t = threadIdx.x;
-  const int64_t g = blockIdx.y;
+  const int64_t g = blockIdx.y;      // query row (q, partial records)
+  const int64_t gk = g / P.n_q;      // cache group it reads
   const int split = blockIdx.x;
   const int64_t len = P.seq_end - P.seq_begin;
   const int64_t s0 = P.seq_begin + len * split / P.n_splits;
@@ -95,7 +97,7 @@ __global__ void __launch_bounds__(D)
     float logit = -INFINITY;
     float va = 0.f, vb = 0.f;
     if (valid) {
-      const int64_t row = g * P.seq_len + s;
+      const int64_t row = gk * P.seq_len + s;
       float m1 = 0.f, m2 = 0.f;
 #pragma unroll
       for (int w = 0; w < W; ++w) {
@@ -303,7 +305,8 @@ __global__ void __launch_bounds__(256)
 
   const int t = threadIdx.x;
   const int lane = t & 31;
-  const int64_t g = blockIdx.y;
+  const int64_t g = blockIdx.y;      // query row (q, partial records)
+  const int64_t gk = g / P.n_q;      // cache group it reads
   const int split = blockIdx.x;
   const int64_t len = P.seq_end - P.seq_begin;
   const int64_t s0 = P.seq_begin + len * split / P.n_splits;
@@ -363,7 +366,7 @@ __global__ void __launch_bounds__(256)
   constexpr int R = C::kRPT;
   for (int64_t c0 = s0; c0 < s1; c0 += C::kChunk) {
     const int n = (int)min((int64_t)C::kChunk, s1 - c0);
-    const int64_t row0 = g * P.seq_len + c0;
+    const int64_t row0 = gk * P.seq_len + c0;
     // this thread's rows of the chunk: t + r * NT, r < R
     float lg[R];
     // ---------------- pass 1: scores -> logits (two rows in flight)
@@ -662,7 +665,8 @@ __global__ void __launch_bounds__(256, 2)
 
   const int t = threadIdx.x;
   const int lane = t & 31;
-  const int64_t g = blockIdx.y;
+  const int64_t g = blockIdx.y;      // query row (q, partial records)
+  const int64_t gk = g / P.n_q;      // cache group it reads
   const int split = blockIdx.x;
   const int64_t len = P.seq_end - P.seq_begin;
   const int64_t s0 = P.seq_begin + len * split / P.n_splits;
@@ -719,7 +723,7 @@ __global__ void __launch_bounds__(256, 2)
 
   for (int64_t c0 = s0; c0 < s1; c0 += C::kSeg) {
     const int n = (int)min((int64_t)C::kSeg, s1 - c0);
-    const int64_t row0 = g * P.seq_len + c0;
+    const int64_t row0 = gk * P.seq_len + c0;
     const int nb = (n + NT * B - 1) / (NT * B);  // batches of B rows per thread
 
     // K table into entries 0..31 of every row: T[v][slot] = sum of q~ over
@@ -921,10 +925,11 @@ kh_status launch_decode_partial(const DecodeRequest& r, cudaStream_t stream) {
   P.part_stride = r.part_stride; P.part_offset = r.part_offset;
   P.sm_scale = r.sm_scale;
   P.n_splits = r.n_splits;
+  P.n_q = r.n_q;
   P.c0 = r.cb.c[0];
   P.c1 = r.cb.c[1];
   for (int i = 0; i < r.D; ++i) P.dk[i] = r.dk[i];
-  const dim3 grid((unsigned)r.n_splits, (unsigned)r.n_groups);
+  const dim3 grid((unsigned)r.n_splits, (unsigned)(r.n_groups * r.n_q));
   const char* env = getenv("KUDAHITAM_DECODE_PATH");
   const int path = (env && strcmp(env, "v1") == 0) ? 1 : (env && strcmp(env, "v2") == 0) ? 2 : 3;
   if (path == 1) {

@@ -87,6 +87,7 @@ struct DecodeRequest {
   Codebook cb;
   float sm_scale;
   int n_splits;
+  int n_q = 1;  // queries per cache group; q and partials have n_groups * n_q rows
   float* partials;
   int64_t part_stride, part_offset;
 };

@@ -42,6 +42,9 @@ SIGNATURES = {
     "kh_decode_partial": (_c_i, [_vp, _c_i64, _c_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                  _vp, _c_i64, _c_i64, _c_i64, _vp, _vp, _vp, _c_i, _c_f,
                                  _c_i, _vp, _c_i64, _c_i64, _vp]),
+    "kh_decode_partial_gqa": (_c_i, [_vp, _c_i64, _c_i, _c_i, _vp, _vp, _vp, _vp, _vp, _vp,
+                                     _vp, _vp, _c_i64, _c_i64, _c_i64, _vp, _vp, _vp, _c_i,
+                                     _c_f, _c_i, _vp, _c_i64, _c_i64, _vp]),
     "kh_decode_combine": (_c_i, [_vp, _c_i64, _c_i, _c_i, _vp, _vp, _vp]),
     "kh_decode_attn": (_c_i, [_vp, _c_i64, _c_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                               _c_i64, _vp, _vp, _vp, _c_i, _c_f, _c_i, _vp, _c_i64, _vp,

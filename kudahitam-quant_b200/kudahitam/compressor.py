@@ -165,15 +165,20 @@ class KudahitamCompressorV2:
                          v_compressor: Optional["KudahitamCompressorV2"] = None,
                          sm_scale: Optional[float] = None,
                          n_splits: Optional[int] = None) -> torch.Tensor:
-        """softmax(score / sqrt(D)) . V_hat for queries [B, H, D] (one decode
-        token) against compressed K and V caches [B, H, S, D].  V may use its
-        own compressor (its own d); both must use bits=1 with the residual
-        plane.  Returns float32 [B, H, D]."""
+        """softmax(score / sqrt(D)) . V_hat for queries [B, H_q, D] or
+        [B, H_q, 1, D] (one decode token) against compressed K and V caches
+        [B, H_kv, S, D], H_q a multiple of H_kv (grouped-query heads share
+        their KV head without expanding the cache).  V may use its own
+        compressor (its own d); both must use bits=1 with the residual plane.
+        Returns float32 [B, H_q, D]."""
         vc = v_compressor or self
         kp, vp = k_compressed.packed, v_compressed.packed
-        B, H = queries.shape[0], queries.shape[1]
-        q = queries.reshape(B * H, self.head_dim)
+        B, Hq = queries.shape[0], queries.shape[1]
+        Bk, Hk = kp.shape[0], kp.shape[1]
+        if Bk != B or Hq % Hk:
+            raise ValueError(f"{Hq} query heads do not map onto {Hk} KV heads (batch {B}/{Bk})")
+        q = queries.reshape(B * Hk, Hq // Hk, self.head_dim)
         out = ops.decode_attention(q, kp, vp, self._d_host, vc._d_host, self._c_host,
                                    sm_scale=sm_scale or 1.0 / math.sqrt(self.head_dim),
                                    n_splits=n_splits)
-        return out.view(B, H, self.head_dim)
+        return out.view(B, Hq, self.head_dim)

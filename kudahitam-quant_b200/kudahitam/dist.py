@@ -55,25 +55,26 @@ def decode_attention_seq_sharded(q: torch.Tensor, k_local: ops.PackedKV,
                                  n_splits: Optional[int] = None, group=None,
                                  partials: Optional[torch.Tensor] = None) -> torch.Tensor:
     """Decode attention where each rank holds S_local cached rows per group
-    (k_local / v_local: G * S_local rows).  Returns float32 [G, D] on every
-    rank."""
+    (k_local / v_local: G * S_local rows).  q is [G, D] or [G, n_q, D]
+    (grouped-query heads).  Returns float32 with q's shape on every rank."""
     world, rank = _world(group)
-    G, D = q.shape
+    G, D = q.shape[0], q.shape[-1]
+    R = q.numel() // D  # query rows: G * n_q
     S_loc = k_local.n_rows // max(G, 1)
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(D)
     if n_splits is None:
-        n_splits = ops.default_splits(G, S_loc, q.device)
+        n_splits = ops.default_splits(R, S_loc, q.device)
     parts = world * n_splits
-    if partials is None or partials.numel() < G * parts * (D + 2):
-        partials = torch.empty(G * parts * (D + 2), dtype=torch.float32, device=q.device)
-    buf = partials[: G * parts * (D + 2)].view(G, parts, D + 2)
+    if partials is None or partials.numel() < R * parts * (D + 2):
+        partials = torch.empty(R * parts * (D + 2), dtype=torch.float32, device=q.device)
+    buf = partials[: R * parts * (D + 2)].view(R, parts, D + 2)
     buf.zero_()
     ops.decode_partial(q, k_local, v_local, dk, dv, centroids, sm_scale, n_splits, buf,
                        part_stride=parts, part_offset=rank * n_splits, seq_len=S_loc)
     if world > 1:
         dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=group)
-    out = torch.empty((G, D), dtype=torch.float32, device=q.device)
+    out = torch.empty(q.shape, dtype=torch.float32, device=q.device)
     return ops.decode_combine(buf, parts, dv, out)
 
 

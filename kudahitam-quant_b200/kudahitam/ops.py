@@ -261,51 +261,72 @@ def decode_partial(q: torch.Tensor, k: PackedKV, v: PackedKV, dk, dv, centroids,
                    sm_scale: float, n_splits: int, partials: torch.Tensor,
                    part_stride: int, part_offset: int, seq_len: int,
                    seq_begin: int = 0, seq_end: Optional[int] = None) -> torch.Tensor:
+    """Split-K partial records of decode attention.  q is [G, D] (one query
+    per cache group) or [G, n_q, D] (grouped-query attention: n_q query heads
+    share each cache group; records cover G * n_q query rows).  Rows of cache
+    group g are rows [g * seq_len + seq_begin, g * seq_len + seq_end)."""
     dev = _require_cuda(q, k.norms, v.norms, partials)
-    G, D = q.shape
+    if q.dim() == 2:
+        G, D = q.shape
+        n_q = 1
+    else:
+        G, n_q, D = q.shape
     seq_end = seq_len if seq_end is None else seq_end
     if not (k.residual and v.residual):
         raise ValueError("decode attention needs caches compressed with the residual plane")
     qf = q.to(torch.float32).contiguous()
     dkh, dvh, ch = _host_f32(dk), _host_f32(dv), _host_f32(centroids)
     with torch.cuda.device(dev):
-        _lib.call("kh_decode_partial", _vp(qf), G, D, _vp(k.code), _vp(k.res), _vp(k.norms),
-                  _vp(k.rnorms), _vp(v.code), _vp(v.res), _vp(v.norms), _vp(v.rnorms),
-                  seq_len, seq_begin, seq_end, _vp(dkh), _vp(dvh), _vp(ch), ch.numel(),
-                  float(sm_scale), n_splits, _vp(partials), part_stride, part_offset,
-                  _stream(dev))
+        _lib.call("kh_decode_partial_gqa", _vp(qf), G, n_q, D, _vp(k.code), _vp(k.res),
+                  _vp(k.norms), _vp(k.rnorms), _vp(v.code), _vp(v.res), _vp(v.norms),
+                  _vp(v.rnorms), seq_len, seq_begin, seq_end, _vp(dkh), _vp(dvh), _vp(ch),
+                  ch.numel(), float(sm_scale), n_splits, _vp(partials), part_stride,
+                  part_offset, _stream(dev))
     return partials
 
 
 def decode_combine(partials: torch.Tensor, n_parts: int, dv, out: torch.Tensor) -> torch.Tensor:
+    """Merge split-K records into out ([R, D] or [G, n_q, D]: one row per
+    query row of the records)."""
     dev = _require_cuda(partials, out)
-    G, D = out.shape
+    D = out.shape[-1]
+    R = out.numel() // D if D else 0
     dvh = _host_f32(dv)
     with torch.cuda.device(dev):
-        _lib.call("kh_decode_combine", _vp(partials), G, n_parts, D, _vp(dvh), _vp(out),
+        _lib.call("kh_decode_combine", _vp(partials), R, n_parts, D, _vp(dvh), _vp(out),
                   _stream(dev))
     return out
 
 
 def decode_attention(q: torch.Tensor, k: PackedKV, v: PackedKV, dk, dv, centroids,
                      sm_scale: Optional[float] = None, n_splits: Optional[int] = None,
-                     workspace: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """softmax(score * sm_scale) . V_hat for one query per group.
-    q [G, D]; k / v hold G * S rows.  Returns float32 [G, D]."""
+                     workspace: Optional[torch.Tensor] = None,
+                     seq_len: Optional[int] = None, length: Optional[int] = None
+                     ) -> torch.Tensor:
+    """softmax(score * sm_scale) . V_hat.  q is [G, D] or [G, n_q, D]
+    (n_q query heads per cache group, without expanding the cache).  The
+    cache holds G groups of seq_len rows (default: all rows split evenly);
+    the first `length` rows of each group (default seq_len) are attended.
+    Returns float32 with q's shape."""
     dev = _require_cuda(q, k.norms, v.norms)
-    G, D = q.shape
-    S = k.n_rows // max(G, 1)
+    G, D = q.shape[0], q.shape[-1]
+    n_q = 1 if q.dim() == 2 else q.shape[1]
+    S = k.n_rows // max(G, 1) if seq_len is None else int(seq_len)
     if G * S != k.n_rows or v.n_rows != k.n_rows:
-        raise ValueError("K/V caches do not hold G * S rows")
+        raise ValueError("K/V caches do not hold G * seq_len rows")
+    L = S if length is None else int(length)
+    if not 0 <= L <= S:
+        raise ValueError("length must be within [0, seq_len]")
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(D)
     if n_splits is None:
-        n_splits = default_splits(G, S, dev)
-    need = decode_workspace_bytes(G, n_splits, D)
+        n_splits = default_splits(G * n_q, L, dev)
+    need = decode_workspace_bytes(G * n_q, n_splits, D)
     if workspace is None or workspace.numel() * workspace.element_size() < need:
         workspace = torch.empty(max(need // 4, 1), dtype=torch.float32, device=dev)
-    out = torch.empty((G, D), dtype=torch.float32, device=dev)
-    decode_partial(q, k, v, dk, dv, centroids, sm_scale, n_splits, workspace, n_splits, 0, S)
+    out = torch.empty(q.shape, dtype=torch.float32, device=dev)
+    decode_partial(q, k, v, dk, dv, centroids, sm_scale, n_splits, workspace, n_splits, 0, S,
+                   0, L)
     return decode_combine(workspace, n_splits, dv, out)
 
 

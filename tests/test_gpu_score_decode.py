@@ -183,13 +183,59 @@ def test_decode_long_splits_and_peaked_softmax(sm_mult, decode_path):
 def test_decode_split_invariance_and_empty_splits(decode_path):
     D, G, S = 128, 3, 5
     dk, dv, c, k, v = _caches(G, S, D, seed=1)
-    q = torch.randn(G, D, device="cuda")
+    for seed in range(4):
+        q = torch.randn(G, D, generator=torch.Generator().manual_seed(seed)).cuda()
+        pk = ops.compress(k.cuda(), dk, c)
+        pv = ops.compress(v.cuda(), dv, c)
+        base = ops.decode_attention(q, pk, pv, dk, dv, c, n_splits=1).cpu().numpy()
+        for n in (2, 5, 8, 64):  # 64 splits over 5 rows: most splits are empty
+            got = ops.decode_attention(q, pk, pv, dk, dv, c, n_splits=n).cpu().numpy()
+            # split-K reassociation only: normwise per group (elementwise
+            # checks are meaningless for outputs near zero after the
+            # D-term transform)
+            for gi in range(G):
+                assert K.normwise(got[gi], base[gi]) < 2e-6, (seed, n, gi)
+
+
+def test_decode_grouped_query_heads_share_the_cache(decode_path):
+    """q [G, n_q, D]: every query row reads its group's cache without any
+    expansion, and equals the one-query decode of the same row bit for bit."""
+    D, G, S, n_q = 128, 3, 2500, 4
+    dk, dv, c, k, v = _caches(G, S, D, seed=7)
     pk = ops.compress(k.cuda(), dk, c)
     pv = ops.compress(v.cuda(), dv, c)
-    base = ops.decode_attention(q, pk, pv, dk, dv, c, n_splits=1)
-    for n in (2, 5, 8, 64):  # 64 splits over 5 rows: most splits are empty
-        got = ops.decode_attention(q, pk, pv, dk, dv, c, n_splits=n)
-        assert torch.allclose(got, base, rtol=1e-4, atol=1e-6), n  # split-K reassociation
+    q = torch.randn(G, n_q, D, generator=torch.Generator().manual_seed(5)).cuda()
+    got = ops.decode_attention(q, pk, pv, dk, dv, c, n_splits=3)
+    assert got.shape == (G, n_q, D)
+    for j in range(n_q):
+        one = ops.decode_attention(q[:, j].contiguous(), pk, pv, dk, dv, c, n_splits=3)
+        assert torch.equal(got[:, j], one), j
+    # the compressor API maps H_q = 2 H_kv query heads onto the KV heads
+    ck = KudahitamCompressorV2(D, 1, seed=10)
+    cv = KudahitamCompressorV2(D, 1, seed=11)
+    kk = torch.randn(2, 2, 700, D, device="cuda", dtype=torch.bfloat16)
+    vv = torch.randn(2, 2, 700, D, device="cuda", dtype=torch.bfloat16)
+    qq = torch.randn(2, 4, D, device="cuda", dtype=torch.bfloat16)
+    a = ck.decode_attention(qq, ck.compress(kk), cv.compress(vv), v_compressor=cv)
+    b = ck.decode_attention(qq[:, 0::2].contiguous(), ck.compress(kk), cv.compress(vv),
+                            v_compressor=cv)  # heads 0, 2 -> KV heads 0, 1
+    assert a.shape == (2, 4, D) and torch.equal(a[:, 0::2], b)
+
+
+def test_decode_capacity_stride_and_length(decode_path):
+    """Groups laid out with a capacity stride larger than the filled length
+    (an appendable cache): only the first `length` rows are attended."""
+    D, G, S, cap = 128, 2, 900, 1500
+    dk, dv, c, k, v = _caches(G, cap, D, seed=9)
+    pk = ops.compress(k.cuda(), dk, c)
+    pv = ops.compress(v.cuda(), dv, c)
+    kk = k.view(G, cap, D)[:, :S].contiguous()
+    vv = v.view(G, cap, D)[:, :S].contiguous()
+    ref = ops.decode_attention(torch.ones(G, D).cuda(), ops.compress(kk.cuda(), dk, c),
+                               ops.compress(vv.cuda(), dv, c), dk, dv, c, n_splits=2)
+    got = ops.decode_attention(torch.ones(G, D).cuda(), pk, pv, dk, dv, c, n_splits=2,
+                               seq_len=cap, length=S)
+    assert torch.equal(got, ref)
 
 
 def test_decode_seq_sharded_emulated_on_one_gpu(decode_path):
