@@ -44,8 +44,15 @@ DEC_BYTES_PER_ROW = 2 * (2 * DEC_D // 8 + 8)  # K and V: 2 planes + 2 norms each
 FALLBACK_HBM_GBS = 6650.0
 
 # dram__bytes_read.sum + dram__bytes_write.sum per compressed row, from the ncu
-# capture summarised in profiles/ (None until a capture exists).
-NCU_TRAFFIC_BYTES_PER_ROW = None
+# capture in profiles/compress_tc_fp16_d256_2bit.md (524,288 rows of the same
+# row format): 268.52 MB read + 8.86 MB written.  Reads equal the algorithmic
+# bytes; most of the packed output is still in L2 when the kernel ends, so
+# the DRAM write count is below the 72 B/row written.  Traffic grows in
+# proportion to the rows, so it is scaled to a full launch.
+NCU_TRAFFIC_BYTES_PER_ROW = (268.516096e6 + 8.860672e6) / 524288
+# Same for the decode step (profiles/decode_v3_q32x16_s40000.md): bytes per
+# cached row of K and V, on the bench's decode workload itself.
+NCU_DECODE_TRAFFIC_BYTES_PER_ROW = (1.755635e9 + 5.170176e6) / (512 * 40000)
 
 
 def peaks() -> tuple[float, str]:
@@ -251,6 +258,11 @@ def run_engine(args, world, rank, local):
         if rank == 0:
             print(json.dumps({"decode": dec}), flush=True)
         return
+    if args.only == "layers":
+        lay = layers_bench(dev, args)
+        if rank == 0:
+            print(json.dumps({"layers_28": lay}), flush=True)
+        return
     k, v = synth_kv(2 + 1000 * rank, dev)
     d = rademacher(D, 1)
     c = lloyd_max(1, D)
@@ -345,6 +357,8 @@ def run_engine(args, world, rank, local):
     del hk, hv, gk, gv
 
     dec = decode_bench(dev, args, world, rank) if args.only == "all" else None
+    lay = (layers_bench(dev, args)
+           if args.only == "all" and not args.no_layers and world == 1 else None)
 
     line = {"metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
@@ -352,12 +366,59 @@ def run_engine(args, world, rank, local):
             "dtype": "f32", "data": "synthetic", "config": workload_config(world),
             "hbm_gbs": achieved, "hbm_frac_of_measured": achieved / peak,
             "hbm_frac_of_spec_8000": achieved / 8000.0,
-            "roofline": roof, "e2e": e2e, "decode": dec,
+            "roofline": roof, "e2e": e2e, "decode": dec, "layers_28": lay,
             "gpu_launches": args.steps, "clocks": clk.summary()}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_run()
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def layers_bench(dev, args) -> dict:
+    """28-layer batched compression: per layer K and V bf16 [32, 16, 8192, 128]
+    (N(0, 0.5^2) times a per-layer scale drawn from U[0.5, 2]), 56 tensors of
+    4.19 M rows (60.1 GB resident) compressed in one batched launch per step,
+    in 1-bit mode (code + norm, 20 B/row) and 2-bit mode (40 B/row)."""
+    from kudahitam import ops
+    from kudahitam.codebook import lloyd_max, rademacher
+    L, Bc, Hc, Sc, Dc = 28, 32, 16, 8192, 128
+    if args.seq:  # profiling: shrink S
+        Sc = min(Sc, args.seq)
+    scales = torch.empty(L).uniform_(0.5, 2.0, generator=torch.Generator().manual_seed(3))
+    xs = []
+    for l in range(L):
+        g = torch.Generator(device=dev).manual_seed(3 + l)
+        for _ in range(2):
+            x = torch.empty(Bc, Hc, Sc, Dc, device=dev, dtype=torch.bfloat16)
+            for b in range(Bc):  # fp32 temporaries one batch entry at a time
+                x[b] = (torch.randn(Hc, Sc, Dc, device=dev, generator=g)
+                        * (0.5 * float(scales[l]))).to(torch.bfloat16)
+            xs.append(x)
+    d, c = rademacher(Dc, 1), lloyd_max(1, Dc)
+    rows = len(xs) * Bc * Hc * Sc
+    stream = torch.cuda.current_stream(dev)
+    peak, _ = peaks()
+    out = {"config": f"28 layers x (K, V) bf16 [32,16,{Sc},128], one batched launch per step",
+           "rows_per_step": rows, "input_gb": rows * Dc * 2 / 1e9}
+    for mode, residual in (("1bit", False), ("2bit", True)):
+        outs = [ops.empty_packed(x.shape, 1, residual, dev) for x in xs]
+
+        def step():
+            ops.compress_many(xs, d, c, residual=residual, outs=outs)
+
+        for _ in range(2):
+            step()
+        torch.cuda.synchronize()
+        per = time_loop(step, 5, stream)
+        ms = statistics.median(per)
+        bpr = Dc * 2 + (2 * Dc // 8 + 8 if residual else Dc // 8 + 4)
+        gbs = rows * bpr / (ms / 1e3) / 1e9
+        out[mode] = {"ms_per_step": ms, "rows_per_s": rows / (ms / 1e3), "gbs": gbs,
+                     "frac_of_measured_hbm": gbs / peak, "bytes_per_row": bpr}
+        del outs
+    del xs
+    torch.cuda.empty_cache()
+    return out
 
 
 def decode_bench(dev, args, world: int = 1, rank: int = 0) -> dict:
@@ -413,7 +474,13 @@ def decode_bench(dev, args, world: int = 1, rank: int = 0) -> dict:
             "us_per_step": ms * 1e3, "us_per_token": ms * 1e3 / DEC_B,
             "n_splits": n_splits, "scaling": "strong" if world > 1 else None,
             "gbs": bytes_step / (ms / 1e3) / 1e9,
-            "frac_of_measured_hbm_per_gpu": bytes_step / world / (ms / 1e3) / 1e9 / peak}
+            "frac_of_measured_hbm_per_gpu": bytes_step / world / (ms / 1e3) / 1e9 / peak,
+            "roofline": {"bound": "hbm", "achieved": bytes_step / world / (ms / 1e3) / 1e9,
+                         "peak": peak, "unit": "GB/s",
+                         "frac": bytes_step / world / (ms / 1e3) / 1e9 / peak,
+                         "algorithmic_bytes": bytes_step / world,
+                         "traffic": NCU_DECODE_TRAFFIC_BYTES_PER_ROW * G * DEC_S / world,
+                         "kernel": "decode_v3_kernel<128> + decode_combine_kernel<128>"}}
 
 
 def main():
@@ -423,7 +490,9 @@ def main():
     ap.add_argument("--warmup", type=int, default=5)
     ap.add_argument("--impl", choices=["engine", "reference"], default="engine")
     ap.add_argument("--no-cpu-baseline", action="store_true")
-    ap.add_argument("--only", choices=["all", "compress", "decode"], default="all",
+    ap.add_argument("--no-layers", action="store_true",
+                    help="skip the 28-layer batched compression line (60 GB resident)")
+    ap.add_argument("--only", choices=["all", "compress", "decode", "layers"], default="all",
                     help="run one part (small cases for profiler captures)")
     ap.add_argument("--seq", type=int, default=None,
                     help="override S of the compression workload (profiling only)")

@@ -95,14 +95,16 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   const int64_t nw = (int64_t)gridDim.x * WARPS;
   const uint64_t policy = l2_policy_evict_first();
 
-  auto seg_of = [&](int64_t t) {
-    int sg = 0;
+  // Segment of tile t, resumed from a cursor: the issuer and the consumer
+  // each visit their tiles in increasing order (amortised O(1) per tile).
+  auto seg_of = [&](int64_t t, int& sg) {
 #pragma unroll 1
     while (sg + 1 < P.n_seg && t >= P.tile_begin[sg + 1]) ++sg;
     return sg;
   };
+  int sg_issue = 0, sg_use = 0;
   auto issue = [&](int64_t t, int s) {
-    const int sg = seg_of(t);
+    const int sg = seg_of(t, sg_issue);
     const int32_t row0 = (int32_t)((t - P.tile_begin[sg]) * C::kRows);
     mbar_arrive_expect_tx(&bars[s], C::kTileBytes);
 #pragma unroll
@@ -112,7 +114,10 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
   };
 
   if (lane == 0) {
-    if (gw < total) prefetch_tmap(&P.tmap[seg_of(gw)]);
+    if (gw < total) {
+      int sg0 = 0;
+      prefetch_tmap(&P.tmap[seg_of(gw, sg0)]);
+    }
 #pragma unroll
     for (int s = 0; s < STAGES; ++s) {
       const int64_t t = gw + s * nw;
@@ -130,7 +135,7 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
     const uint32_t ph = (uint32_t)((k / STAGES) & 1);
     if (!mbar_wait(&bars[s], ph, P.err)) break;
 
-    const int sg = seg_of(t);
+    const int sg = seg_of(t, sg_use);
     const int64_t row = (t - P.tile_begin[sg]) * C::kRows + r;
     const uint32_t rowbase = wbuf + s * C::kTileBytes + r * 128;
 

@@ -127,7 +127,10 @@ struct TcCfg {
   static constexpr int kBarOff = kStages * kChunkBytes + kNB * kBMatBytes;
   // barriers, the tensor-memory slot, then (D=256) the partner exchange
   static constexpr int kXchOff = kBarOff + (2 * kStages + 4) * 8 + 16;
-  static constexpr int kSmem = 1024 + kXchOff + (D == 256 ? 4 * 128 * 4 : 0);
+  // D=256 exchange: sum of squares [tile parity][warpgroup][128 rows], then
+  // residual sums [warpgroup][128 rows]: 768 floats
+  static constexpr int kXchFloats = (D == 256) ? 6 * 128 : 0;
+  static constexpr int kSmem = 1024 + kXchOff + kXchFloats * 4;
   static_assert(kSmem <= 232448, "exceeds the 227 KB of shared memory a CTA can use");
 };
 
@@ -184,7 +187,7 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* tfull = empty + C::kStages;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
-  float* xch = reinterpret_cast<float*>(g + C::kXchOff);  // D=256: [2 WG][2][128]
+  float* xch = reinterpret_cast<float*>(g + C::kXchOff);  // D=256 partner exchange
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -230,8 +233,10 @@ __global__ void __launch_bounds__(320, 1)
   const uint32_t tmem = *tmem_slot;
 
   const int64_t total = P.tile_begin[P.n_seg];
-  auto seg_of = [&](int64_t t) {
-    int sg = 0;
+  // Segment of tile t.  Each role visits its tiles in increasing order, so
+  // the search resumes from the previous answer (amortised O(1) per tile
+  // instead of a scan of the segment table per tile).
+  auto seg_of = [&](int64_t t, int& sg) {
 #pragma unroll 1
     while (sg + 1 < P.n_seg && t >= P.tile_begin[sg + 1]) ++sg;
     return sg;
@@ -242,9 +247,10 @@ __global__ void __launch_bounds__(320, 1)
     if (lane == 0) {
       const uint64_t policy = l2_policy_evict_first();
       int c = 0;  // chunk counter
+      int sg_cur = 0;
       bool ok = true;
       for (int64_t t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        const int sg = seg_of(t);
+        const int sg = seg_of(t, sg_cur);
         const int32_t row0 = (int32_t)((t - P.tile_begin[sg]) * C::kM);
 #pragma unroll 1
         for (int h = 0; h < C::kNB; ++h, ++c) {
@@ -296,6 +302,7 @@ __global__ void __launch_bounds__(320, 1)
     const int q = warp & 3;          // tensor-memory lane quarter of this warp
     const int r = 32 * q + lane;     // row within the tile
     int i = 0;
+    int sg_cur = 0;
     for (int64_t t = blockIdx.x; t < total; t += gridDim.x, ++i) {
       if constexpr (D == 128) {
         if ((i & 1) != wg) continue;  // warpgroups alternate tiles
@@ -306,7 +313,7 @@ __global__ void __launch_bounds__(320, 1)
       const bool ok = __all_sync(0xffffffffu, mbar_wait(&tfull[b], jb, P.err));
       if (!ok) break;
       tc_fence_after();
-      const int sg = seg_of(t);
+      const int sg = seg_of(t, sg_cur);
       const int64_t row = (t - P.tile_begin[sg]) * C::kM + r;
       const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + b * C::kAccCols;
 
@@ -352,9 +359,13 @@ __global__ void __launch_bounds__(320, 1)
             u[gq][e] = lo.x; u[gq][e + 1] = lo.y;
             u[2 + gq][e] = hi.x; u[2 + gq][e + 1] = hi.y;
           }
-        xch[wg * 256 + r] = ss;
+        // slot by tile parity: the partner may still be reading the previous
+        // tile's slot when this warpgroup writes the next one (with no
+        // residual exchange there is one barrier per tile)
+        float* xs = xch + (i & 1) * 256;
+        xs[wg * 128 + r] = ss;
         named_bar_sync(1, 256);
-        ss = xch[r] + xch[256 + r];
+        ss = xs[r] + xs[128 + r];
       }
       // ss = 128 ||x||^2 for both head dims
       const float norm = ss > 0.f ? sqrtf(ss * (1.0f / 128.0f)) : 1e-8f;

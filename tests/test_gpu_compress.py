@@ -34,7 +34,9 @@ def check_against_oracle(x_cpu: torch.Tensor, p: ops.PackedKV, d, c, residual=Tr
     assert code.shape == (n, D)
     bad = (code != ref["idx"]) & m
     assert not bad.any(), f"{bad.sum()} decided index mismatches"
-    assert (code != ref["idx"]).mean() < 1e-4
+    # undecided elements (inside the 1e-6 band) may go either way; they are
+    # rare (|y| < 1e-6 has probability ~1e-5 per element)
+    assert (code != ref["idx"]).sum() <= max(2, 1e-4 * code.size)
     assert K.rel_err(p.norms.cpu().numpy(), ref["norms"]) < 1e-5
     if residual:
         rm = K.res_mask(y, ref["idx"].astype(np.int64), c)
