@@ -136,6 +136,21 @@ class KudahitamCompressorV2:
         packed = ops.compress(states, self._d_host, self._c_host, residual=self.residual)
         return CompressedKV(packed, self._d_host, self._c_host, self.is_domain_layer)
 
+    def compress_to_host(self, states, device=None, outs=None) -> list:
+        """Compress host-resident (pinned) tensors into host-resident packed
+        caches, streaming them through the GPU with the uploads, the kernel
+        and the downloads overlapped (``ops.compress_host``).  ``states`` is
+        one CPU tensor or a list; returns a list of CompressedKV whose packed
+        planes live in pinned host memory (``outs``: PackedKVs to fill
+        instead).  Synchronise the current CUDA stream before reading them."""
+        xs = list(states) if isinstance(states, (list, tuple)) else [states]
+        dev = device if device is not None else (
+            self.device if str(self.device).startswith("cuda") else None)
+        packed = ops.compress_host(xs, self._d_host, self._c_host, residual=self.residual,
+                                   device=dev, outs=outs)
+        return [CompressedKV(p, self._d_host, self._c_host, self.is_domain_layer)
+                for p in packed]
+
     @torch.no_grad()
     def asymmetric_attention_scores(self, queries: torch.Tensor, compressed) -> torch.Tensor:
         """queries [B, Hq, Lq, D] against a cache of shape [B, Hkv, S, D]

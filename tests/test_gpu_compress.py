@@ -251,3 +251,29 @@ def test_cuda_graph_capture():
 def test_no_device_errors_recorded():
     torch.cuda.synchronize()
     assert _lib.device_error() == 0
+
+
+@pytest.mark.parametrize("residual", [True, False])
+def test_host_streamed_compression_equals_device(residual):
+    """compress_host (uploads, kernels and downloads overlapped over chunks)
+    produces the same packed bytes as compressing on the device."""
+    D = 256
+    d, c = rademacher(D, 3).numpy(), lloyd_max(1, D).numpy()
+    g = torch.Generator().manual_seed(4)
+    xs = [torch.randn(n, D, generator=g).to(torch.float16) for n in (2500, 1, 777)]
+    xs[0] = xs[0].pin_memory()  # pinned and pageable inputs alike
+    outs = ops.compress_host(xs, d, c, residual=residual, device="cuda", chunk_rows=1000)
+    torch.cuda.current_stream().synchronize()
+    for x, o in zip(xs, outs):
+        ref = ops.compress(x.cuda(), d, c, residual=residual)
+        assert not o.code.is_cuda and o.code.is_pinned()
+        assert torch.equal(o.code, ref.code.cpu())
+        assert torch.equal(o.norms, ref.norms.cpu())
+        if residual:
+            assert torch.equal(o.res, ref.res.cpu()) and torch.equal(o.rnorms, ref.rnorms.cpu())
+    # the public method, repeated into the same buffers
+    comp = KudahitamCompressorV2(D, 1, seed=3)
+    a = comp.compress_to_host([xs[2]])
+    b = comp.compress_to_host([xs[2]], outs=[a[0].packed])
+    torch.cuda.current_stream().synchronize()
+    assert torch.equal(b[0].packed.code, comp.compress(xs[2].cuda()).packed.code.cpu())
