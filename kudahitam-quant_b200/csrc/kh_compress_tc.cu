@@ -156,9 +156,11 @@ __device__ __forceinline__ void store_words(uint32_t* dst, const uint32_t* w) {
 // symmetric codebook, the per-group generic code otherwise.
 template <int CK, bool RES, int NG, class P>
 __device__ __forceinline__ void quant_groups(const float (&u)[NG][32], float rs, const P& prm,
-                                             uint32_t* code, uint32_t* resw, float2& acc) {
+                                             uint32_t* code, uint32_t* resw, float2& acc,
+                                             bool nonzero_row) {
   if constexpr (CK == kCbSym2) {
-    quant_sym2_groups<NG, RES>(u, rs, prm.cb.c[1], code, resw, acc);
+    quant_sym2_groups<NG, RES>(u, rs, prm.cb.c[1], code, resw, acc,
+                               nonzero_row ? 0xffffffffu : 0u);
   } else {
     using Q = Quant<CK, RES>;
 #pragma unroll
@@ -374,7 +376,7 @@ __global__ void __launch_bounds__(320, 1)
       uint32_t code[4 * kCW];
       uint32_t resw[4];
       float2 acc = make_float2(0.f, 0.f);
-      quant_groups<CK, RES, 4>(u, rs, P, code, resw, acc);
+      quant_groups<CK, RES, 4>(u, rs, P, code, resw, acc, ss > 0.f);
       float a = acc.x + acc.y;
       if constexpr (D == 256) {
         if (RES) {

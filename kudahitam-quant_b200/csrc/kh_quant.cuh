@@ -177,9 +177,13 @@ struct Quant<kCbGen4, RES> {
 template <int NG, bool RES>
 __device__ __forceinline__ void quant_sym2_groups(const float (&u)[NG][32], float rs,
                                                   float c1, uint32_t* code,
-                                                  uint32_t* resw, float2& acc) {
-  const float2 nrs = make_float2(-rs, -rs);
-  const float2 zero = make_float2(0.f, 0.f);
+                                                  uint32_t* resw, float2& acc,
+                                                  uint32_t row_mask = 0xffffffffu) {
+  // The code bit is 1 for y > 0: push the sign bits of u itself (rs > 0)
+  // and invert the finished word.  An exact +0 then reads as 1 where the
+  // reference's strict argmin picks index 0; such elements are ties inside
+  // the 1e-6 band and either index is correct.  An all-zero row (row_mask
+  // 0) keeps index 0 throughout, as in the reference.
   uint32_t cw[NG], sw[NG];
 #pragma unroll
   for (int g = 0; g < NG; ++g) cw[g] = sw[g] = 0u;
@@ -188,9 +192,8 @@ __device__ __forceinline__ void quant_sym2_groups(const float (&u)[NG][32], floa
   for (int k = 30; k >= 0; k -= 2) {
 #pragma unroll
     for (int g = 0; g < NG; ++g) {
-      const float2 q = __ffma2_rn(make_float2(u[g][k], u[g][k + 1]), nrs, zero);
-      cw[g] = push_sign(cw[g], q.y);
-      cw[g] = push_sign(cw[g], q.x);
+      cw[g] = push_sign(cw[g], u[g][k + 1]);
+      cw[g] = push_sign(cw[g], u[g][k]);
       if (RES) {
         const float t0 = __fmaf_rn(fabsf(u[g][k]), rs, -c1);
         const float t1 = __fmaf_rn(fabsf(u[g][k + 1]), rs, -c1);
@@ -203,8 +206,9 @@ __device__ __forceinline__ void quant_sym2_groups(const float (&u)[NG][32], floa
   }
 #pragma unroll
   for (int g = 0; g < NG; ++g) {
-    code[g] = cw[g];
-    if (RES) resw[g] = cw[g] ^ sw[g];
+    const uint32_t c = ~cw[g] & row_mask;
+    code[g] = c;
+    if (RES) resw[g] = c ^ sw[g];
   }
   acc = __fadd2_rn(acc, __fadd2_rn(a2[0], a2[1]));
 }
