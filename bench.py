@@ -283,7 +283,7 @@ def run_engine(args, world, rank, local):
         t1 = torch.cuda.Event(enable_timing=True)
         t0.record(stream)
         for _ in range(args.steps):
-            step()
+            step()  # one kernel launch per step
         t1.record(stream)
         torch.cuda.synchronize()
         clk.mark_region(h0, time.perf_counter())
@@ -293,14 +293,9 @@ def run_engine(args, world, rank, local):
         ms = max_over_ranks(ms_local, world)
         rows_all = 2 * ROWS_PER_TENSOR * world * args.steps
         value = rows_all / (ms / 1e3)
-
-        # dominant kernel, per-launch times (at least ~0.3 s of launches so the
-        # clock record has samples under this load)
-        n_launch = max(args.steps, 5)
-        if args.only == "all":
-            n_launch = max(n_launch, int(0.3 / max(ms_local / args.steps / 1e3, 1e-6)))
-        per = time_loop(step, min(n_launch, 5000), stream)
-    launch_ms = statistics.median(per)
+    # average launch duration over the timed region (one launch per step,
+    # back to back on this stream; inter-launch gaps count against it)
+    launch_ms = ms_local / args.steps
     rows_launch = 2 * ROWS_PER_TENSOR
     achieved = rows_launch * ALG_BYTES_PER_ROW / (launch_ms / 1e3) / 1e9
     roof = {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
@@ -308,7 +303,8 @@ def run_engine(args, world, rank, local):
             "traffic": (NCU_TRAFFIC_BYTES_PER_ROW * rows_launch
                         if NCU_TRAFFIC_BYTES_PER_ROW else None),
             "algorithmic_bytes": rows_launch * ALG_BYTES_PER_ROW,
-            "launch_ms_median": launch_ms, "launches_timed": len(per),
+            "launch_ms_mean": launch_ms, "launches_timed": args.steps,
+            "timing": "CUDA events around the timed region / launches in it",
             "kernel": ("compress_simt_kernel<__half,256,Sym2,RES>"
                        if os.environ.get("KUDAHITAM_COMPRESS_PATH") == "simt"
                        else "compress_tc_kernel<__half,256,Sym2,RES>")}
