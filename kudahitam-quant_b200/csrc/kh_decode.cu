@@ -792,6 +792,20 @@ __global__ void __launch_bounds__(256, 2)
         }
       }
     }
+    // phase 2's first V rows, loaded now so that their latency overlaps the
+    // block reductions below
+    RowK<D> va[2][B];
+    auto load_vbatch = [&](RowK<D>(&dst)[B], int bi) {
+#pragma unroll
+      for (int u = 0; u < B; ++u) {
+        const int ii = t + (bi * B + u) * NT;
+        const int64_t row = row0 + (ii < n ? ii : 0);
+        load_v_row<D>(P, row, wr, bs, dst[u]);
+        dst[u].n = __ldg(P.v_norms + row);
+        dst[u].rn = __ldg(P.v_rnorms + row);
+      }
+    };
+    load_vbatch(va[0], 0);
     const float m_seg = block_max<NT>(mt, red);  // also: phase-1 table reads done
     const float m_new = fmaxf(m_run, m_seg);
     const float alpha = exp2f(m_run - m_new);  // 0 on the first segment
@@ -816,17 +830,6 @@ __global__ void __launch_bounds__(256, 2)
     float csum = 0.f;  // constant term in quanta
     const float k1 = wa * scale_inv, k2 = wb * scale_inv;
     {
-      RowK<D> a[2][B];
-      auto load_batch = [&](RowK<D>(&dst)[B], int bi) {
-#pragma unroll
-        for (int u = 0; u < B; ++u) {
-          const int ii = t + (bi * B + u) * NT;
-          const int64_t row = row0 + (ii < n ? ii : 0);
-          load_v_row<D>(P, row, wr, bs, dst[u]);
-          dst[u].n = __ldg(P.v_norms + row);
-          dst[u].rn = __ldg(P.v_rnorms + row);
-        }
-      };
       auto scatter_batch = [&](const RowK<D>(&src)[B], int bi) {
 #pragma unroll
         for (int u = 0; u < B; ++u) {
@@ -846,13 +849,12 @@ __global__ void __launch_bounds__(256, 2)
           });
         }
       };
-      load_batch(a[0], 0);
       for (int bi = 0; bi < nb; bi += 2) {
-        load_batch(a[1], bi + 1);
-        scatter_batch(a[0], bi);
+        load_vbatch(va[1], bi + 1);
+        scatter_batch(va[0], bi);
         if (bi + 1 < nb) {
-          load_batch(a[0], bi + 2);
-          scatter_batch(a[1], bi + 1);
+          load_vbatch(va[0], bi + 2);
+          scatter_batch(va[1], bi + 1);
         }
       }
     }
