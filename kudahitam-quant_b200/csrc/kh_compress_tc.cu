@@ -13,7 +13,8 @@
 //   warp 0      TMA producer: 128 x D tile -> shared memory ring (128B swizzle)
 //   warp 1      allocates tensor memory; one lane issues tcgen05.mma
 //   warps 2..9  two epilogue warpgroups; warpgroup g drains accumulator buffer
-//               g (tiles alternate), thread = tensor-memory lane = row
+//               g (tiles alternate), thread = tensor-memory lane = row; at
+//               D = 256 a thread reads its 256 values in two passes of 128
 // All mbarrier waits are bounded (kh::mbar_wait); a timeout records an error
 // bit and every role leaves its loop.  Every TMA load is a plain per-CTA load.
 #include <algorithm>
@@ -121,12 +122,9 @@ struct TcCfg {
   static constexpr uint32_t kTmemCols = 2 * kAccCols;
   static constexpr int kThreads = 320;
   static constexpr int kBarOff = kStages * kChunkBytes + kNB * kBMatBytes;
-  // barriers, the tensor-memory slot, then (D=256) the partner exchange
+  // barriers and the tensor-memory slot
   static constexpr int kXchOff = kBarOff + (2 * kStages + 4) * 8 + 16;
-  // D=256 exchange: sum of squares [tile parity][warpgroup][128 rows], then
-  // residual sums [warpgroup][128 rows]: 768 floats
-  static constexpr int kXchFloats = (D == 256) ? 6 * 128 : 0;
-  static constexpr int kSmem = 1024 + kXchOff + kXchFloats * 4;
+  static constexpr int kSmem = 1024 + kXchOff;
   static_assert(kSmem <= 232448, "exceeds the 227 KB of shared memory a CTA can use");
 };
 
@@ -185,7 +183,6 @@ __global__ void __launch_bounds__(320, 1)
   uint64_t* tfull = empty + C::kStages;
   uint64_t* tempty = tfull + 2;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(tempty + 2);
-  float* xch = reinterpret_cast<float*>(g + C::kXchOff);  // D=256 partner exchange
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -217,7 +214,7 @@ __global__ void __launch_bounds__(320, 1)
     }
     for (int b = 0; b < 2; ++b) {
       mbar_init(&tfull[b], 1);
-      mbar_init(&tempty[b], D == 128 ? 4 : 8);
+      mbar_init(&tempty[b], 4);  // the 4 warps of one warpgroup
     }
     fence_mbar_init();
   }
@@ -302,9 +299,7 @@ __global__ void __launch_bounds__(320, 1)
     int i = 0;
     int sg_cur = 0;
     for (int64_t t = blockIdx.x; t < total; t += gridDim.x, ++i) {
-      if constexpr (D == 128) {
-        if ((i & 1) != wg) continue;  // warpgroups alternate tiles
-      }
+      if ((i & 1) != wg) continue;  // warpgroups alternate tiles (and buffers)
       const int b = i & 1;
       const uint32_t jb = (uint32_t)((i >> 1) & 1);
       // warp-uniform outcome: tcgen05.ld below is a warp-collective
@@ -314,94 +309,103 @@ __global__ void __launch_bounds__(320, 1)
       const int sg = seg_of(t, sg_cur);
       const int64_t row = (t - P.tile_begin[sg]) * C::kM + r;
       const uint32_t ta = tmem + ((uint32_t)(32 * q) << 16) + b * C::kAccCols;
+      constexpr int kRowCW = (D / 32) * kCW;
+      uint32_t code[kRowCW];
+      uint32_t resw[D / 32];
+      float2 acc = make_float2(0.f, 0.f);
+      float norm;
 
-      float u[4][32];
-      float2 s2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
       if constexpr (D == 128) {
+        float u[4][32];
+        float2 s2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
 #pragma unroll
         for (int gq = 0; gq < 4; ++gq) tmem_ld32(ta + 32 * gq, u[gq]);
-      } else {
-        // this warpgroup's half of the pairs: a = acc0[64 wg ..], b = acc1[64 wg ..]
+        tmem_wait_ld();
+        // accumulator in registers: hand the buffer back to the MMA issuer
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[b]);
 #pragma unroll
-        for (int gq = 0; gq < 2; ++gq) {
-          tmem_ld32(ta + 64 * wg + 32 * gq, u[gq]);
-          tmem_ld32(ta + 128 + 64 * wg + 32 * gq, u[2 + gq]);
-        }
-      }
-      tmem_wait_ld();
-      // accumulator in registers: hand the buffer back to the MMA issuer
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&tempty[b]);
-
-#pragma unroll
-      for (int gq = 0; gq < 4; ++gq)
-#pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const float2 p = make_float2(u[gq][e], u[gq][e + 1]);
-          s2[gq & 1] = __ffma2_rn(p, p, s2[gq & 1]);
-        }
-      float ss = (s2[0].x + s2[0].y) + (s2[1].x + s2[1].y);
-      if constexpr (D == 256) {
-        // pairs (a, b) -> (a + b, a - b) = (u_lo, u_hi); exchange the partial
-        // sum of a^2 + b^2 with the other warpgroup (same row)
-        const float2 neg1 = make_float2(-1.f, -1.f);
-#pragma unroll
-        for (int gq = 0; gq < 2; ++gq)
+        for (int gq = 0; gq < 4; ++gq)
 #pragma unroll
           for (int e = 0; e < 32; e += 2) {
-            const float2 a = make_float2(u[gq][e], u[gq][e + 1]);
-            const float2 bb = make_float2(u[2 + gq][e], u[2 + gq][e + 1]);
-            const float2 lo = __fadd2_rn(a, bb);
-            const float2 hi = __ffma2_rn(bb, neg1, a);
-            u[gq][e] = lo.x; u[gq][e + 1] = lo.y;
-            u[2 + gq][e] = hi.x; u[2 + gq][e + 1] = hi.y;
+            const float2 p = make_float2(u[gq][e], u[gq][e + 1]);
+            s2[gq & 1] = __ffma2_rn(p, p, s2[gq & 1]);
           }
-        // slot by tile parity: the partner may still be reading the previous
-        // tile's slot when this warpgroup writes the next one (with no
-        // residual exchange there is one barrier per tile)
-        float* xs = xch + (i & 1) * 256;
-        xs[wg * 128 + r] = ss;
-        named_bar_sync(1, 256);
-        ss = xs[r] + xs[128 + r];
-      }
-      // ss = 128 ||x||^2 for both head dims
-      const float norm = ss > 0.f ? sqrtf(ss * (1.0f / 128.0f)) : 1e-8f;
-      const float rs = 1.0f / (norm * (D == 128 ? 11.313708498984761f : 16.0f));
-
-      uint32_t code[4 * kCW];
-      uint32_t resw[4];
-      float2 acc = make_float2(0.f, 0.f);
-      quant_groups<CK, RES, 4>(u, rs, P, code, resw, acc, ss > 0.f);
-      float a = acc.x + acc.y;
-      if constexpr (D == 256) {
-        if (RES) {
-          xch[512 + wg * 128 + r] = a;
-          named_bar_sync(1, 256);
-          a = xch[512 + r] + xch[512 + 128 + r];
+        const float ss = (s2[0].x + s2[0].y) + (s2[1].x + s2[1].y);  // = 128 ||x||^2
+        norm = ss > 0.f ? sqrtf(ss * (1.0f / 128.0f)) : 1e-8f;
+        const float rs = 1.0f / (norm * 11.313708498984761f);
+        quant_groups<CK, RES, 4>(u, rs, P, code, resw, acc, ss > 0.f);
+      } else {
+        // D = 256: a = X_lo B in columns [0,128), b = X_hi B in [128,256);
+        // u_lo = a + b, u_hi = a - b.  The thread owns the whole row and
+        // reads its 256 values twice, 128 at a time: sums of squares first
+        // (sum a^2 + b^2 = 128 ||x||^2), then the butterfly and quantisation
+        // of 64 columns of a and b (words 2h, 2h+1 of u_lo, 4+2h, 5+2h of u_hi).
+        float2 s2[2] = {make_float2(0.f, 0.f), make_float2(0.f, 0.f)};
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          float v[4][32];
+#pragma unroll
+          for (int gq = 0; gq < 4; ++gq) tmem_ld32(ta + 128 * h + 32 * gq, v[gq]);
+          tmem_wait_ld();
+#pragma unroll
+          for (int gq = 0; gq < 4; ++gq)
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              const float2 p = make_float2(v[gq][e], v[gq][e + 1]);
+              s2[gq & 1] = __ffma2_rn(p, p, s2[gq & 1]);
+            }
+        }
+        const float ss = (s2[0].x + s2[0].y) + (s2[1].x + s2[1].y);
+        norm = ss > 0.f ? sqrtf(ss * (1.0f / 128.0f)) : 1e-8f;
+        const float rs = 1.0f / (norm * 16.0f);
+        const float2 neg1 = make_float2(-1.f, -1.f);
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          float u[4][32];  // a cols 64h.., 64h+32.., then b cols 64h.., 64h+32..
+          tmem_ld32(ta + 64 * h, u[0]);
+          tmem_ld32(ta + 64 * h + 32, u[1]);
+          tmem_ld32(ta + 128 + 64 * h, u[2]);
+          tmem_ld32(ta + 128 + 64 * h + 32, u[3]);
+          tmem_wait_ld();
+          if (h == 1) {  // every read of this buffer done: hand it back
+            tc_fence_before();
+            __syncwarp();
+            if (lane == 0) mbar_arrive(&tempty[b]);
+          }
+#pragma unroll
+          for (int gq = 0; gq < 2; ++gq)
+#pragma unroll
+            for (int e = 0; e < 32; e += 2) {
+              const float2 pa = make_float2(u[gq][e], u[gq][e + 1]);
+              const float2 pb = make_float2(u[2 + gq][e], u[2 + gq][e + 1]);
+              const float2 lo = __fadd2_rn(pa, pb);
+              const float2 hi = __ffma2_rn(pb, neg1, pa);
+              u[gq][e] = lo.x; u[gq][e + 1] = lo.y;
+              u[2 + gq][e] = hi.x; u[2 + gq][e + 1] = hi.y;
+            }
+          uint32_t ch[4 * kCW], rh[4];
+          quant_groups<CK, RES, 4>(u, rs, P, ch, rh, acc, ss > 0.f);
+#pragma unroll
+          for (int w = 0; w < 2 * kCW; ++w) {
+            code[2 * h * kCW + w] = ch[w];
+            code[(4 + 2 * h) * kCW + w] = ch[2 * kCW + w];
+          }
+          resw[2 * h] = rh[0];
+          resw[2 * h + 1] = rh[1];
+          resw[4 + 2 * h] = rh[2];
+          resw[5 + 2 * h] = rh[3];
         }
       }
+      const float a = acc.x + acc.y;
       const float rn = a > 0.f ? norm * sqrtf(a) : 1e-8f;
 
       if (row < P.n_rows[sg]) {
-        constexpr int kRowCW = (D / 32) * kCW;
-        uint32_t* crow = P.code[sg] + row * kRowCW;
-        if constexpr (D == 128) {
-          store_words<4 * kCW>(crow, code);
-          if (RES) store_words<4>(P.res[sg] + row * 4, resw);
-        } else {
-          // groups held: u_lo 64wg.. (words 2wg, 2wg+1), u_hi (words 4+2wg, 5+2wg)
-          store_words<2 * kCW>(crow + 2 * wg * kCW, code);
-          store_words<2 * kCW>(crow + (4 + 2 * wg) * kCW, code + 2 * kCW);
-          if (RES) {
-            store_words<2>(P.res[sg] + row * 8 + 2 * wg, resw);
-            store_words<2>(P.res[sg] + row * 8 + 4 + 2 * wg, resw + 2);
-          }
-        }
-        if (D == 128 || wg == 0) {
-          P.norms[sg][row] = norm;
-          if (RES) P.rnorms[sg][row] = rn;
-        }
+        store_words<kRowCW>(P.code[sg] + row * kRowCW, code);
+        if (RES) store_words<D / 32>(P.res[sg] + row * (D / 32), resw);
+        P.norms[sg][row] = norm;
+        if (RES) P.rnorms[sg][row] = rn;
       }
     }
   }
