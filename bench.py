@@ -258,6 +258,10 @@ def run_engine(args, world, rank, local):
         if rank == 0:
             print(json.dumps({"decode": dec}), flush=True)
         return
+    if args.only == "fp32":
+        if rank == 0:
+            print(json.dumps({"fp32_1bit": fp32_1bit_bench(dev, args)}), flush=True)
+        return
     if args.only == "layers":
         lay = layers_bench(dev, args)
         if rank == 0:
@@ -345,6 +349,7 @@ def run_engine(args, world, rank, local):
     dec = decode_bench(dev, args, world, rank) if args.only == "all" else None
     lay = (layers_bench(dev, args)
            if args.only == "all" and not args.no_layers and world == 1 else None)
+    f32 = fp32_1bit_bench(dev, args) if args.only == "all" and world == 1 else None
 
     line = {"metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
@@ -353,11 +358,74 @@ def run_engine(args, world, rank, local):
             "hbm_gbs": achieved, "hbm_frac_of_measured": achieved / peak,
             "hbm_frac_of_spec_8000": achieved / 8000.0,
             "roofline": roof, "e2e": e2e, "decode": dec, "layers_28": lay,
+            "fp32_1bit": f32,
             "gpu_launches": args.steps, "clocks": clk.summary()}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_run()
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def fp32_1bit_bench(dev, args) -> dict:
+    """The CPU-runnable configuration in 1-bit mode on the GPU: K and V fp32
+    [1, 16, 10000, 128], N(0,1) with 3 channels per head scaled by 10
+    (seeded), code + norm per row (532 B/row), both tensors in one launch;
+    plus the same at S = 40000 (655 MB of input, above L2)."""
+    from kudahitam import ops
+    from kudahitam.codebook import lloyd_max, rademacher
+    d, c = rademacher(128, 1), lloyd_max(1, 128)
+    peak, _ = peaks()
+    stream = torch.cuda.current_stream(dev)
+    out = {"config": "K, V fp32 [1,16,S,128], 3 outlier channels x10 per head, 1-bit mode"}
+    for S_ in (10000, 40000):
+        g = torch.Generator(device=dev).manual_seed(0)
+        xs = []
+        for _ in range(2):
+            x = torch.randn(1, 16, S_, 128, device=dev, generator=g)
+            for h in range(16):
+                ch = torch.randperm(128, device=dev, generator=g)[:3]
+                x[0, h][:, ch] *= 10.0
+            xs.append(x)
+        outs = [ops.empty_packed(x.shape, 1, False, dev) for x in xs]
+
+        def step():
+            ops.compress_many(xs, d, c, residual=False, outs=outs)
+
+        for _ in range(3):
+            step()
+        torch.cuda.synchronize()
+        # host cost of one API call (the GPU is idle between short launches)
+        h0 = time.perf_counter()
+        for _ in range(20):
+            step()
+        host_us = (time.perf_counter() - h0) / 20 * 1e6
+        torch.cuda.synchronize()
+        per = time_loop(step, 20, stream)
+        # the same launch replayed from a CUDA graph: kernel time without the
+        # host's per-call work
+        side = torch.cuda.Stream(dev)
+        side.wait_stream(stream)
+        graph = torch.cuda.CUDAGraph()
+        with torch.cuda.stream(side):
+            step()
+            with torch.cuda.graph(graph, stream=side):
+                step()
+        stream.wait_stream(side)
+        torch.cuda.synchronize()
+        gper = time_loop(graph.replay, 20, stream)
+        del graph
+        ms, gms = statistics.median(per), statistics.median(gper)
+        rows = 2 * 16 * S_
+        bpr = 128 * 4 + 128 // 8 + 4
+        out[f"S{S_}"] = {"rows": rows, "us_per_step": ms * 1e3, "rows_per_s": rows / (ms / 1e3),
+                         "gbs": rows * bpr / (ms / 1e3) / 1e9,
+                         "frac_of_measured_hbm": rows * bpr / (ms / 1e3) / 1e9 / peak,
+                         "graph_us_per_step": gms * 1e3,
+                         "graph_frac_of_measured_hbm": rows * bpr / (gms / 1e3) / 1e9 / peak,
+                         "host_us_per_call": host_us,
+                         "l2": "fits in L2" if rows * 512 < 126e6 else "above L2"}
+        del xs, outs
+    return out
 
 
 def layers_bench(dev, args) -> dict:
@@ -478,7 +546,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-layers", action="store_true",
                     help="skip the 28-layer batched compression line (60 GB resident)")
-    ap.add_argument("--only", choices=["all", "compress", "decode", "layers"], default="all",
+    ap.add_argument("--only", choices=["all", "compress", "decode", "layers", "fp32"], default="all",
                     help="run one part (small cases for profiler captures)")
     ap.add_argument("--seq", type=int, default=None,
                     help="override S of the compression workload (profiling only)")

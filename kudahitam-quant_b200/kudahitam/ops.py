@@ -20,20 +20,42 @@ _DTYPE_CODE = {torch.float32: _lib.KH_F32, torch.float16: _lib.KH_F16,
                torch.bfloat16: _lib.KH_BF16}
 
 HEAD_DIMS = (128, 256)
+_MAX_SEGMENTS = 64  # kh_max_segments(); checked against the library by the tests
 
 
-def _vp(t: Optional[torch.Tensor]) -> Optional[ctypes.c_void_p]:
-    return None if t is None else ctypes.c_void_p(t.data_ptr())
+def _vp(t: Optional[torch.Tensor]) -> Optional[int]:
+    """Device or host address of a tensor for a void* argument (None = NULL)."""
+    return None if t is None else t.data_ptr()
 
 
 def _host_f32(t) -> torch.Tensor:
     """Contiguous float32 CPU copy (d vectors and centroids travel by value)."""
+    if (isinstance(t, torch.Tensor) and t.dtype == torch.float32 and not t.is_cuda
+            and not t.requires_grad and t.is_contiguous()):
+        return t  # already in the form the library reads
     t = torch.as_tensor(t)
     return t.detach().to(device="cpu", dtype=torch.float32).contiguous()
 
 
-def _stream(device: torch.device) -> ctypes.c_void_p:
-    return ctypes.c_void_p(torch.cuda.current_stream(device).cuda_stream)
+def _stream(device: torch.device) -> int:
+    return torch.cuda.current_stream(device).cuda_stream
+
+
+class _Nothing:
+    def __enter__(self):
+        return self
+
+    def __exit__(self, *exc):
+        return False
+
+
+_NOTHING = _Nothing()
+
+
+def _on(dev: torch.device):
+    """``torch.cuda.device(dev)`` when dev is not the current device (the
+    switch costs microseconds per call on the common single-device path)."""
+    return _NOTHING if dev.index == torch.cuda.current_device() else torch.cuda.device(dev)
 
 
 def _require_cuda(*ts: Optional[torch.Tensor]) -> torch.device:
@@ -54,6 +76,8 @@ def _rows(x: torch.Tensor) -> tuple[torch.Tensor, int]:
     """[N, D] view with unit inner stride and a 16-byte row pitch (copies
     only when the layout does not allow it)."""
     D = x.shape[-1]
+    if x.is_contiguous() and x.data_ptr() % 16 == 0 and (D * x.element_size()) % 16 == 0:
+        return x.view(-1, D), D  # the common case: used in place
     x2 = x.reshape(-1, D)
     elt = x2.element_size()
     ok = (x2.stride(-1) == 1 and x2.data_ptr() % 16 == 0
@@ -156,7 +180,7 @@ def compress(x: torch.Tensor, d, centroids, residual: bool = True,
     x2, stride = _rows(x)
     if out is None:
         out = empty_packed(x.shape, bits, residual, dev)
-    with torch.cuda.device(dev):
+    with _on(dev):
         _lib.call("kh_compress", _vp(x2), _DTYPE_CODE[x.dtype], x2.shape[0], D, stride,
                   _vp(dh), _vp(ch), n_c, int(residual), _vp(out.code), _vp(out.res),
                   _vp(out.norms), _vp(out.rnorms), _stream(dev))
@@ -233,7 +257,7 @@ def compress_host(xs: Sequence[torch.Tensor], d, centroids, residual: bool = Tru
     fields = ("code", "res", "norms", "rnorms") if residual else ("code", "norms")
     k = 0
     last = None
-    with torch.cuda.device(dev):
+    with _on(dev):
         for x, o in zip(xs, outs):
             rows = x.reshape(-1, D)
             if not rows.is_contiguous():
@@ -296,24 +320,26 @@ def compress_many(xs: Sequence[torch.Tensor], d, centroids, residual: bool = Tru
     outs = list(outs) if outs is not None else [empty_packed(t.shape, bits, residual, dev)
                                                 for t in xs]
     rows = [_rows(t) for t in xs]
-    maxseg = _lib.lib().kh_max_segments()
-    with torch.cuda.device(dev):
+    maxseg = _MAX_SEGMENTS
+    with _on(dev):
+        stream = _stream(dev)
         for i0 in range(0, len(xs), maxseg):
             sl = range(i0, min(len(xs), i0 + maxseg))
             n = len(sl)
-            P = ctypes.c_void_p * n
-            I = ctypes.c_int64 * n
+            P = ctypes.c_uint64 * n
             args = [
                 P(*[rows[i][0].data_ptr() for i in sl]),
-                I(*[rows[i][0].shape[0] for i in sl]),
-                I(*[rows[i][1] for i in sl]),
+                P(*[rows[i][0].shape[0] for i in sl]),
+                P(*[rows[i][1] for i in sl]),
                 P(*[outs[i].code.data_ptr() for i in sl]),
                 P(*[(outs[i].res.data_ptr() if residual else 0) for i in sl]),
                 P(*[outs[i].norms.data_ptr() for i in sl]),
                 P(*[(outs[i].rnorms.data_ptr() if residual else 0) for i in sl]),
             ]
-            _lib.call("kh_compress_batched", n, *[ctypes.cast(a, ctypes.c_void_p) for a in args],
-                      _DTYPE_CODE[dt], D, _vp(dh), _vp(ch), n_c, int(residual), _stream(dev))
+            # the arrays are int64 / pointer tables: pass their addresses
+            _lib.call("kh_compress_batched", n, *[ctypes.addressof(a) for a in args],
+                      _DTYPE_CODE[dt], D, dh.data_ptr(), ch.data_ptr(), n_c, int(residual),
+                      stream)
     return outs
 
 
@@ -324,7 +350,7 @@ def fwht_(x: torch.Tensor) -> torch.Tensor:
     if x.dtype != torch.float32 or not x.is_contiguous():
         raise ValueError("fwht_ needs a contiguous float32 tensor")
     D = x.shape[-1]
-    with torch.cuda.device(dev):
+    with _on(dev):
         _lib.call("kh_fwht_inplace", _vp(x), x.numel() // D if D else 0, D, _stream(dev))
     return x
 
@@ -345,7 +371,7 @@ def materialize(p: PackedKV, d, centroids, idx: bool = True, kmse: bool = True,
     o_idx = torch.empty((n, D), dtype=torch.uint8, device=dev) if idx else None
     o_k = torch.empty((n, D), dtype=torch.float32, device=dev) if kmse else None
     o_s = torch.empty((n, D), dtype=torch.int8, device=dev) if (signs and p.res is not None) else None
-    with torch.cuda.device(dev):
+    with _on(dev):
         _lib.call("kh_materialize", _vp(p.code), _vp(p.res), _vp(p.norms), n, D, _vp(dh),
                   _vp(ch), n_c, _vp(o_idx), _vp(o_k), _vp(o_s), _stream(dev))
     return {"idx": o_idx, "kmse": o_k, "signs": o_s}
@@ -366,7 +392,7 @@ def score(q: torch.Tensor, p: PackedKV, d, centroids, seq_len: Optional[int] = N
     qf = q.to(torch.float32).contiguous()
     dh, ch = _host_f32(d), _host_f32(centroids)
     out = torch.empty((G, nq, S), dtype=torch.float32, device=dev)
-    with torch.cuda.device(dev):
+    with _on(dev):
         _lib.call("kh_score", _vp(qf), G, nq, D, _vp(p.code), _vp(p.res), _vp(p.norms),
                   _vp(p.rnorms), S, _vp(dh), _vp(ch), ch.numel(), _vp(out), _stream(dev))
     return out
@@ -403,7 +429,7 @@ def decode_partial(q: torch.Tensor, k: PackedKV, v: PackedKV, dk, dv, centroids,
         raise ValueError("decode attention needs caches compressed with the residual plane")
     qf = q.to(torch.float32).contiguous()
     dkh, dvh, ch = _host_f32(dk), _host_f32(dv), _host_f32(centroids)
-    with torch.cuda.device(dev):
+    with _on(dev):
         _lib.call("kh_decode_partial_gqa", _vp(qf), G, n_q, D, _vp(k.code), _vp(k.res),
                   _vp(k.norms), _vp(k.rnorms), _vp(v.code), _vp(v.res), _vp(v.norms),
                   _vp(v.rnorms), seq_len, seq_begin, seq_end, _vp(dkh), _vp(dvh), _vp(ch),
@@ -419,7 +445,7 @@ def decode_combine(partials: torch.Tensor, n_parts: int, dv, out: torch.Tensor) 
     D = out.shape[-1]
     R = out.numel() // D if D else 0
     dvh = _host_f32(dv)
-    with torch.cuda.device(dev):
+    with _on(dev):
         _lib.call("kh_decode_combine", _vp(partials), R, n_parts, D, _vp(dvh), _vp(out),
                   _stream(dev))
     return out
@@ -496,7 +522,7 @@ def fused_asymmetric_attention(q: torch.Tensor, k_packed: torch.Tensor, signs: t
     kp = prep(k_packed, torch.uint8)
     dv, kn, rn, cb = (prep(t, torch.float32) for t in (d_vec, k_norms, r_norms, centroids))
     out = torch.empty((H, S), dtype=torch.float32, device=dev)
-    with torch.cuda.device(dev):
+    with _on(dev):
         _lib.call("kh_score_packed_compat", _vp(qh), H, D, S, _vp(kp), _vp(sg), _vp(dv),
                   _vp(kn), _vp(rn), _vp(cb), int(layer_id), int(active_mask) & 0xFF,
                   float(scale), _vp(out), _stream(dev))
