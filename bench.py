@@ -258,6 +258,10 @@ def run_engine(args, world, rank, local):
         if rank == 0:
             print(json.dumps({"decode": dec}), flush=True)
         return
+    if args.only == "score":
+        if rank == 0:
+            print(json.dumps({"score": score_bench(dev, args)}), flush=True)
+        return
     if args.only == "fp32":
         if rank == 0:
             print(json.dumps({"fp32_1bit": fp32_1bit_bench(dev, args)}), flush=True)
@@ -350,6 +354,7 @@ def run_engine(args, world, rank, local):
     lay = (layers_bench(dev, args)
            if args.only == "all" and not args.no_layers and world == 1 else None)
     f32 = fp32_1bit_bench(dev, args) if args.only == "all" and world == 1 else None
+    sco = score_bench(dev, args) if args.only == "all" and world == 1 else None
 
     line = {"metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
@@ -358,12 +363,49 @@ def run_engine(args, world, rank, local):
             "hbm_gbs": achieved, "hbm_frac_of_measured": achieved / peak,
             "hbm_frac_of_spec_8000": achieved / 8000.0,
             "roofline": roof, "e2e": e2e, "decode": dec, "layers_28": lay,
-            "fp32_1bit": f32,
+            "fp32_1bit": f32, "score": sco,
             "gpu_launches": args.steps, "clocks": clk.summary()}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_run()
     if rank == 0:
         print(json.dumps(line), flush=True)
+
+
+def score_bench(dev, args) -> dict:
+    """Asymmetric scores (the reference's asymmetric_attention_scores) of q
+    [32, 16, 128] against a 2-bit-mode packed K cache [32, 16, 40000, 128]:
+    40 B read and 4 B written per cached row."""
+    from kudahitam import ops
+    from kudahitam.codebook import lloyd_max, rademacher
+    G, S_, Dq = DEC_B * DEC_H, DEC_S, DEC_D
+    d, c = rademacher(Dq, 10), lloyd_max(1, Dq)
+    g = torch.Generator(device=dev).manual_seed(5)
+    pk = ops.empty_packed((G, S_, Dq), 1, True, dev)
+    for i in range(0, G, 64):
+        x = torch.randn(64, S_, Dq, device=dev, generator=g).to(torch.bfloat16)
+        ops.compress(x, d, c, out=pk.rows(i * S_, (i + 64) * S_))
+    q = torch.randn(G, 1, Dq, generator=torch.Generator().manual_seed(4)).to(dev)
+    out = torch.empty(G, 1, S_, device=dev)
+    stream = torch.cuda.current_stream(dev)
+    dh, ch = ops._host_f32(d), ops._host_f32(c)
+
+    def step():
+        # the op's own launch, writing into a preallocated output
+        from kudahitam import _lib
+        _lib.call("kh_score", q.data_ptr(), G, 1, Dq, pk.code.data_ptr(), pk.res.data_ptr(),
+                  pk.norms.data_ptr(), pk.rnorms.data_ptr(), S_, dh.data_ptr(),
+                  ch.data_ptr(), 2, out.data_ptr(), stream.cuda_stream)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    ms = statistics.median(time_loop(step, 20, stream))
+    peak, _ = peaks()
+    bytes_step = G * S_ * (40 + 4)
+    return {"config": "q [32,16,1,128] vs 2-bit-mode packed K [32,16,40000,128]",
+            "us_per_step": ms * 1e3, "gbs": bytes_step / (ms / 1e3) / 1e9,
+            "frac_of_measured_hbm": bytes_step / (ms / 1e3) / 1e9 / peak,
+            "kernel": "score_tab_kernel<128, residual>"}
 
 
 def fp32_1bit_bench(dev, args) -> dict:
@@ -546,7 +588,7 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-layers", action="store_true",
                     help="skip the 28-layer batched compression line (60 GB resident)")
-    ap.add_argument("--only", choices=["all", "compress", "decode", "layers", "fp32"], default="all",
+    ap.add_argument("--only", choices=["all", "compress", "decode", "layers", "fp32", "score"], default="all",
                     help="run one part (small cases for profiler captures)")
     ap.add_argument("--seq", type=int, default=None,
                     help="override S of the compression workload (profiling only)")

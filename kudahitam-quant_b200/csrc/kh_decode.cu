@@ -19,6 +19,7 @@
 #include <type_traits>
 #include <utility>
 
+#include "kh_bytetab.cuh"
 #include "kh_common.cuh"
 #include "kh_internal.h"
 
@@ -204,23 +205,8 @@ __global__ void __launch_bounds__(D)
 // softmax weight into a histogram per byte position, H_p[byte] += w; after a
 // chunk of rows the histograms are folded into the D accumulators
 // (acc[8p+b] = sum over v with bit b set of H_p[v]).
-//
-// Bank-conflict-free addressing: a table / histogram entry (slot j, value v)
-// lives at float index 32 v + j, i.e. in bank j.  Lane l of a warp visits
-// byte position p = (k + l) mod P at step k (P = D/8 positions), in copy
-// c = l / P of the table (32 / P copies), slot j = p + P c: the 32 lanes of
-// a warp always touch 32 distinct banks.  A lane reads its row's bytes in
-// that rotated order by loading the plane's words rotated by
-// (l mod P) / 4 and funnel-shifting by 8 (l mod 4) bits.
-// Calls f(std::integral_constant<int, I>) for I = 0 .. N-1, fully unrolled.
-template <class F, int... I>
-__device__ __forceinline__ void static_for_impl(F&& f, std::integer_sequence<int, I...>) {
-  (f(std::integral_constant<int, I>{}), ...);
-}
-template <int N, class F>
-__device__ __forceinline__ void static_for(F&& f) {
-  static_for_impl(f, std::make_integer_sequence<int, N>{});
-}
+// Tables and histograms use the bank-conflict-free slot rotation described
+// in kh_bytetab.cuh (entry (slot j, value v) at float index 32 v + j).
 
 template <int D>
 struct V2Cfg {
@@ -234,54 +220,6 @@ struct V2Cfg {
   static constexpr int kSmem = (3 * kTab + D + 64 + 4 * D) * 4;
 };
 
-// Rotated view of one row plane: byte k of the result = plane byte
-// (k + r) mod P, r = lane mod P.
-template <int D>
-__device__ __forceinline__ void load_rotated(const uint32_t* __restrict__ plane, int wr,
-                                             int bs, uint32_t (&rot)[D / 32]) {
-  constexpr int kW = D / 32;
-  uint32_t w[kW];
-  static_for<kW>([&](auto ic) {
-    constexpr int i = decltype(ic)::value;
-    w[i] = __ldg(plane + ((i + wr) & (kW - 1)));
-  });
-  static_for<kW>([&](auto ic) {
-    constexpr int i = decltype(ic)::value;
-    rot[i] = __funnelshift_r(w[i], w[(i + 1) % kW], bs);
-  });
-}
-
-// byte k of a rotated plane, zero-extended
-template <int K>
-__device__ __forceinline__ uint32_t byte_of(const uint32_t* rot) {
-  return __byte_perm(rot[K >> 2], 0u, 0x4440u + (K & 3));
-}
-
-template <int NT>
-__device__ __forceinline__ float block_sum(float v, float* red) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);
-  __syncthreads();
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-  __syncthreads();
-  float r = 0.f;
-#pragma unroll
-  for (int i = 0; i < NT / 32; ++i) r += red[i];
-  return r;
-}
-
-template <int NT>
-__device__ __forceinline__ float block_max(float v, float* red) {
-#pragma unroll
-  for (int o = 16; o > 0; o >>= 1) v = fmaxf(v, __shfl_xor_sync(0xffffffffu, v, o));
-  __syncthreads();
-  if ((threadIdx.x & 31) == 0) red[threadIdx.x >> 5] = v;
-  __syncthreads();
-  float r = red[0];
-#pragma unroll
-  for (int i = 1; i < NT / 32; ++i) r = fmaxf(r, red[i]);
-  return r;
-}
 
 template <int D>
 struct RowK {
@@ -537,9 +475,6 @@ __global__ void __launch_bounds__(256)
 // loaded while the current rows are scored / scattered.  (Bulk L2
 // prefetches of the rows a few batches ahead were measured slower.)
 // Build-time tuning knobs of decode v3 (defaults are the measured best).
-#ifndef KH_DECODE_WIDE_LOADS
-#define KH_DECODE_WIDE_LOADS 1
-#endif
 #ifndef KH_DECODE_SEG
 #define KH_DECODE_SEG 8192
 #endif
@@ -561,19 +496,6 @@ struct V3Cfg {
       (kTabWords + kSeg + 2048 + D + 2 * kP * 16 + 64) * 4;
 };
 
-// Byte address 256 * (byte B of x) + (byte B of slots): one byte-permute.
-// slots packs four lane slot offsets (each 4 * slot < 128) one per byte;
-// result bytes 2 and 3 replicate the (zero) sign bit of the slot byte.
-// (prmt.b32 generic mode: a selector nibble with its msb set replicates the
-// sign bit of the selected byte.)
-template <int B>
-__device__ __forceinline__ uint32_t tab_addr(uint32_t x, uint32_t slots) {
-  constexpr uint32_t ys = 4u + B;  // selector of byte B of `slots`
-  constexpr uint32_t sel = ((8u | ys) << 12) | ((8u | ys) << 8) | (B << 4) | ys;
-  uint32_t r;
-  asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(x), "r"(slots), "n"(sel));
-  return r;
-}
 
 template <int D>
 struct RowKV {
@@ -581,28 +503,6 @@ struct RowKV {
   float n, rn, vn, vrn;
 };
 
-// v3 plane load.  D = 128: one 16-byte load per row (4 L1 wavefronts per
-// warp instead of 16 for four rotated 4-byte loads), rotated in registers:
-// words by wr (two select stages), then bytes by bs (funnel shifts).
-// D = 256: rotated 4-byte loads as in v2.
-template <int D>
-__device__ __forceinline__ void load_rotated_v3(const uint32_t* __restrict__ plane, int wr,
-                                                int bs, uint32_t (&rot)[D / 32]) {
-  if constexpr (D == 128 && KH_DECODE_WIDE_LOADS) {
-    const uint4 v = __ldg(reinterpret_cast<const uint4*>(plane));
-    const bool h = wr & 2, o = wr & 1;
-    const uint32_t y0 = h ? v.z : v.x, y1 = h ? v.w : v.y;
-    const uint32_t y2 = h ? v.x : v.z, y3 = h ? v.y : v.w;
-    const uint32_t z0 = o ? y1 : y0, z1 = o ? y2 : y1;
-    const uint32_t z2 = o ? y3 : y2, z3 = o ? y0 : y3;
-    rot[0] = __funnelshift_r(z0, z1, bs);
-    rot[1] = __funnelshift_r(z1, z2, bs);
-    rot[2] = __funnelshift_r(z2, z3, bs);
-    rot[3] = __funnelshift_r(z3, z0, bs);
-  } else {
-    load_rotated<D>(plane, wr, bs, rot);
-  }
-}
 
 template <int D>
 __device__ __forceinline__ void load_k_row(const DecodeParams& P, int64_t row, int wr, int bs,

@@ -8,8 +8,14 @@
 // so for a two-level codebook, with M1 = sum_{idx_i=1} q~_i,
 // M2 = sum_{sign_i=+1} q~_i and Q = sum_i q~_i:
 //   score = norm (c0 Q + (c1 - c0) M1) + r_norm / sqrt(D) (2 M2 - Q).
+// Two-level codebooks take the table-driven kernel (score_tab_kernel); the
+// 4-level codebook (and KUDAHITAM_SCORE_PATH=direct) the direct one.
 #include <cmath>
+#include <cstdlib>
+#include <cstring>
+#include <mutex>
 
+#include "kh_bytetab.cuh"
 #include "kh_common.cuh"
 #include "kh_internal.h"
 
@@ -134,6 +140,142 @@ __global__ void __launch_bounds__(kScoreThreads)
   }
 }
 
+// Table-driven scores for the two-level codebook.  M1 and M2 are both
+// sums of q~ over the set bits of a plane, so one byte table serves both:
+// T[v][slot] = sum of q~ over the set bits of byte value v at the slot's byte
+// position.  A row costs D/8 lookups per plane instead of D bit-selects.
+// One CTA serves one query row (query j of cache group g) and kRows cached
+// rows, so the query transform and the table are built once per kRows rows.
+// Table rows are 256 bytes apart (slots 0..31 used) so that one byte-permute
+// forms each lookup address (see tab_addr).
+template <int D>
+struct ScoreTabCfg {
+  static constexpr int kP = D / 8;
+  static constexpr int kThreads = 256;
+  static constexpr int kRows = 8192;   // cached rows per CTA
+  static constexpr int kBatch = 2;     // rows per thread in flight
+  // table [256][64] | q~ [D] | nibble tables [2][16][kP] | reduction scratch [32]
+  static constexpr int kSmem = (256 * 64 + D + 2 * kP * 16 + 32) * 4;
+};
+
+template <int D, bool RES>
+__global__ void __launch_bounds__(256, 2)
+    score_tab_kernel(const __grid_constant__ ScoreParams P) {
+  using C = ScoreTabCfg<D>;
+  constexpr int kP = C::kP;
+  constexpr int kW = D / 32;
+  constexpr int NT = C::kThreads;
+  constexpr int B = C::kBatch;
+  extern __shared__ __align__(16) unsigned char smem_s[];
+  unsigned char* tabb = smem_s;
+  float* qt = reinterpret_cast<float*>(smem_s) + 256 * 64;
+  float* nib = qt + D;
+  float* red = nib + 2 * kP * 16;
+
+  const int t = threadIdx.x;
+  const int lane = t & 31;
+  const int64_t y = blockIdx.y;      // query row: cache group y / n_q
+  const int64_t gk = y / P.n_q;
+  const int64_t s0 = (int64_t)blockIdx.x * C::kRows;
+  const int n = (int)min((int64_t)C::kRows, P.seq_len - s0);
+  const int64_t row0 = gk * P.seq_len + s0;
+  const float inv_sqrt_d = 1.0f / sqrtf((float)D);
+  const float c0 = P.cb.c[0], dc = P.cb.c[1] - P.cb.c[0];
+
+  for (int i = t; i < D; i += NT) qt[i] = P.q[y * D + i] * P.d[i];
+  __syncthreads();
+  for (int h = 1; h < D; h <<= 1) {
+    for (int b = t; b < D / 2; b += NT) {
+      const int lo = (b / h) * 2 * h + (b % h);
+      const float a = qt[lo], c = qt[lo + h];
+      qt[lo] = a + c;
+      qt[lo + h] = a - c;
+    }
+    __syncthreads();
+  }
+  float qpart = 0.f;
+  for (int i = t; i < D; i += NT) {
+    qt[i] *= inv_sqrt_d;
+    qpart += qt[i];
+  }
+  const float Q = block_sum<NT>(qpart, red);
+  for (int e = t; e < 2 * kP * 16; e += NT) {  // layout [hi][nibble][pos]
+    const int hi = e / (kP * 16), nv = (e / kP) & 15, pos = e % kP;
+    float sm = 0.f;
+#pragma unroll
+    for (int k = 0; k < 4; ++k) sm += ((nv >> k) & 1) ? qt[8 * pos + 4 * hi + k] : 0.f;
+    nib[e] = sm;
+  }
+  __syncthreads();
+  for (int e = t; e < 256 * 32; e += NT) {
+    const int v = e >> 5, slot = e & 31, pos = slot % kP;
+    reinterpret_cast<float*>(tabb)[v * 64 + slot] =
+        nib[(v & 15) * kP + pos] + nib[kP * 16 + (v >> 4) * kP + pos];
+  }
+  __syncthreads();
+
+  const int rr = lane % kP;
+  const int wr = rr >> 2, bs = 8 * (rr & 3);
+  uint32_t slot4[kP / 4];  // byte (k & 3) of slot4[k >> 2] = 4 * slot(k)
+  static_for<kP / 4>([&](auto mc) {
+    constexpr int m = decltype(mc)::value;
+    uint32_t w = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      w |= (4u * (uint32_t)(((4 * m + j + lane) % kP) + kP * (lane / kP))) << (8 * j);
+    slot4[m] = w;
+  });
+
+  struct Row {
+    uint32_t c[kW], r[RES ? kW : 1];
+    float n, rn;
+  };
+  const int nb = (n + NT * B - 1) / (NT * B);
+  auto load_batch = [&](Row (&dst)[B], int bi) {
+#pragma unroll
+    for (int u = 0; u < B; ++u) {
+      const int ii = t + (bi * B + u) * NT;
+      const int64_t row = row0 + (ii < n ? ii : 0);
+      load_rotated_v3<D>(P.code + row * kW, wr, bs, dst[u].c);
+      dst[u].n = __ldg(P.norms + row);
+      if constexpr (RES) {
+        load_rotated_v3<D>(P.res + row * kW, wr, bs, dst[u].r);
+        dst[u].rn = __ldg(P.rnorms + row);
+      }
+    }
+  };
+  auto score_batch = [&](const Row (&src)[B], int bi) {
+#pragma unroll
+    for (int u = 0; u < B; ++u) {
+      float2 m = make_float2(0.f, 0.f);
+      static_for<kP>([&](auto kc) {
+        constexpr int k = decltype(kc)::value;
+        const float x1 = *reinterpret_cast<const float*>(
+            tabb + tab_addr<k & 3>(src[u].c[k >> 2], slot4[k >> 2]));
+        float x2 = 0.f;
+        if constexpr (RES)
+          x2 = *reinterpret_cast<const float*>(
+              tabb + tab_addr<k & 3>(src[u].r[k >> 2], slot4[k >> 2]));
+        m = __fadd2_rn(m, make_float2(x1, x2));
+      });
+      float sc = src[u].n * (c0 * Q + dc * m.x);
+      if constexpr (RES) sc += inv_sqrt_d * (2.f * m.y - Q) * src[u].rn;
+      const int ii = t + (bi * B + u) * NT;
+      if (ii < n) P.out[y * P.seq_len + s0 + ii] = sc;
+    }
+  };
+  Row a[2][B];
+  load_batch(a[0], 0);
+  for (int bi = 0; bi < nb; bi += 2) {
+    load_batch(a[1], bi + 1);
+    score_batch(a[0], bi);
+    if (bi + 1 < nb) {
+      load_batch(a[0], bi + 2);
+      score_batch(a[1], bi + 1);
+    }
+  }
+}
+
 }  // namespace
 
 kh_status launch_score(const float* q, int64_t n_groups, int n_q, int D,
@@ -152,6 +294,32 @@ kh_status launch_score(const float* q, int64_t n_groups, int n_q, int D,
   P.n_q = n_q;
   P.cb = cb;
   for (int i = 0; i < D; ++i) P.d[i] = d[i];
+  const char* env = getenv("KUDAHITAM_SCORE_PATH");
+  if (cb.n_c == 2 && !(env && strcmp(env, "direct") == 0)) {
+    // table-driven path: one CTA per (8192 cached rows, query row)
+    int dev = 0;
+    if (cudaGetDevice(&dev) != cudaSuccess) return KH_ECUDA;
+    const int64_t bxt = (seq_len + 8191) / 8192;
+    const int64_t rows_q = n_groups * (int64_t)n_q;
+    if (bxt > 0x7fffffff || rows_q >= 65536) return KH_EINVAL;
+    const dim3 gridt((unsigned)bxt, (unsigned)rows_q);
+    static std::once_flag once[4][64];
+    auto launch = [&](auto kern, int slot, int smem) {
+      std::call_once(once[slot][dev & 63], [&] {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+      });
+      kern<<<gridt, 256, smem, stream>>>(P);
+    };
+    const bool r = res != nullptr;
+    if (D == 128) {
+      if (r) launch(score_tab_kernel<128, true>, 0, ScoreTabCfg<128>::kSmem);
+      else launch(score_tab_kernel<128, false>, 1, ScoreTabCfg<128>::kSmem);
+    } else {
+      if (r) launch(score_tab_kernel<256, true>, 2, ScoreTabCfg<256>::kSmem);
+      else launch(score_tab_kernel<256, false>, 3, ScoreTabCfg<256>::kSmem);
+    }
+    return cudaGetLastError() == cudaSuccess ? KH_OK : KH_ELAUNCH;
+  }
   const int64_t bx = (seq_len + kScoreThreads - 1) / kScoreThreads;
   if (bx > 0x7fffffff) return KH_EINVAL;
   const dim3 grid((unsigned)bx, (unsigned)n_groups);

@@ -68,6 +68,28 @@ def test_scores_match_oracle(D, bits, residual):
     assert max(errs) < 1e-4, f"engine vs oracle: {errs}"
 
 
+@pytest.mark.parametrize("residual", [True, False])
+def test_table_scores_span_several_ctas_and_equal_direct_kernel(residual, monkeypatch):
+    """Groups longer than one table CTA (8192 rows) with a ragged tail, two
+    queries per group: the table-driven kernel against the direct
+    bit-select kernel and against the reference formula on the same cache."""
+    D, G, S, nq = 128, 2, 2 * 8192 + 1234, 2
+    d, c = rademacher(D, 4).numpy(), lloyd_max(1, D).numpy()
+    x = K.synth((1, G, S, D), dtype=torch.bfloat16, seed=12)
+    q = torch.randn(G, nq, D, generator=torch.Generator().manual_seed(2)).cuda()
+    p = ops.compress(x.cuda(), d, c, residual=residual)
+    tab = ops.score(q, p, d, c, seq_len=S).cpu().numpy()
+    monkeypatch.setenv("KUDAHITAM_SCORE_PATH", "direct")
+    direct = ops.score(q, p, d, c, seq_len=S).cpu().numpy()
+    m = ops.materialize(p, d, c)
+    own = O.score(q.cpu().numpy(), m["kmse"].cpu().numpy().reshape(G, S, D),
+                  m["signs"].cpu().numpy().reshape(G, S, D) if residual else None,
+                  p.rnorms.cpu().numpy().reshape(G, S) if residual else None, d)
+    for gi in range(G):
+        assert K.normwise(tab[gi], own[gi]) < 1e-4
+        assert K.normwise(tab[gi], direct[gi]) < 1e-5
+
+
 def test_gqa_scores_share_kv_heads():
     D, S = 128, 200
     comp = KudahitamCompressorV2(D, 1, seed=0)
