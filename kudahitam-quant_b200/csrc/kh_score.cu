@@ -153,7 +153,7 @@ struct ScoreTabCfg {
   static constexpr int kP = D / 8;
   static constexpr int kThreads = 256;
   static constexpr int kRows = 8192;   // cached rows per CTA
-  static constexpr int kBatch = 2;     // rows per thread in flight
+  static constexpr int kBatch = D == 128 ? 4 : 2;  // rows per thread in flight
   // table [256][64] | q~ [D] | nibble tables [2][16][kP] | reduction scratch [32]
   static constexpr int kSmem = (256 * 64 + D + 2 * kP * 16 + 32) * 4;
 };
