@@ -100,3 +100,29 @@ def test_other_entry_points_validate():
     assert L.kh_decode_attn(FAKE, 2, 128, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 100,
                             D128, D128, C2, 2, 0.1, 4, FAKE, 16, FAKE,
                             None) == _lib.KH_EINVAL  # workspace too small
+
+
+def test_gqa_decode_and_compat_scorer_validate():
+    L = _lib.lib()
+    args = (FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 100, 0, 100, D128, D128, C2, 2,
+            0.1, 2, FAKE, 2, 0, None)
+    assert L.kh_decode_partial_gqa(FAKE, 2, 0, 128, *args) == _lib.KH_EINVAL  # n_q < 1
+    assert L.kh_decode_partial_gqa(FAKE, 16384, 4, 128, *args) == _lib.KH_EINVAL  # grid.y
+    assert L.kh_decode_partial_gqa(FAKE, 0, 4, 128, *args) == _lib.KH_OK  # nothing to do
+    assert L.kh_decode_partial_gqa(FAKE, 2, 2, 96, *args) == _lib.KH_EINVAL  # head_dim
+    ok = dict(q=FAKE, H=2, D=128, S=10, kp=FAKE, sg=FAKE, d=FAKE, kn=FAKE, rn=FAKE, c=FAKE,
+              layer=0, mask=0)
+
+    def compat(**kw):
+        a = dict(ok)
+        a.update(kw)
+        return L.kh_score_packed_compat(a["q"], a["H"], a["D"], a["S"], a["kp"], a["sg"],
+                                        a["d"], a["kn"], a["rn"], a["c"], a["layer"],
+                                        a["mask"], 0.1, FAKE, None)
+    assert compat(D=96) == _lib.KH_EINVAL
+    assert compat(layer=-1) == _lib.KH_EINVAL
+    assert compat(H=0) == _lib.KH_OK
+    assert compat(S=0) == _lib.KH_OK
+    assert compat(kp=ctypes.c_void_p(0x10002)) == _lib.KH_EALIGN
+    assert compat(q=ctypes.c_void_p(0x10001)) == _lib.KH_EALIGN
+    assert compat(c=None) == _lib.KH_EINVAL
