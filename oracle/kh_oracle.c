@@ -11,9 +11,9 @@
  *              KudaHitamQuant_full.py:373-377 (with fwht() = the GPU
  *              `forward` kernel, i.e. orthonormal)
  *   compat   : fused_asymmetric_attention_packed_kernel,
- *              KudaHitamCUDA.cu:695-772 (packed-byte scorer); no golden
- *              vectors exist for it (the reference kernel needs a GPU and its
- *              callers need the HBBA encoder), so its parity is unpinned
+ *              KudaHitamCUDA.cu:695-772 (packed-byte scorer); pinned bit for
+ *              bit against the reference kernel itself on the GPU
+ *              (build_ref.py, tests/test_gpu_reference_kernels.py)
  *
  * Arithmetic follows the kernel in fp32 and in its order: the same
  * butterfly stage order, the same segmented shuffle-tree reductions, the

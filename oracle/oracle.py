@@ -222,3 +222,26 @@ def merge_partials(parts: np.ndarray) -> tuple[np.ndarray, np.ndarray, np.ndarra
     M = np.where(live, m, -np.inf).max(axis=1)
     e = np.where(live, np.exp(m - np.where(np.isfinite(M), M, 0.0)[:, None]), 0.0)
     return M, (l * e).sum(axis=1), (acc * e[..., None]).sum(axis=1)
+
+
+_ref_mod = None
+
+
+def reference_kernels():
+    """The reference's own CUDA kernels (KudaHitamCUDA.cu, built for sm_100a
+    by build_ref.py into _ref/kh_ref.so), or None when that build is absent.
+    Exposes ultra_fused_full_fusion (kernel v8), forward (FWHT) and
+    fused_asymmetric_attention, with the reference's argument conventions."""
+    global _ref_mod
+    if _ref_mod is None:
+        so = _DIR / "_ref" / "kh_ref.so"
+        if not so.exists():
+            return None
+        import importlib.util
+
+        import torch  # noqa: F401  (the module links against torch)
+        spec = importlib.util.spec_from_file_location("kh_ref", so)
+        mod = importlib.util.module_from_spec(spec)
+        spec.loader.exec_module(mod)
+        _ref_mod = mod
+    return _ref_mod

@@ -1,12 +1,12 @@
 """The reference's packed-byte scorer (fused_asymmetric_attention,
 KudaHitamCUDA.cu:695-797).
 
-No golden vectors exist for it: the reference kernel needs a GPU and its
-input encoder is the HBBA variant.  The oracle restates the kernel's own
-arithmetic (kh_oracle.c: khx_compat_score) and is checked here against an
-independent float64 evaluation of the kernel's formula; the engine must then
-equal the oracle bit for bit (same per-lane fused multiply-add order, same
-butterfly reduction)."""
+The oracle restates the kernel's own arithmetic (kh_oracle.c:
+khx_compat_score) and is checked here against an independent float64
+evaluation of the kernel's formula; the engine must equal the oracle bit for
+bit (same per-lane fused multiply-add order, same butterfly reduction).
+test_gpu_reference_kernels.py checks both against the reference kernel
+itself on the GPU."""
 import numpy as np
 import pytest
 import torch
