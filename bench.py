@@ -12,7 +12,9 @@ Also reported: decode attention over a 2-bit compressed cache (q bf16
 
 ``--impl reference`` times the reference algorithm's CPU implementation (the
 oracle port of KudaHitamCUDA.cu:13-195, OpenMP over every host thread) on a
-bounded sample of the same workload.
+bounded sample of the same workload; for context its line also carries the
+reference's own CUDA kernel v8 timed on this GPU on the same rows, when that
+kernel has been built from the reference source (oracle/build_ref.py).
 """
 from __future__ import annotations
 
@@ -222,7 +224,50 @@ def run_reference(args, world, rank):
             "cpu_baseline": {**vals[-1], "value": v},
             "e2e": {"value": v, "unit": "rows/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
+    gk = reference_kernel_on_gpu(args)
+    if gk is not None:
+        line["reference_kernel_v8_on_this_gpu"] = gk
     print(json.dumps(line), flush=True)
+
+
+def reference_kernel_on_gpu(args):
+    """For context: the reference's own CUDA kernel v8 (KudaHitamCUDA.cu:13-231,
+    built from the reference source into oracle/_ref) on this GPU, on the same
+    K and V rows, through its own launcher (which allocates the 6D+8 bytes per
+    row of reference-layout outputs each call).  None without a GPU or that
+    build."""
+    if not torch.cuda.is_available():
+        return None
+    from oracle import oracle as O
+    ref = O.reference_kernels()
+    if ref is None:
+        return None
+    from kudahitam.codebook import lloyd_max, rademacher
+    dev = torch.device("cuda", 0)
+    k, v = synth_kv(2, dev)
+    rows = [t.reshape(-1, D).contiguous() for t in (k, v)]
+    assert (rows[0].shape[0] * D) % 2048 == 0  # the kernel is only safe on whole blocks
+    d, c = rademacher(D, 1).to(dev), lloyd_max(1, D).to(dev)
+    stream = torch.cuda.current_stream(dev)
+
+    def step():
+        for r in rows:
+            ref.ultra_fused_full_fusion(r, d, c)
+
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    ms = statistics.median(time_loop(step, max(5, min(args.steps, 20)), stream))
+    n = 2 * rows[0].shape[0]
+    peak, _ = peaks()
+    moved = n * (D * 2 + 6 * D + 8)
+    out = {"rows_per_s": n / (ms / 1e3), "ms_per_step": ms,
+           "bytes_per_row": D * 2 + 6 * D + 8, "gbs": moved / (ms / 1e3) / 1e9,
+           "frac_of_measured_hbm": moved / (ms / 1e3) / 1e9 / peak,
+           "note": "reference kernel v8 with its own launcher, same K and V fp16 rows"}
+    del k, v, rows
+    torch.cuda.empty_cache()
+    return out
 
 
 def workload_config(world: int) -> dict:
