@@ -47,11 +47,11 @@ FALLBACK_HBM_GBS = 6650.0
 
 # dram__bytes_read.sum + dram__bytes_write.sum per compressed row, from the ncu
 # capture in profiles/compress_tc_fp16_d256_2bit.md (524,288 rows of the same
-# row format): 268.52 MB read + 8.86 MB written.  Reads equal the algorithmic
+# row format): 268.48 MB read + 8.79 MB written.  Reads equal the algorithmic
 # bytes; most of the packed output is still in L2 when the kernel ends, so
 # the DRAM write count is below the 72 B/row written.  Traffic grows in
 # proportion to the rows, so it is scaled to a full launch.
-NCU_TRAFFIC_BYTES_PER_ROW = (268.516096e6 + 8.860672e6) / 524288
+NCU_TRAFFIC_BYTES_PER_ROW = (268.480256e6 + 8.786688e6) / 524288
 # Same for the decode step (profiles/decode_v3_q32x16_s40000.md): bytes per
 # cached row of K and V, on the bench's decode workload itself.
 NCU_DECODE_TRAFFIC_BYTES_PER_ROW = (1.755635e9 + 5.170176e6) / (512 * 40000)

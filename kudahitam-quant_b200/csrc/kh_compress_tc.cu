@@ -122,15 +122,12 @@ struct TcCfg {
   static constexpr uint32_t kTmemCols = 2 * kAccCols;
   static constexpr int kThreads = 320;
   static constexpr int kBarOff = kStages * kChunkBytes + kNB * kBMatBytes;
-  // barriers and the tensor-memory slot
-  static constexpr int kXchOff = kBarOff + (2 * kStages + 4) * 8 + 16;
-  static constexpr int kSmem = 1024 + kXchOff;
+  // then the barriers and the tensor-memory slot; 1024 bytes of slack align
+  // the stage ring to the 128B swizzle's 1024-byte atom
+  static constexpr int kEndOff = kBarOff + (2 * kStages + 4) * 8 + 16;
+  static constexpr int kSmem = 1024 + kEndOff;
   static_assert(kSmem <= 232448, "exceeds the 227 KB of shared memory a CTA can use");
 };
-
-__device__ __forceinline__ void named_bar_sync(int id, int n) {
-  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(n) : "memory");
-}
 
 // Store this row's packed words w[0..n) at dst (16-byte vectors when possible).
 template <int N>
