@@ -92,18 +92,40 @@ __device__ __forceinline__ uint32_t tab_addr(uint32_t x, uint32_t slots) {
   return r;
 }
 
-// Rotated plane load for row-per-thread table lookups.  D = 128: one 16-byte load per row (4 L1 wavefronts per
-// warp instead of 16 for four rotated 4-byte loads), rotated in registers:
-// words by wr (two select stages), then bytes by bs (funnel shifts).
-// D = 256: rotated 4-byte loads as in v2.
+// Row-per-thread table lookups read a plane in two steps, so that the
+// rotation's data-dependent instructions run where the bytes are used, one
+// batch after the load was issued, and never stall the loads behind them.
+// load_plane: D = 128, one 16-byte load per row (4 L1 wavefronts per warp
+// instead of 16 for four 4-byte loads); D = 256, eight 4-byte loads whose
+// word order is already rotated by wr through the addresses.
 template <int D>
-__device__ __forceinline__ void load_rotated_v3(const uint32_t* __restrict__ plane, int wr,
-                                                int bs, uint32_t (&rot)[D / 32]) {
+__device__ __forceinline__ void load_plane(const uint32_t* __restrict__ plane, int wr,
+                                           uint32_t (&w)[D / 32]) {
   if constexpr (D == 128) {
     const uint4 v = __ldg(reinterpret_cast<const uint4*>(plane));
+    w[0] = v.x;
+    w[1] = v.y;
+    w[2] = v.z;
+    w[3] = v.w;
+  } else {
+    constexpr int kW = D / 32;
+    static_for<kW>([&](auto ic) {
+      constexpr int i = decltype(ic)::value;
+      w[i] = __ldg(plane + ((i + wr) & (kW - 1)));
+    });
+  }
+}
+
+// rotate_plane: the rotated view of a plane read by load_plane (byte k =
+// plane byte (k + r) mod P, r = 4 wr + bs / 8).  D = 128 rotates the words
+// by wr here (two select stages); both then shift by bs bits.
+template <int D>
+__device__ __forceinline__ void rotate_plane(const uint32_t (&w)[D / 32], int wr, int bs,
+                                             uint32_t (&rot)[D / 32]) {
+  if constexpr (D == 128) {
     const bool h = wr & 2, o = wr & 1;
-    const uint32_t y0 = h ? v.z : v.x, y1 = h ? v.w : v.y;
-    const uint32_t y2 = h ? v.x : v.z, y3 = h ? v.y : v.w;
+    const uint32_t y0 = h ? w[2] : w[0], y1 = h ? w[3] : w[1];
+    const uint32_t y2 = h ? w[0] : w[2], y3 = h ? w[1] : w[3];
     const uint32_t z0 = o ? y1 : y0, z1 = o ? y2 : y1;
     const uint32_t z2 = o ? y3 : y2, z3 = o ? y0 : y3;
     rot[0] = __funnelshift_r(z0, z1, bs);
@@ -111,7 +133,11 @@ __device__ __forceinline__ void load_rotated_v3(const uint32_t* __restrict__ pla
     rot[2] = __funnelshift_r(z2, z3, bs);
     rot[3] = __funnelshift_r(z3, z0, bs);
   } else {
-    load_rotated<D>(plane, wr, bs, rot);
+    constexpr int kW = D / 32;
+    static_for<kW>([&](auto ic) {
+      constexpr int i = decltype(ic)::value;
+      rot[i] = __funnelshift_r(w[i], w[(i + 1) % kW], bs);
+    });
   }
 }
 

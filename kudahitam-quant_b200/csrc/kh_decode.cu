@@ -508,8 +508,8 @@ template <int D>
 __device__ __forceinline__ void load_k_row(const DecodeParams& P, int64_t row, int wr, int bs,
                                            RowKV<D>& a) {
   constexpr int kW = D / 32;
-  load_rotated_v3<D>(P.k_code + row * kW, wr, bs, a.c);
-  load_rotated_v3<D>(P.k_res + row * kW, wr, bs, a.r);
+  load_plane<D>(P.k_code + row * kW, wr, a.c);
+  load_plane<D>(P.k_res + row * kW, wr, a.r);
   a.n = __ldg(P.k_norms + row);
   a.rn = __ldg(P.k_rnorms + row);
   a.vn = __ldg(P.v_norms + row);
@@ -520,8 +520,8 @@ template <int D>
 __device__ __forceinline__ void load_v_row(const DecodeParams& P, int64_t row, int wr, int bs,
                                            RowK<D>& a) {
   constexpr int kW = D / 32;
-  load_rotated_v3<D>(P.v_code + row * kW, wr, bs, a.c);
-  load_rotated_v3<D>(P.v_res + row * kW, wr, bs, a.r);
+  load_plane<D>(P.v_code + row * kW, wr, a.c);
+  load_plane<D>(P.v_res + row * kW, wr, a.r);
 }
 
 template <int NT>
@@ -654,12 +654,15 @@ __global__ void __launch_bounds__(256, 2)
 #pragma unroll
         for (int u = 0; u < B; ++u) {
           float2 m = make_float2(0.f, 0.f);
+          uint32_t rc[D / 32], rs[D / 32];
+          rotate_plane<D>(src[u].c, wr, bs, rc);
+          rotate_plane<D>(src[u].r, wr, bs, rs);
           static_for<kP>([&](auto kc) {
             constexpr int k = decltype(kc)::value;
             const float x1 = *reinterpret_cast<const float*>(
-                tabb + tab_addr<k & 3>(src[u].c[k >> 2], slot4[k >> 2]));
+                tabb + tab_addr<k & 3>(rc[k >> 2], slot4[k >> 2]));
             const float x2 = *reinterpret_cast<const float*>(
-                tabb + tab_addr<k & 3>(src[u].r[k >> 2], slot4[k >> 2]));
+                tabb + tab_addr<k & 3>(rs[k >> 2], slot4[k >> 2]));
             m = __fadd2_rn(m, make_float2(x1, x2));
           });
           const float score = src[u].n * (P.c0 * Q + dc * m.x) +
@@ -739,12 +742,15 @@ __global__ void __launch_bounds__(256, 2)
           const int f1 = __float2int_rn(p * src[u].n * k1);
           const int f2 = __float2int_rn(p * src[u].rn * k2);
           csum += (float)f1 * c0dc - 0.5f * (float)f2;
+          uint32_t rc[D / 32], rs[D / 32];
+          rotate_plane<D>(src[u].c, wr, bs, rc);
+          rotate_plane<D>(src[u].r, wr, bs, rs);
           static_for<kP>([&](auto kc) {
             constexpr int k = decltype(kc)::value;
-            atomicAdd(reinterpret_cast<int*>(tabb + tab_addr<k & 3>(src[u].c[k >> 2], slot4[k >> 2])),
+            atomicAdd(reinterpret_cast<int*>(tabb + tab_addr<k & 3>(rc[k >> 2], slot4[k >> 2])),
                       f1);
             atomicAdd(reinterpret_cast<int*>(tabb + 128 +
-                                             tab_addr<k & 3>(src[u].r[k >> 2], slot4[k >> 2])),
+                                             tab_addr<k & 3>(rs[k >> 2], slot4[k >> 2])),
                       f2);
           });
         }

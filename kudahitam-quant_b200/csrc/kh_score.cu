@@ -236,10 +236,10 @@ __global__ void __launch_bounds__(256, 2)
     for (int u = 0; u < B; ++u) {
       const int ii = t + (bi * B + u) * NT;
       const int64_t row = row0 + (ii < n ? ii : 0);
-      load_rotated_v3<D>(P.code + row * kW, wr, bs, dst[u].c);
+      load_plane<D>(P.code + row * kW, wr, dst[u].c);
       dst[u].n = __ldg(P.norms + row);
       if constexpr (RES) {
-        load_rotated_v3<D>(P.res + row * kW, wr, bs, dst[u].r);
+        load_plane<D>(P.res + row * kW, wr, dst[u].r);
         dst[u].rn = __ldg(P.rnorms + row);
       }
     }
@@ -248,14 +248,17 @@ __global__ void __launch_bounds__(256, 2)
 #pragma unroll
     for (int u = 0; u < B; ++u) {
       float2 m = make_float2(0.f, 0.f);
+      uint32_t rc[kW], rs[RES ? kW : 1];
+      rotate_plane<D>(src[u].c, wr, bs, rc);
+      if constexpr (RES) rotate_plane<D>(src[u].r, wr, bs, rs);
       static_for<kP>([&](auto kc) {
         constexpr int k = decltype(kc)::value;
         const float x1 = *reinterpret_cast<const float*>(
-            tabb + tab_addr<k & 3>(src[u].c[k >> 2], slot4[k >> 2]));
+            tabb + tab_addr<k & 3>(rc[k >> 2], slot4[k >> 2]));
         float x2 = 0.f;
         if constexpr (RES)
           x2 = *reinterpret_cast<const float*>(
-              tabb + tab_addr<k & 3>(src[u].r[k >> 2], slot4[k >> 2]));
+              tabb + tab_addr<k & 3>(rs[k >> 2], slot4[k >> 2]));
         m = __fadd2_rn(m, make_float2(x1, x2));
       });
       float sc = src[u].n * (c0 * Q + dc * m.x);
