@@ -476,7 +476,7 @@ __global__ void __launch_bounds__(256)
 // prefetches of the rows a few batches ahead were measured slower.)
 // Build-time tuning knobs of decode v3 (defaults are the measured best).
 #ifndef KH_DECODE_SEG
-#define KH_DECODE_SEG 8192
+#define KH_DECODE_SEG 4096
 #endif
 #ifndef KH_DECODE_BATCH128
 #define KH_DECODE_BATCH128 2
@@ -485,15 +485,21 @@ __global__ void __launch_bounds__(256)
 template <int D>
 struct V3Cfg {
   static constexpr int kP = D / 8;
-  static constexpr int kCopies = 32 / kP;
+  static constexpr int kCopies = 32 / kP;  // K-table copies (bank-conflict-free slots)
+  static_assert(kCopies * kP == 32, "32 slots per table row");
   static constexpr int kThreads = 256;
-  static constexpr int kSeg = KH_DECODE_SEG;
+  // D = 128: the K table and both V histograms fit in words 0..31 of every
+  // 64-word table row (half-row layout); words 32..63 of the 256 rows hold
+  // the segment's logits (8192) in phase 1 and the fold partials after
+  // phase 2.  D = 256 needs all 64 words for its two V histograms.
+  static constexpr bool kHalf = D == 128;
+  static constexpr int kSeg = kHalf ? 8192 : KH_DECODE_SEG;
   static constexpr int kBatch = D == 128 ? KH_DECODE_BATCH128 : 1;  // rows per thread in flight
-  // tab [256][64] | logits [kSeg] | fold partials [2][4][32][8] | q~ [D] |
-  // nibble tables [2][kP][16] | reduction scratch [64]
+  // tab [256][64] | (D = 256: logits [kSeg] | fold partials [2][4][32][8]) |
+  // q~ [D] | nibble tables [2][kP][16] | reduction scratch [64]
   static constexpr int kTabWords = 256 * 64;
   static constexpr int kSmem =
-      (kTabWords + kSeg + 2048 + D + 2 * kP * 16 + 64) * 4;
+      (kTabWords + (kHalf ? 0 : kSeg + 2048) + D + 2 * kP * 16 + 64) * 4;
 };
 
 
@@ -514,14 +520,6 @@ __device__ __forceinline__ void load_k_row(const DecodeParams& P, int64_t row, i
   a.rn = __ldg(P.k_rnorms + row);
   a.vn = __ldg(P.v_norms + row);
   a.vrn = __ldg(P.v_rnorms + row);
-}
-
-template <int D>
-__device__ __forceinline__ void load_v_row(const DecodeParams& P, int64_t row, int wr, int bs,
-                                           RowK<D>& a) {
-  constexpr int kW = D / 32;
-  load_plane<D>(P.v_code + row * kW, wr, a.c);
-  load_plane<D>(P.v_res + row * kW, wr, a.r);
 }
 
 template <int NT>
@@ -557,9 +555,18 @@ __global__ void __launch_bounds__(256, 2)
   constexpr float kLn2 = 0.6931471805599453f;
   extern __shared__ __align__(16) unsigned char smem_raw[];
   unsigned char* tabb = smem_raw;                                    // [256][64] words
-  float* lg = reinterpret_cast<float*>(smem_raw) + C::kTabWords;    // [kSeg]
-  int* part = reinterpret_cast<int*>(lg + C::kSeg);                 // [2][4][32][8]
-  float* qt = reinterpret_cast<float*>(part + 2048);                // [D]
+  float* lg = reinterpret_cast<float*>(smem_raw) + C::kTabWords;    // [kSeg] (D = 256)
+  int* part = reinterpret_cast<int*>(lg + (C::kHalf ? 0 : C::kSeg));  // [2048] (D = 256)
+  float* qt = reinterpret_cast<float*>(part + (C::kHalf ? 0 : 2048));  // [D]
+  // element e of the logits / fold partials: half-row layout puts it in word
+  // 32 + (e mod 32) of table row e / 32 (a warp's 32 consecutive elements
+  // fill one half row: conflict-free)
+  auto upper = [&](int e) -> int* {
+    if constexpr (C::kHalf)
+      return reinterpret_cast<int*>(tabb + 256 * (e >> 5) + 128 + 4 * (e & 31));
+    else
+      return part + e;
+  };
   float* nib = qt + D;                                               // [2][kP][16]
   float* red = nib + 2 * kP * 16;                                    // [64]
 
@@ -619,6 +626,23 @@ __global__ void __launch_bounds__(256, 2)
     slot4[m] = w;
   });
 
+  // phase-2 plane order.  Half-row layout: the code-plane histogram is slots
+  // pos, the residual one slots 16 + pos (one copy each); lanes 0..15
+  // scatter the code plane with the first atomic of each byte step and lanes
+  // 16..31 the residual plane, then the other way round, so every atomic
+  // instruction of a warp touches 32 distinct banks.  D = 256: all lanes
+  // code plane first (slots 0..31), residual plane second (slots 32..63).
+  const bool swap = C::kHalf && lane >= 16;
+  const uint32_t* vx = swap ? P.v_res : P.v_code;
+  const uint32_t* vy = swap ? P.v_code : P.v_res;
+  const float* vxn = swap ? P.v_rnorms : P.v_norms;
+  const float* vyn = swap ? P.v_norms : P.v_rnorms;
+  uint32_t slot4y[kP / 4];  // slots of the second atomic (half-row layout)
+  static_for<kP / 4>([&](auto mc) {
+    constexpr int m = decltype(mc)::value;
+    slot4y[m] = slot4[m] ^ 0x40404040u;  // 4 * (slot +- 16) in every byte
+  });
+
   float m_run = -INFINITY, l_run = 0.f, c_run = 0.f, acc = 0.f;
 
   for (int64_t c0 = s0; c0 < s1; c0 += C::kSeg) {
@@ -669,7 +693,12 @@ __global__ void __launch_bounds__(256, 2)
                               inv_sqrt_d * (2.f * m.y - Q) * src[u].rn;
           const int ii = t + (bi * B + u) * NT;
           l2[u] = ii < n ? score * lscale : -INFINITY;
-          if (ii < n) lg[ii] = l2[u];
+          if (ii < n) {
+            if constexpr (C::kHalf)
+              *reinterpret_cast<float*>(upper(ii)) = l2[u];
+            else
+              lg[ii] = l2[u];
+          }
           mb = fmaxf(mb, l2[u]);
         }
         if (mb > -INFINITY) {
@@ -703,9 +732,10 @@ __global__ void __launch_bounds__(256, 2)
       for (int u = 0; u < B; ++u) {
         const int ii = t + (bi * B + u) * NT;
         const int64_t row = row0 + (ii < n ? ii : 0);
-        load_v_row<D>(P, row, wr, bs, dst[u]);
-        dst[u].n = __ldg(P.v_norms + row);
-        dst[u].rn = __ldg(P.v_rnorms + row);
+        load_plane<D>(vx + row * (D / 32), wr, dst[u].c);
+        load_plane<D>(vy + row * (D / 32), wr, dst[u].r);
+        dst[u].n = __ldg(vxn + row);
+        dst[u].rn = __ldg(vyn + row);
       }
     };
     load_vbatch(va[0], 0);
@@ -714,10 +744,15 @@ __global__ void __launch_bounds__(256, 2)
     const float alpha = exp2f(m_run - m_new);  // 0 on the first segment
     m_run = m_new;
 
-    // zero both histograms (all 64 entries of every row)
+    // zero both histograms (D = 128: words 0..31 of every row, keeping the
+    // logits; D = 256: all 64 words)
     {
       int4* z = reinterpret_cast<int4*>(tabb);
-      for (int e = t; e < C::kTabWords / 4; e += NT) z[e] = make_int4(0, 0, 0, 0);
+      if constexpr (C::kHalf) {
+        for (int e = t; e < C::kTabWords / 8; e += NT) z[(e >> 3) * 16 + (e & 7)] = make_int4(0, 0, 0, 0);
+      } else {
+        for (int e = t; e < C::kTabWords / 4; e += NT) z[e] = make_int4(0, 0, 0, 0);
+      }
     }
     {
       const float r = mt > -INFINITY ? exp2f(mt - m_new) : 0.f;
@@ -732,26 +767,37 @@ __global__ void __launch_bounds__(256, 2)
     // ---------------- phase 2b: scatter V bytes with fixed-point weights
     float csum = 0.f;  // constant term in quanta
     const float k1 = wa * scale_inv, k2 = wb * scale_inv;
+    const float kx = swap ? k2 : k1, ky = swap ? k1 : k2;           // (x, y) = this lane's
+    const float cx = swap ? -0.5f : c0dc, cy = swap ? c0dc : -0.5f;  // plane order
     {
       auto scatter_batch = [&](const RowK<D>(&src)[B], int bi) {
 #pragma unroll
         for (int u = 0; u < B; ++u) {
           const int ii = t + (bi * B + u) * NT;
           const bool ok = ii < n;
-          const float p = ok ? exp2f(lg[ok ? ii : 0] - m_new) : 0.f;
-          const int f1 = __float2int_rn(p * src[u].n * k1);
-          const int f2 = __float2int_rn(p * src[u].rn * k2);
-          csum += (float)f1 * c0dc - 0.5f * (float)f2;
-          uint32_t rc[D / 32], rs[D / 32];
-          rotate_plane<D>(src[u].c, wr, bs, rc);
-          rotate_plane<D>(src[u].r, wr, bs, rs);
+          float l2;
+          if constexpr (C::kHalf)
+            l2 = *reinterpret_cast<const float*>(upper(ok ? ii : 0));
+          else
+            l2 = lg[ok ? ii : 0];
+          const float p = ok ? exp2f(l2 - m_new) : 0.f;
+          const int fx = __float2int_rn(p * src[u].n * kx);
+          const int fy = __float2int_rn(p * src[u].rn * ky);
+          csum += (float)fx * cx + (float)fy * cy;
+          uint32_t rx[D / 32], ry[D / 32];
+          rotate_plane<D>(src[u].c, wr, bs, rx);
+          rotate_plane<D>(src[u].r, wr, bs, ry);
           static_for<kP>([&](auto kc) {
             constexpr int k = decltype(kc)::value;
-            atomicAdd(reinterpret_cast<int*>(tabb + tab_addr<k & 3>(rc[k >> 2], slot4[k >> 2])),
-                      f1);
-            atomicAdd(reinterpret_cast<int*>(tabb + 128 +
-                                             tab_addr<k & 3>(rs[k >> 2], slot4[k >> 2])),
-                      f2);
+            atomicAdd(reinterpret_cast<int*>(tabb + tab_addr<k & 3>(rx[k >> 2], slot4[k >> 2])),
+                      fx);
+            if constexpr (C::kHalf)
+              atomicAdd(reinterpret_cast<int*>(tabb + tab_addr<k & 3>(ry[k >> 2], slot4y[k >> 2])),
+                        fy);
+            else
+              atomicAdd(reinterpret_cast<int*>(tabb + 128 +
+                                               tab_addr<k & 3>(ry[k >> 2], slot4[k >> 2])),
+                        fy);
           });
         }
       };
@@ -766,9 +812,33 @@ __global__ void __launch_bounds__(256, 2)
     }
     const float c_c = block_sum<NT>(csum, red) * scale;  // also fences the histograms
 
-    // ---------------- fold: thread (plane, quarter, slot) sums its 64 bins
-    // per bit of the byte value; bits 6, 7 of v are the quarter's bits
-    {
+    // ---------------- fold.  Half-row layout: thread (group of 32 byte
+    // values, slot) sums its 32 bins per bit of the byte value; bits 5..7 of
+    // v are the group's bits.
+    if constexpr (C::kHalf) {
+      const int slot = t & 31, grp = t >> 5;
+      const int* hb = reinterpret_cast<const int*>(tabb) + slot;
+      int sb[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+      int tt = 0;
+      static_for<32>([&](auto jc) {
+        constexpr int j = decltype(jc)::value;
+        const int h = hb[(32 * grp + j) * 64];
+        tt += h;
+        if (j & 1) sb[0] += h;
+        if (j & 2) sb[1] += h;
+        if (j & 4) sb[2] += h;
+        if (j & 8) sb[3] += h;
+        if (j & 16) sb[4] += h;
+      });
+      sb[5] = (grp & 1) ? tt : 0;
+      sb[6] = (grp & 2) ? tt : 0;
+      sb[7] = (grp & 4) ? tt : 0;
+      int4* pp = reinterpret_cast<int4*>(upper((grp * 32 + slot) * 8));
+      pp[0] = make_int4(sb[0], sb[1], sb[2], sb[3]);
+      pp[1] = make_int4(sb[4], sb[5], sb[6], sb[7]);
+    } else {
+      // D = 256: thread (plane, quarter, slot) sums its 64 bins; bits 6, 7
+      // of v are the quarter's bits
       const int slot = t & 31, pl = (t >> 5) & 1, q = t >> 6;
       const int* hb = reinterpret_cast<const int*>(tabb) + 32 * pl + slot;
       int sb[8] = {0, 0, 0, 0, 0, 0, 0, 0};
@@ -794,15 +864,25 @@ __global__ void __launch_bounds__(256, 2)
     if (t < D) {
       const int pos = t >> 3, bb = t & 7;
       float a = 0.f;
+      if constexpr (C::kHalf) {
+        int sc = 0, sr = 0;  // one plane each: a subset sum of one histogram, < 2^31
 #pragma unroll
-      for (int pl = 0; pl < 2; ++pl) {
-        int s = 0;  // one plane: a subset sum of one histogram, < 2^31
+        for (int grp = 0; grp < 8; ++grp) {
+          sc += *upper((grp * 32 + pos) * 8 + bb);
+          sr += *upper((grp * 32 + 16 + pos) * 8 + bb);
+        }
+        a = (float)sc + (float)sr;
+      } else {
 #pragma unroll
-        for (int q = 0; q < 4; ++q)
+        for (int pl = 0; pl < 2; ++pl) {
+          int s = 0;  // one plane: a subset sum of one histogram, < 2^31
 #pragma unroll
-          for (int cp = 0; cp < C::kCopies; ++cp)
-            s += part[((pl * 4 + q) * 32 + pos + kP * cp) * 8 + bb];
-        a += (float)s;
+          for (int q = 0; q < 4; ++q)
+#pragma unroll
+            for (int cp = 0; cp < C::kCopies; ++cp)
+              s += part[((pl * 4 + q) * 32 + pos + kP * cp) * 8 + bb];
+          a += (float)s;
+        }
       }
       acc = acc * alpha + a * scale;
     }
