@@ -496,10 +496,9 @@ struct V3Cfg {
   static constexpr int kSeg = kHalf ? 8192 : KH_DECODE_SEG;
   static constexpr int kBatch = D == 128 ? KH_DECODE_BATCH128 : 1;  // rows per thread in flight
   // tab [256][64] | (D = 256: logits [kSeg] | fold partials [2][4][32][8]) |
-  // q~ [D] | nibble tables [2][kP][16] | reduction scratch [64]
+  // q~ [D] | reduction scratch [64]
   static constexpr int kTabWords = 256 * 64;
-  static constexpr int kSmem =
-      (kTabWords + (kHalf ? 0 : kSeg + 2048) + D + 2 * kP * 16 + 64) * 4;
+  static constexpr int kSmem = (kTabWords + (kHalf ? 0 : kSeg + 2048) + D + 64) * 4;
 };
 
 
@@ -567,8 +566,7 @@ __global__ void __launch_bounds__(256, 2)
     else
       return part + e;
   };
-  float* nib = qt + D;                                               // [2][kP][16]
-  float* red = nib + 2 * kP * 16;                                    // [64]
+  float* red = qt + D;                                               // [64]
 
   const int t = threadIdx.x;
   const int lane = t & 31;
@@ -585,7 +583,7 @@ __global__ void __launch_bounds__(256, 2)
   const float c0dc = P.c0 / dc;
   const float wa = inv_sqrt_d * dc, wb = 2.f * qjl;  // V weight = p (wa |v| + wb r_norm)
 
-  // q~ = H(q (.) d) / sqrt(D) and its nibble partial-sum tables
+  // q~ = H(q (.) d) / sqrt(D)
   for (int i = t; i < D; i += NT) qt[i] = P.q[g * D + i] * P.dk[i];
   __syncthreads();
   for (int h = 1; h < D; h <<= 1) {
@@ -603,14 +601,6 @@ __global__ void __launch_bounds__(256, 2)
     qpart += qt[i];
   }
   const float Q = block_sum<NT>(qpart, red);  // (its barriers also publish qt)
-  for (int e = t; e < 2 * kP * 16; e += NT) {  // layout [hi][nibble][pos]
-    const int hi = e / (kP * 16), nv = (e / kP) & 15, pos = e % kP;
-    float s = 0.f;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) s += ((nv >> k) & 1) ? qt[8 * pos + 4 * hi + k] : 0.f;
-    nib[e] = s;
-  }
-  __syncthreads();
 
   // lane constants: byte k of a rotated plane is plane byte (k + rr) mod kP,
   // looked up in slot ((k + lane) mod kP) + kP (lane / kP)
@@ -651,11 +641,31 @@ __global__ void __launch_bounds__(256, 2)
     const int nb = (n + NT * B - 1) / (NT * B);  // batches of B rows per thread
 
     // K table into entries 0..31 of every row: T[v][slot] = sum of q~ over
-    // the set bits of v at the slot's byte position
-    for (int e = t; e < 256 * 32; e += NT) {
-      const int v = e >> 5, slot = e & 31, pos = slot % kP;
-      reinterpret_cast<float*>(tabb)[v * 64 + slot] =
-          nib[(v & 15) * kP + pos] + nib[kP * 16 + (v >> 4) * kP + pos];
+    // the set bits of v at the slot's byte position.  Thread t fills slot
+    // t mod 32 for the byte values v = t / 32 + 8 k (k < 32): the low nibble
+    // of v is t / 32 + 8 (k mod 2), the high nibble k / 2.
+    {
+      const int slot = t & 31, pos = slot % kP, w = t >> 5;
+      float qb[8];
+#pragma unroll
+      for (int b = 0; b < 8; ++b) qb[b] = qt[8 * pos + b];
+      float lo[2];
+#pragma unroll
+      for (int h = 0; h < 2; ++h) {
+        const int nv = w + 8 * h;
+        lo[h] = ((nv & 1) ? qb[0] : 0.f) + ((nv & 2) ? qb[1] : 0.f) +
+                ((nv & 4) ? qb[2] : 0.f) + ((nv & 8) ? qb[3] : 0.f);
+      }
+      float* tf = reinterpret_cast<float*>(tabb) + slot;
+      static_for<32>([&](auto kc) {
+        constexpr int k = decltype(kc)::value, hv = k >> 1;
+        float hi = 0.f;
+        if constexpr ((hv & 1) != 0) hi += qb[4];
+        if constexpr ((hv & 2) != 0) hi += qb[5];
+        if constexpr ((hv & 4) != 0) hi += qb[6];
+        if constexpr ((hv & 8) != 0) hi += qb[7];
+        tf[(w + 8 * k) * 64] = lo[k & 1] + hi;
+      });
     }
     __syncthreads();
 
