@@ -78,6 +78,37 @@ __device__ __forceinline__ float block_max(float v, float* red) {
 }
 
 
+// Fills entries 0..31 of the 256 table rows (row stride 64 floats):
+// T[v][slot] = sum of q~ over the set bits of byte value v at the slot's
+// byte position slot mod (D / 8).  Thread t of a 256-thread block fills slot
+// t mod 32 for the byte values v = t / 32 + 8 k (k < 32): the low nibble of
+// v is t / 32 + 8 (k mod 2), the high nibble k / 2; the eight q~ elements of
+// the byte position stay in registers.
+template <int D>
+__device__ __forceinline__ void build_byte_table(float* tab, const float* qt, int t) {
+  const int slot = t & 31, pos = slot % (D / 8), w = t >> 5;
+  float qb[8];
+#pragma unroll
+  for (int b = 0; b < 8; ++b) qb[b] = qt[8 * pos + b];
+  float lo[2];
+#pragma unroll
+  for (int h = 0; h < 2; ++h) {
+    const int nv = w + 8 * h;
+    lo[h] = ((nv & 1) ? qb[0] : 0.f) + ((nv & 2) ? qb[1] : 0.f) +
+            ((nv & 4) ? qb[2] : 0.f) + ((nv & 8) ? qb[3] : 0.f);
+  }
+  float* tf = tab + slot;
+  static_for<32>([&](auto kc) {
+    constexpr int k = decltype(kc)::value, hv = k >> 1;
+    float hi = 0.f;
+    if constexpr ((hv & 1) != 0) hi += qb[4];
+    if constexpr ((hv & 2) != 0) hi += qb[5];
+    if constexpr ((hv & 4) != 0) hi += qb[6];
+    if constexpr ((hv & 8) != 0) hi += qb[7];
+    tf[(w + 8 * k) * 64] = lo[k & 1] + hi;
+  });
+}
+
 // Byte address 256 * (byte B of x) + (byte B of slots): one byte-permute.
 // slots packs four lane slot offsets (each 4 * slot < 128) one per byte;
 // result bytes 2 and 3 replicate the (zero) sign bit of the slot byte.

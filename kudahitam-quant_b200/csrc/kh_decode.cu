@@ -466,14 +466,24 @@ __global__ void __launch_bounds__(256)
 //            fixed-point scale 2^30 / sum(weights) (any bin <= 2^30 + n/2);
 //   fold     histograms -> D accumulators, rescaled online across segments.
 // Table and histograms share one array of 256 rows (one per byte value) of
-// 64 32-bit entries: the K table uses entries 0..31 during phase 1, the two V
-// histograms entries 0..31 (code plane) and 32..63 (residual plane) during
-// phase 2.  Row v starts at byte 256 v, so one byte-permute of (plane word,
-// lane slot offset) yields the byte address 256 v + 4 slot, and the residual
-// histogram is the same address + 128 (an immediate).  Slots follow the
-// conflict-free rotation described for v2.  The next rows' plane words are
-// loaded while the current rows are scored / scattered.  (Bulk L2
-// prefetches of the rows a few batches ahead were measured slower.)
+// 64 32-bit entries; row v starts at byte 256 v, so one byte-permute of
+// (plane word, lane slot offset) yields the byte address 256 v + 4 slot.
+// Slots follow the conflict-free rotation described for v2.
+//   D = 128 (half-row layout): the K table (two copies of 16 positions) and
+//     the two V histograms (one copy each: code plane slots 0..15, residual
+//     plane 16..31) use entries 0..31; half the lanes scatter the residual
+//     plane first, so each atomic instruction of a warp still covers 32
+//     banks.  Entries 32..63 hold the segment's 8192 logits during phases 1
+//     and 2, then the fold partials.  65 KB of shared memory per CTA leaves
+//     two CTAs per SM with the L1 room their in-flight row loads need (the
+//     same kernel with 109 KB of shared memory ran 20 % slower).
+//   D = 256: the K table uses entries 0..31, the V histograms 0..31 (code
+//     plane) and 32..63 (residual plane, the same address + 128).
+// The K table is rebuilt from q~ for every segment, since phase 2 overwrites
+// it.  Each thread keeps kRing batches of rows in a register ring: the
+// plane words of the next kRing - 1 batches load while one batch is scored
+// or scattered.  (Bulk L2 prefetches of the rows a few batches ahead were
+// measured slower.)
 // Build-time tuning knobs of decode v3 (defaults are the measured best).
 #ifndef KH_DECODE_SEG
 #define KH_DECODE_SEG 4096
@@ -494,7 +504,10 @@ struct V3Cfg {
   // phase 2.  D = 256 needs all 64 words for its two V histograms.
   static constexpr bool kHalf = D == 128;
   static constexpr int kSeg = kHalf ? 8192 : KH_DECODE_SEG;
-  static constexpr int kBatch = D == 128 ? KH_DECODE_BATCH128 : 1;  // rows per thread in flight
+  static constexpr int kBatch = D == 128 ? KH_DECODE_BATCH128 : 1;  // rows per thread per batch
+  // batches in the register ring: kRing - 1 batches are loading while one
+  // is scored or scattered
+  static constexpr int kRing = D == 128 ? 3 : 2;
   // tab [256][64] | (D = 256: logits [kSeg] | fold partials [2][4][32][8]) |
   // q~ [D] | reduction scratch [64]
   static constexpr int kTabWords = 256 * 64;
@@ -640,33 +653,8 @@ __global__ void __launch_bounds__(256, 2)
     const int64_t row0 = gk * P.seq_len + c0;
     const int nb = (n + NT * B - 1) / (NT * B);  // batches of B rows per thread
 
-    // K table into entries 0..31 of every row: T[v][slot] = sum of q~ over
-    // the set bits of v at the slot's byte position.  Thread t fills slot
-    // t mod 32 for the byte values v = t / 32 + 8 k (k < 32): the low nibble
-    // of v is t / 32 + 8 (k mod 2), the high nibble k / 2.
-    {
-      const int slot = t & 31, pos = slot % kP, w = t >> 5;
-      float qb[8];
-#pragma unroll
-      for (int b = 0; b < 8; ++b) qb[b] = qt[8 * pos + b];
-      float lo[2];
-#pragma unroll
-      for (int h = 0; h < 2; ++h) {
-        const int nv = w + 8 * h;
-        lo[h] = ((nv & 1) ? qb[0] : 0.f) + ((nv & 2) ? qb[1] : 0.f) +
-                ((nv & 4) ? qb[2] : 0.f) + ((nv & 8) ? qb[3] : 0.f);
-      }
-      float* tf = reinterpret_cast<float*>(tabb) + slot;
-      static_for<32>([&](auto kc) {
-        constexpr int k = decltype(kc)::value, hv = k >> 1;
-        float hi = 0.f;
-        if constexpr ((hv & 1) != 0) hi += qb[4];
-        if constexpr ((hv & 2) != 0) hi += qb[5];
-        if constexpr ((hv & 4) != 0) hi += qb[6];
-        if constexpr ((hv & 8) != 0) hi += qb[7];
-        tf[(w + 8 * k) * 64] = lo[k & 1] + hi;
-      });
-    }
+    // K table into entries 0..31 of every row
+    build_byte_table<D>(reinterpret_cast<float*>(tabb), qt, t);
     __syncthreads();
 
     // ---------------- phase 1: logits (log2 units) of the segment, online
@@ -674,7 +662,7 @@ __global__ void __launch_bounds__(256, 2)
     float mt = -INFINITY;
     float2 sums = make_float2(0.f, 0.f);
     {
-      RowKV<D> a[2][B];
+      RowKV<D> a[C::kRing][B];
       auto load_batch = [&](RowKV<D>(&dst)[B], int bi) {
 #pragma unroll
         for (int u = 0; u < B; ++u) {
@@ -724,19 +712,20 @@ __global__ void __launch_bounds__(256, 2)
           mt = mb;
         }
       };
-      load_batch(a[0], 0);
-      for (int bi = 0; bi < nb; bi += 2) {
-        load_batch(a[1], bi + 1);
-        score_batch(a[0], bi);
-        if (bi + 1 < nb) {
-          load_batch(a[0], bi + 2);
-          score_batch(a[1], bi + 1);
-        }
+      static_for<C::kRing - 1>([&](auto jc) { load_batch(a[decltype(jc)::value], decltype(jc)::value); });
+      for (int bi = 0; bi < nb; bi += C::kRing) {
+        static_for<C::kRing>([&](auto jc) {
+          constexpr int j = decltype(jc)::value;
+          if (bi + j < nb) {
+            load_batch(a[(j + C::kRing - 1) % C::kRing], bi + j + C::kRing - 1);
+            score_batch(a[j], bi + j);
+          }
+        });
       }
     }
     // phase 2's first V rows, loaded now so that their latency overlaps the
     // block reductions below
-    RowK<D> va[2][B];
+    RowK<D> va[C::kRing][B];
     auto load_vbatch = [&](RowK<D>(&dst)[B], int bi) {
 #pragma unroll
       for (int u = 0; u < B; ++u) {
@@ -748,7 +737,7 @@ __global__ void __launch_bounds__(256, 2)
         dst[u].rn = __ldg(vyn + row);
       }
     };
-    load_vbatch(va[0], 0);
+    static_for<C::kRing - 1>([&](auto jc) { load_vbatch(va[decltype(jc)::value], decltype(jc)::value); });
     const float m_seg = block_max<NT>(mt, red);  // also: phase-1 table reads done
     const float m_new = fmaxf(m_run, m_seg);
     const float alpha = exp2f(m_run - m_new);  // 0 on the first segment
@@ -811,13 +800,14 @@ __global__ void __launch_bounds__(256, 2)
           });
         }
       };
-      for (int bi = 0; bi < nb; bi += 2) {
-        load_vbatch(va[1], bi + 1);
-        scatter_batch(va[0], bi);
-        if (bi + 1 < nb) {
-          load_vbatch(va[0], bi + 2);
-          scatter_batch(va[1], bi + 1);
-        }
+      for (int bi = 0; bi < nb; bi += C::kRing) {
+        static_for<C::kRing>([&](auto jc) {
+          constexpr int j = decltype(jc)::value;
+          if (bi + j < nb) {
+            load_vbatch(va[(j + C::kRing - 1) % C::kRing], bi + j + C::kRing - 1);
+            scatter_batch(va[j], bi + j);
+          }
+        });
       }
     }
     const float c_c = block_sum<NT>(csum, red) * scale;  // also fences the histograms

@@ -154,8 +154,11 @@ struct ScoreTabCfg {
   static constexpr int kThreads = 256;
   static constexpr int kRows = 8192;   // cached rows per CTA
   static constexpr int kBatch = D == 128 ? 4 : 2;  // rows per thread in flight
-  // table [256][64] | q~ [D] | nibble tables [2][16][kP] | reduction scratch [32]
-  static constexpr int kSmem = (256 * 64 + D + 2 * kP * 16 + 32) * 4;
+  // table [256][64] (entries 0..31 of each row used) | q~ [D] | reduction
+  // scratch [32]: 65 KB, so two CTAs per SM fit the 132 KB shared-memory
+  // carveout and leave the rest of the 256 KB to the L1 that holds the
+  // in-flight row loads
+  static constexpr int kSmem = (256 * 64 + D + 32) * 4;
 };
 
 template <int D, bool RES>
@@ -169,8 +172,7 @@ __global__ void __launch_bounds__(256, 2)
   extern __shared__ __align__(16) unsigned char smem_s[];
   unsigned char* tabb = smem_s;
   float* qt = reinterpret_cast<float*>(smem_s) + 256 * 64;
-  float* nib = qt + D;
-  float* red = nib + 2 * kP * 16;
+  float* red = qt + D;
 
   const int t = threadIdx.x;
   const int lane = t & 31;
@@ -198,20 +200,8 @@ __global__ void __launch_bounds__(256, 2)
     qt[i] *= inv_sqrt_d;
     qpart += qt[i];
   }
-  const float Q = block_sum<NT>(qpart, red);
-  for (int e = t; e < 2 * kP * 16; e += NT) {  // layout [hi][nibble][pos]
-    const int hi = e / (kP * 16), nv = (e / kP) & 15, pos = e % kP;
-    float sm = 0.f;
-#pragma unroll
-    for (int k = 0; k < 4; ++k) sm += ((nv >> k) & 1) ? qt[8 * pos + 4 * hi + k] : 0.f;
-    nib[e] = sm;
-  }
-  __syncthreads();
-  for (int e = t; e < 256 * 32; e += NT) {
-    const int v = e >> 5, slot = e & 31, pos = slot % kP;
-    reinterpret_cast<float*>(tabb)[v * 64 + slot] =
-        nib[(v & 15) * kP + pos] + nib[kP * 16 + (v >> 4) * kP + pos];
-  }
+  const float Q = block_sum<NT>(qpart, red);  // (its barriers also publish qt)
+  build_byte_table<D>(reinterpret_cast<float*>(tabb), qt, t);
   __syncthreads();
 
   const int rr = lane % kP;
