@@ -153,7 +153,10 @@ struct ScoreTabCfg {
   static constexpr int kP = D / 8;
   static constexpr int kThreads = 256;
   static constexpr int kRows = 8192;   // cached rows per CTA
-  static constexpr int kBatch = D == 128 ? 4 : 2;  // rows per thread in flight
+  static constexpr int kBatch = 2;  // rows per thread per batch
+  // batches in the register ring: kRing - 1 batches are loading while one
+  // is scored
+  static constexpr int kRing = D == 128 ? 4 : 2;
   // table [256][64] (entries 0..31 of each row used) | q~ [D] | reduction
   // scratch [32]: 65 KB, so two CTAs per SM fit the 132 KB shared-memory
   // carveout and leave the rest of the 256 KB to the L1 that holds the
@@ -257,15 +260,16 @@ __global__ void __launch_bounds__(256, 2)
       if (ii < n) P.out[y * P.seq_len + s0 + ii] = sc;
     }
   };
-  Row a[2][B];
-  load_batch(a[0], 0);
-  for (int bi = 0; bi < nb; bi += 2) {
-    load_batch(a[1], bi + 1);
-    score_batch(a[0], bi);
-    if (bi + 1 < nb) {
-      load_batch(a[0], bi + 2);
-      score_batch(a[1], bi + 1);
-    }
+  Row a[C::kRing][B];
+  static_for<C::kRing - 1>([&](auto jc) { load_batch(a[decltype(jc)::value], decltype(jc)::value); });
+  for (int bi = 0; bi < nb; bi += C::kRing) {
+    static_for<C::kRing>([&](auto jc) {
+      constexpr int j = decltype(jc)::value;
+      if (bi + j < nb) {
+        load_batch(a[(j + C::kRing - 1) % C::kRing], bi + j + C::kRing - 1);
+        score_batch(a[j], bi + j);
+      }
+    });
   }
 }
 
