@@ -595,7 +595,8 @@ def decode_bench(dev, args, world: int = 1, rank: int = 0) -> dict:
             ops.decode_partial(qf, pk, pv, dk, dv, c, sm, n_splits, ws, n_splits, 0, S_loc)
             ops.decode_combine(ws, n_splits, dv, out)
     else:
-        buf = torch.empty(G * world * n_splits * (DEC_D + 2), device=dev)
+        buf = torch.empty(khdist.seq_sharded_workspace_numel(G, n_splits, world, DEC_D),
+                          device=dev)
 
         def step():
             khdist.decode_attention_seq_sharded(qf, pk, pv, dk, dv, c, sm, n_splits,

@@ -204,7 +204,13 @@ int kh_decode_partial_gqa(const float* q, int64_t n_groups, int n_q, int head_di
  * (D+2) floats per group -- (running max, running sum-exp, D rotated-domain
  * accumulators) -- at partials + (g*part_stride + part_offset + split)*(D+2).
  * kh_decode_combine merges n_parts records per group and writes
- * out[g][D] = d (.) H(sum acc) / sum l.
+ * out[g][D] = d (.) H(sum acc) / sum l.  kh_decode_combine_strided does the
+ * same with record p of group g at partials + g*group_stride + p*part_stride
+ * (strides in floats, so a transposed view of gathered records works).
+ * kh_decode_merge merges the same way but writes one record of (D+2) floats
+ * per group at merged + g*(D+2), still in the rotated domain: a rank of a
+ * sequence-sharded decode merges its own splits with it and gathers one
+ * record per group from every rank.  Records with l = 0 are skipped.
  * kh_decode_attn = partial + combine using a caller workspace of
  * kh_decode_workspace_bytes(n_groups, n_splits, D) bytes.
  */
@@ -224,6 +230,14 @@ int kh_decode_partial(const float* q, int64_t n_groups, int head_dim,
 int kh_decode_combine(const float* partials, int64_t n_groups, int n_parts,
                       int head_dim, const float* d_v_host, float* out,
                       void* stream);
+
+int kh_decode_combine_strided(const float* partials, int64_t n_groups, int n_parts,
+                              int64_t group_stride, int64_t part_stride, int head_dim,
+                              const float* d_v_host, float* out, void* stream);
+
+int kh_decode_merge(const float* partials, int64_t n_groups, int n_parts,
+                    int64_t group_stride, int64_t part_stride, int head_dim,
+                    float* merged, void* stream);
 
 int kh_decode_attn(const float* q, int64_t n_groups, int head_dim,
                    const uint32_t* k_code, const uint32_t* k_res,

@@ -381,16 +381,40 @@ int kh_decode_partial(const float* q, int64_t n_groups, int head_dim,
                                n_splits, partials, part_stride, part_offset, stream);
 }
 
-int kh_decode_combine(const float* partials, int64_t n_groups, int n_parts,
-                      int head_dim, const float* d_v_host, float* out,
-                      void* stream) {
+int kh_decode_combine_strided(const float* partials, int64_t n_groups, int n_parts,
+                              int64_t group_stride, int64_t part_stride, int head_dim,
+                              const float* d_v_host, float* out, void* stream) {
   if (n_groups < 0 || n_parts < 1 || !valid_head_dim(head_dim)) return KH_EINVAL;
+  if (group_stride < 0 || part_stride < 0) return KH_EINVAL;
   if (!check_d(d_v_host, head_dim)) return KH_EINVAL;
   if (n_groups == 0) return KH_OK;
   if (!partials || !out) return KH_EINVAL;
   if (!aligned4(partials) || !aligned4(out)) return KH_EALIGN;
-  return launch_decode_combine(partials, n_groups, n_parts, head_dim, d_v_host,
-                               out, static_cast<cudaStream_t>(stream));
+  return launch_decode_combine(partials, n_groups, n_parts, group_stride, part_stride,
+                               head_dim, d_v_host, false, out,
+                               static_cast<cudaStream_t>(stream));
+}
+
+int kh_decode_combine(const float* partials, int64_t n_groups, int n_parts,
+                      int head_dim, const float* d_v_host, float* out,
+                      void* stream) {
+  if (n_parts < 1 || !valid_head_dim(head_dim)) return KH_EINVAL;
+  const int64_t rec = head_dim + 2;
+  return kh_decode_combine_strided(partials, n_groups, n_parts, (int64_t)n_parts * rec, rec,
+                                   head_dim, d_v_host, out, stream);
+}
+
+int kh_decode_merge(const float* partials, int64_t n_groups, int n_parts,
+                    int64_t group_stride, int64_t part_stride, int head_dim,
+                    float* merged, void* stream) {
+  if (n_groups < 0 || n_parts < 1 || !valid_head_dim(head_dim)) return KH_EINVAL;
+  if (group_stride < 0 || part_stride < 0) return KH_EINVAL;
+  if (n_groups == 0) return KH_OK;
+  if (!partials || !merged) return KH_EINVAL;
+  if (!aligned4(partials) || !aligned4(merged)) return KH_EALIGN;
+  return launch_decode_combine(partials, n_groups, n_parts, group_stride, part_stride,
+                               head_dim, nullptr, true, merged,
+                               static_cast<cudaStream_t>(stream));
 }
 
 int kh_decode_attn(const float* q, int64_t n_groups, int head_dim,

@@ -156,29 +156,42 @@ __global__ void __launch_bounds__(D)
   rec[2 + t] = acc;
 }
 
-template <int D>
+// Merges n_parts split-K records per query row; record p of row g is at
+// parts + g * gs + p * ps (floats).  Records with l = 0 (empty splits) are
+// skipped.  kRecord: writes the merged record (m, l, acc) at
+// out + g * (D + 2), still in the rotated domain (the multi-GPU path gathers
+// these); otherwise out[g] = d (.) H(acc) / l.
+template <int D, bool kRecord>
 __global__ void __launch_bounds__(D)
-    decode_combine_kernel(const float* __restrict__ parts, int n_parts,
-                          float* __restrict__ out, const float* __restrict__ dv_unused,
+    decode_combine_kernel(const float* __restrict__ parts, int n_parts, int64_t gs,
+                          int64_t ps, float* __restrict__ out,
                           const __grid_constant__ DecodeParams P) {
-  (void)dv_unused;
   __shared__ float sh[D];
   const int t = threadIdx.x;
   const int64_t g = blockIdx.x;
-  const float* base = parts + g * (int64_t)n_parts * (D + 2);
+  const float* base = parts + g * gs;
   float M = -INFINITY;
   for (int r = 0; r < n_parts; ++r) {
-    const float* rec = base + (int64_t)r * (D + 2);
+    const float* rec = base + (int64_t)r * ps;
     if (rec[1] > 0.f) M = fmaxf(M, rec[0]);
   }
   float L = 0.f, a = 0.f;
   for (int r = 0; r < n_parts; ++r) {
-    const float* rec = base + (int64_t)r * (D + 2);
+    const float* rec = base + (int64_t)r * ps;
     if (rec[1] > 0.f) {
       const float e = expf(rec[0] - M);
       L += rec[1] * e;
       a += rec[2 + t] * e;
     }
+  }
+  if constexpr (kRecord) {
+    float* rec = out + g * (D + 2);
+    rec[2 + t] = a;
+    if (t == 0) {
+      rec[0] = M;
+      rec[1] = L;
+    }
+    return;
   }
   sh[t] = a;
   __syncthreads();
@@ -945,19 +958,31 @@ kh_status launch_decode_partial(const DecodeRequest& r, cudaStream_t stream) {
   return cudaGetLastError() == cudaSuccess ? KH_OK : KH_ELAUNCH;
 }
 
-kh_status launch_decode_combine(const float* partials, int64_t n_groups,
-                                int n_parts, int D, const float* dv,
-                                float* out, cudaStream_t stream) {
+kh_status launch_decode_combine(const float* partials, int64_t n_groups, int n_parts,
+                                int64_t group_stride, int64_t part_stride, int D,
+                                const float* dv, bool records, float* out,
+                                cudaStream_t stream) {
   DecodeParams P;
   memset(&P, 0, sizeof(P));
-  for (int i = 0; i < D; ++i) P.dk[i] = dv[i];
+  if (dv)
+    for (int i = 0; i < D; ++i) P.dk[i] = dv[i];
   if (n_groups > 0x7fffffff) return KH_EINVAL;
-  if (D == 128)
-    decode_combine_kernel<128><<<(unsigned)n_groups, 128, 0, stream>>>(
-        partials, n_parts, out, nullptr, P);
-  else
-    decode_combine_kernel<256><<<(unsigned)n_groups, 256, 0, stream>>>(
-        partials, n_parts, out, nullptr, P);
+  const unsigned grid = (unsigned)n_groups;
+  if (D == 128) {
+    if (records)
+      decode_combine_kernel<128, true><<<grid, 128, 0, stream>>>(partials, n_parts, group_stride,
+                                                                part_stride, out, P);
+    else
+      decode_combine_kernel<128, false><<<grid, 128, 0, stream>>>(partials, n_parts, group_stride,
+                                                                 part_stride, out, P);
+  } else {
+    if (records)
+      decode_combine_kernel<256, true><<<grid, 256, 0, stream>>>(partials, n_parts, group_stride,
+                                                                part_stride, out, P);
+    else
+      decode_combine_kernel<256, false><<<grid, 256, 0, stream>>>(partials, n_parts, group_stride,
+                                                                 part_stride, out, P);
+  }
   return cudaGetLastError() == cudaSuccess ? KH_OK : KH_ELAUNCH;
 }
 

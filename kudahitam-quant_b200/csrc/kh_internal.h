@@ -93,9 +93,13 @@ struct DecodeRequest {
 };
 
 kh_status launch_decode_partial(const DecodeRequest& r, cudaStream_t stream);
-kh_status launch_decode_combine(const float* partials, int64_t n_groups,
-                                int n_parts, int D, const float* dv,
-                                float* out, cudaStream_t stream);
+// Merges n_parts records per query row (record p of row g at
+// partials + g * group_stride + p * part_stride floats): records = true writes
+// merged records (D + 2 floats per row), else d (.) H(acc) / l into out[g][D].
+kh_status launch_decode_combine(const float* partials, int64_t n_groups, int n_parts,
+                                int64_t group_stride, int64_t part_stride, int D,
+                                const float* dv, bool records, float* out,
+                                cudaStream_t stream);
 
 // Device address of the sticky error word on the current device.
 uint32_t* device_error_ptr();

@@ -46,6 +46,9 @@ SIGNATURES = {
                                      _vp, _vp, _c_i64, _c_i64, _c_i64, _vp, _vp, _vp, _c_i,
                                      _c_f, _c_i, _vp, _c_i64, _c_i64, _vp]),
     "kh_decode_combine": (_c_i, [_vp, _c_i64, _c_i, _c_i, _vp, _vp, _vp]),
+    "kh_decode_combine_strided": (_c_i, [_vp, _c_i64, _c_i, _c_i64, _c_i64, _c_i, _vp, _vp,
+                                         _vp]),
+    "kh_decode_merge": (_c_i, [_vp, _c_i64, _c_i, _c_i64, _c_i64, _c_i, _vp, _vp]),
     "kh_decode_attn": (_c_i, [_vp, _c_i64, _c_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                               _c_i64, _vp, _vp, _vp, _c_i, _c_f, _c_i, _vp, _c_i64, _vp,
                               _vp]),

@@ -4,11 +4,12 @@
   contiguous slice of the flattened batch x head axis and ranks compress their
   slices with no communication.
 * Decode attention over a sequence-sharded cache: every rank runs the split-K
-  partial kernel over its own slice of S and writes (m, l, acc[D]) records into
-  its slot of a zero-initialised [G, world * n_splits, D+2] buffer; one
-  all-reduce(SUM) turns that buffer into the gathered records of all ranks
-  (slots of other ranks are zero and records with l == 0 are ignored by the
-  merge), and every rank merges them locally with ``kh_decode_combine``.
+  partial kernel over its own slice of S, merges its splits into one
+  (m, l, acc[D]) record per query row (``kh_decode_merge``), and one
+  all-gather gives every rank the [world, R, D+2] records of all ranks, which
+  ``kh_decode_combine_strided`` merges into the output (records with l == 0,
+  from ranks or splits that own no rows, are ignored).  Each rank sends
+  R * (D+2) floats: 266 KB for 512 query rows at D = 128.
 """
 from __future__ import annotations
 
@@ -36,17 +37,27 @@ def _world(group) -> tuple[int, int]:
     return 1, 0
 
 
-def gather_partials(local: torch.Tensor, group=None) -> torch.Tensor:
-    """[G, P, R] records of this rank -> [G, world * P, R] records of all ranks
-    (rank r at slots [r*P, (r+1)*P)), by one all-reduce over a zero buffer."""
-    world, rank = _world(group)
-    G, P, R = local.shape
+def gather_records(local: torch.Tensor, group=None,
+                   out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """This rank's [R, D+2] merged records -> [world, R, D+2], the records of
+    every rank (rank r at [r]), by one all-gather."""
+    world, _ = _world(group)
+    R, W = local.shape
+    if out is None:
+        out = torch.empty((world, R, W), dtype=local.dtype, device=local.device)
     if world == 1:
-        return local
-    buf = torch.zeros((G, world * P, R), dtype=local.dtype, device=local.device)
-    buf[:, rank * P:(rank + 1) * P] = local
-    dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=group)
-    return buf
+        out[0].copy_(local)
+        return out
+    dist.all_gather_into_tensor(out.view(world * R, W), local.contiguous(), group=group)
+    return out
+
+
+def seq_sharded_workspace_numel(n_rows: int, n_splits: int, world: int, head_dim: int) -> int:
+    """Floats of workspace ``decode_attention_seq_sharded`` uses: the local
+    split records, and with world > 1 the merged record and the gathered
+    records of every rank."""
+    extra = 1 + world if world > 1 else 0
+    return n_rows * (head_dim + 2) * (n_splits + extra)
 
 
 def decode_attention_seq_sharded(q: torch.Tensor, k_local: ops.PackedKV,
@@ -57,7 +68,7 @@ def decode_attention_seq_sharded(q: torch.Tensor, k_local: ops.PackedKV,
     """Decode attention where each rank holds S_local cached rows per group
     (k_local / v_local: G * S_local rows).  q is [G, D] or [G, n_q, D]
     (grouped-query heads).  Returns float32 with q's shape on every rank."""
-    world, rank = _world(group)
+    world, _ = _world(group)
     G, D = q.shape[0], q.shape[-1]
     R = q.numel() // D  # query rows: G * n_q
     S_loc = k_local.n_rows // max(G, 1)
@@ -65,17 +76,22 @@ def decode_attention_seq_sharded(q: torch.Tensor, k_local: ops.PackedKV,
         sm_scale = 1.0 / math.sqrt(D)
     if n_splits is None:
         n_splits = ops.default_splits(R, S_loc, q.device)
-    parts = world * n_splits
-    if partials is None or partials.numel() < R * parts * (D + 2):
-        partials = torch.empty(R * parts * (D + 2), dtype=torch.float32, device=q.device)
-    buf = partials[: R * parts * (D + 2)].view(R, parts, D + 2)
-    buf.zero_()
-    ops.decode_partial(q, k_local, v_local, dk, dv, centroids, sm_scale, n_splits, buf,
-                       part_stride=parts, part_offset=rank * n_splits, seq_len=S_loc)
-    if world > 1:
-        dist.all_reduce(buf, op=dist.ReduceOp.SUM, group=group)
+    rec = D + 2
+    need = seq_sharded_workspace_numel(R, n_splits, world, D)
+    if partials is None or partials.numel() < need:
+        partials = torch.empty(need, dtype=torch.float32, device=q.device)
+    local = partials[: R * n_splits * rec].view(R, n_splits, rec)
+    ops.decode_partial(q, k_local, v_local, dk, dv, centroids, sm_scale, n_splits, local,
+                       part_stride=n_splits, part_offset=0, seq_len=S_loc)
     out = torch.empty(q.shape, dtype=torch.float32, device=q.device)
-    return ops.decode_combine(buf, parts, dv, out)
+    if world == 1:
+        return ops.decode_combine(local, n_splits, dv, out)
+    off = R * n_splits * rec
+    merged = partials[off: off + R * rec].view(R, rec)
+    ops.decode_merge(local, merged)
+    gathered = partials[off + R * rec: need].view(world, R, rec)
+    gather_records(merged, group, out=gathered)
+    return ops.decode_combine_records(gathered.transpose(0, 1), dv, out)
 
 
 def max_over_ranks(value: float, group=None, device=None) -> float:

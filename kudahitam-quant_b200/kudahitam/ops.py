@@ -451,6 +451,45 @@ def decode_combine(partials: torch.Tensor, n_parts: int, dv, out: torch.Tensor) 
     return out
 
 
+def _record_view(records: torch.Tensor, D: int):
+    """(rows, parts, row stride, part stride) of a [R, P, D+2] float32 record
+    view whose last dimension is contiguous."""
+    if records.dtype != torch.float32 or records.dim() != 3 or records.shape[2] != D + 2:
+        raise ValueError(f"records must be float32 [R, P, {D + 2}], got "
+                         f"{records.dtype} {tuple(records.shape)}")
+    if records.stride(2) != 1:
+        raise ValueError("records must be contiguous in their last dimension")
+    return records.shape[0], records.shape[1], records.stride(0), records.stride(1)
+
+
+def decode_combine_records(records: torch.Tensor, dv, out: torch.Tensor) -> torch.Tensor:
+    """decode_combine over a strided [R, P, D+2] record view (for example the
+    transpose of records gathered as [world, R, D+2])."""
+    dev = _require_cuda(records, out)
+    D = out.shape[-1]
+    R, P, gs, ps = _record_view(records, D)
+    if out.numel() != R * D:
+        raise ValueError(f"out holds {out.numel()} values, records describe {R} x {D}")
+    dvh = _host_f32(dv)
+    with _on(dev):
+        _lib.call("kh_decode_combine_strided", _vp(records), R, P, gs, ps, D, _vp(dvh),
+                  _vp(out), _stream(dev))
+    return out
+
+
+def decode_merge(records: torch.Tensor, merged: torch.Tensor) -> torch.Tensor:
+    """Merge the P records of each row of a [R, P, D+2] view into one record
+    per row: merged [R, D+2], still in the rotated domain."""
+    dev = _require_cuda(records, merged)
+    D = merged.shape[-1] - 2
+    R, P, gs, ps = _record_view(records, D)
+    if merged.numel() != R * (D + 2) or not merged.is_contiguous():
+        raise ValueError(f"merged must be a contiguous float32 [{R}, {D + 2}]")
+    with _on(dev):
+        _lib.call("kh_decode_merge", _vp(records), R, P, gs, ps, D, _vp(merged), _stream(dev))
+    return merged
+
+
 def decode_attention(q: torch.Tensor, k: PackedKV, v: PackedKV, dk, dv, centroids,
                      sm_scale: Optional[float] = None, n_splits: Optional[int] = None,
                      workspace: Optional[torch.Tensor] = None,

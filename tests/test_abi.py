@@ -100,6 +100,17 @@ def test_other_entry_points_validate():
     assert L.kh_decode_attn(FAKE, 2, 128, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 100,
                             D128, D128, C2, 2, 0.1, 4, FAKE, 16, FAKE,
                             None) == _lib.KH_EINVAL  # workspace too small
+    assert L.kh_decode_merge(FAKE, 2, 0, 260, 130, 128, FAKE, None) == _lib.KH_EINVAL
+    assert L.kh_decode_merge(FAKE, 2, 2, 260, 130, 96, FAKE, None) == _lib.KH_EINVAL
+    assert L.kh_decode_merge(FAKE, 2, 2, -1, 130, 128, FAKE, None) == _lib.KH_EINVAL
+    assert L.kh_decode_merge(FAKE, 0, 2, 260, 130, 128, FAKE, None) == _lib.KH_OK
+    assert L.kh_decode_merge(FAKE, 2, 2, 260, 130, 128, None, None) == _lib.KH_EINVAL
+    assert L.kh_decode_merge(ctypes.c_void_p(0x10002), 2, 2, 260, 130, 128, FAKE,
+                             None) == _lib.KH_EALIGN
+    assert L.kh_decode_combine_strided(FAKE, 2, 2, 260, -130, 128, D128, FAKE,
+                                       None) == _lib.KH_EINVAL
+    assert L.kh_decode_combine_strided(FAKE, 2, 2, 260, 130, 128, None, FAKE,
+                                       None) == _lib.KH_EINVAL  # no d vector
 
 
 def test_gqa_decode_and_compat_scorer_validate():

@@ -1,9 +1,9 @@
 """world_size-2 gloo tests of the multi-GPU host logic, on CPU.
 
-The decode combine gathers every rank's split-K records with one all-reduce
-over a zeroed buffer; these tests run that exchange for real (gloo) with
-records computed by the oracle and check the merged result against the
-unsharded oracle.  Kernels are covered by the -m gpu tests."""
+The sequence-sharded decode merges each rank's split-K records into one
+record per query row and all-gathers those; these tests run that exchange for
+real (gloo) with records computed and merged by the oracle and check the final
+merge against the unsharded oracle.  Kernels are covered by the -m gpu tests."""
 import os
 import socket
 
@@ -12,7 +12,7 @@ import torch
 import torch.distributed as dist
 import torch.multiprocessing as mp
 
-from kudahitam.dist import gather_partials, max_over_ranks, shard_range
+from kudahitam.dist import gather_records, max_over_ranks, shard_range
 
 
 def _free_port() -> int:
@@ -48,11 +48,13 @@ def _worker(rank, world, port, S, D, G, q):
                 lo = a + (b - a) * k // n_splits
                 hi = a + (b - a) * (k + 1) // n_splits
                 local[g, k] = _records(logits[g, lo:hi], vals[g, lo:hi])
-        full = gather_partials(torch.from_numpy(local), None).numpy()
-        assert full.shape == (G, world * n_splits, D + 2)
-        assert np.array_equal(full[:, rank * n_splits:(rank + 1) * n_splits], local)
         from oracle.oracle import merge_partials
-        M, L, acc = merge_partials(full)
+        m_loc, l_loc, acc_loc = merge_partials(local)  # this rank's splits
+        mine = np.concatenate([m_loc[:, None], l_loc[:, None], acc_loc], axis=1)
+        full = gather_records(torch.from_numpy(mine), None).numpy()
+        assert full.shape == (world, G, D + 2)
+        assert np.array_equal(full[rank], mine)
+        M, L, acc = merge_partials(full.transpose(1, 0, 2))
         got = acc / L[:, None]
         p = np.exp(logits - logits.max(1, keepdims=True))
         want = np.einsum("gs,gsd->gd", p / p.sum(1, keepdims=True), vals)

@@ -283,6 +283,58 @@ def test_decode_seq_sharded_emulated_on_one_gpu(decode_path):
     assert torch.allclose(got, want, rtol=1e-4, atol=1e-5)
 
 
+def test_decode_merge_then_gathered_combine(decode_path):
+    """The multi-GPU record path on one GPU: every emulated rank merges its
+    own splits into one record per row (kh_decode_merge); the stacked
+    [world, G, D+2] records are combined through a transposed, strided view
+    (kh_decode_combine_strided).  The last rank owns no rows."""
+    D, G, S, world, n_splits = 128, 4, 1000, 4, 3
+    dk, dv, c, k, v = _caches(G, S, D, seed=4)
+    q = torch.randn(G, D, device="cuda")
+    kc, vc = k.cuda().view(G, S, D), v.cuda().view(G, S, D)
+    from kudahitam.dist import shard_range
+    a_last, _ = shard_range(S, world, world - 1)
+    gathered = torch.empty(world, G, D + 2, device="cuda")
+    for r in range(world):
+        a, b = shard_range(S, world, r)
+        if r == world - 1:
+            a, b = 0, 0  # an empty shard: its records carry l = 0
+        lo, hi = (a, b) if b > a else (0, 1)  # any valid cache for the empty shard
+        local = torch.empty(G, n_splits, D + 2, device="cuda")
+        pk = ops.compress(kc[:, lo:hi].contiguous(), dk, c)
+        pv = ops.compress(vc[:, lo:hi].contiguous(), dv, c)
+        ops.decode_partial(q, pk, pv, dk, dv, c, 1 / math.sqrt(D), n_splits, local,
+                           part_stride=n_splits, part_offset=0, seq_len=hi - lo,
+                           seq_begin=0, seq_end=b - a)
+        ops.decode_merge(local, gathered[r])
+    assert torch.all(gathered[world - 1, :, 1] == 0)
+    got = ops.decode_combine_records(gathered.transpose(0, 1), dv,
+                                     torch.empty(G, D, device="cuda"))
+    pk = ops.compress(kc[:, :a_last].contiguous(), dk, c)
+    pv = ops.compress(vc[:, :a_last].contiguous(), dv, c)
+    want = ops.decode_attention(q, pk, pv, dk, dv, c, 1 / math.sqrt(D), n_splits=8)
+    assert torch.allclose(got, want, rtol=1e-4, atol=1e-5)
+
+
+def test_decode_combine_strided_matches_plain():
+    """kh_decode_combine is kh_decode_combine_strided with the packed
+    strides: bitwise the same output; merging first and combining the one
+    merged record gives the same values."""
+    D, G, P = 128, 6, 5
+    g = torch.Generator(device="cuda").manual_seed(0)
+    rec = torch.randn(G, P, D + 2, device="cuda", generator=g)
+    rec[..., 1] = rec[..., 1].abs() + 0.1
+    rec[2, 1, 1] = 0.0  # an empty split
+    dv = torch.ones(D)
+    a = ops.decode_combine(rec, P, dv, torch.empty(G, D, device="cuda"))
+    b = ops.decode_combine_records(rec, dv, torch.empty(G, D, device="cuda"))
+    assert torch.equal(a, b)
+    merged = ops.decode_merge(rec, torch.empty(G, D + 2, device="cuda"))
+    c = ops.decode_combine_records(merged.view(G, 1, D + 2), dv,
+                                   torch.empty(G, D, device="cuda"))
+    assert torch.allclose(a, c, rtol=1e-5, atol=1e-6)
+
+
 def test_compressor_decode_api():
     D = 128
     ck = KudahitamCompressorV2(D, 1, seed=10)
