@@ -82,6 +82,19 @@ __device__ __forceinline__ bool mbar_wait(uint64_t* bar, uint32_t parity,
   return true;
 }
 
+// ------------------------------------------- programmatic dependent launch
+// Wait until the previous grid in the stream has completed and its memory
+// operations are visible (returns at once when this grid was not launched
+// as a programmatic dependent).
+__device__ __forceinline__ void grid_dependency_wait() {
+  asm volatile("griddepcontrol.wait;" ::: "memory");
+}
+// Allow the next grid in the stream (if launched as a programmatic
+// dependent) to be scheduled once every CTA of this grid has signalled.
+__device__ __forceinline__ void grid_dependents_launch() {
+  asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
 // ---------------------------------------------------------------- TMA
 __device__ __forceinline__ void prefetch_tmap(const CUtensorMap* m) {
   asm volatile("prefetch.tensormap [%0];" ::"l"(reinterpret_cast<uint64_t>(m))

@@ -238,6 +238,10 @@ __global__ void __launch_bounds__(320, 1)
     // ------------------------------------------------------ TMA producer
     if (lane == 0) {
       const uint64_t policy = l2_policy_evict_first();
+      // The set-up above reads only kernel parameters, so with a programmatic
+      // launch it overlaps the previous kernel in the stream; rows are read
+      // (and hence outputs written) only after that kernel has completed.
+      grid_dependency_wait();
       int c = 0;  // chunk counter
       int sg_cur = 0;
       bool ok = true;
@@ -255,6 +259,9 @@ __global__ void __launch_bounds__(320, 1)
           tma_load_2d(dst + C::kBoxBytes, &P.tmap[sg], h * 128 + 64, row0, &full[s], policy);
         }
       }
+      // this CTA has issued its last row loads: the next kernel in the stream
+      // may start its set-up on SMs as they free up
+      grid_dependents_launch();
     }
   } else if (warp == 1) {
     // ------------------------------------------------------ MMA issuer
@@ -456,7 +463,20 @@ kh_status launch_tc_typed(const CompressRequest& req, cudaStream_t stream) {
   P.cb = req.cb;
   for (int e = 0; e < D; ++e) P.dsign[e] = req.dflip[e] ? -1.f : 1.f;
   const int grid = (int)std::max<int64_t>(1, std::min<int64_t>(tiles, sm_count()));
-  kern<<<grid, C::kThreads, C::kSmem, stream>>>(P);
+  // Programmatic dependent launch: this grid may start while the previous
+  // kernel in the stream finishes; its producer waits for that kernel's
+  // completion before the first row load.
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = dim3((unsigned)grid);
+  cfg.blockDim = dim3(C::kThreads);
+  cfg.dynamicSmemBytes = C::kSmem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  if (cudaLaunchKernelEx(&cfg, kern, P) != cudaSuccess) return KH_ELAUNCH;
   return cudaGetLastError() == cudaSuccess ? KH_OK : KH_ELAUNCH;
 }
 
