@@ -4,6 +4,8 @@
 // from the PTX ISA.  Every TMA load here is a plain per-CTA load.
 #pragma once
 
+#include <utility>
+
 #include <cuda.h>
 #include <cuda_runtime.h>
 #include <cuda_bf16.h>
@@ -93,6 +95,26 @@ __device__ __forceinline__ void grid_dependency_wait() {
 // dependent) to be scheduled once every CTA of this grid has signalled.
 __device__ __forceinline__ void grid_dependents_launch() {
   asm volatile("griddepcontrol.launch_dependents;" ::: "memory");
+}
+
+// Host: launch with programmatic stream serialisation, so that the kernel's
+// CTAs may start (and run their parameter-only set-up) while the previous
+// kernel in the stream finishes.  The kernel must call grid_dependency_wait()
+// before it touches global memory that earlier work may write or read.
+template <typename... KArgs, typename... Args>
+inline cudaError_t launch_programmatic(void (*kern)(KArgs...), dim3 grid, dim3 block,
+                                       size_t smem, cudaStream_t stream, Args&&... args) {
+  cudaLaunchConfig_t cfg = {};
+  cfg.gridDim = grid;
+  cfg.blockDim = block;
+  cfg.dynamicSmemBytes = smem;
+  cfg.stream = stream;
+  cudaLaunchAttribute attr[1];
+  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+  attr[0].val.programmaticStreamSerializationAllowed = 1;
+  cfg.attrs = attr;
+  cfg.numAttrs = 1;
+  return cudaLaunchKernelEx(&cfg, kern, std::forward<Args>(args)...);
 }
 
 // ---------------------------------------------------------------- TMA

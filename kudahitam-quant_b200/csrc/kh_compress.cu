@@ -118,6 +118,9 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       int sg0 = 0;
       prefetch_tmap(&P.tmap[seg_of(gw, sg0)]);
     }
+    // launched as a programmatic dependent: rows are read (and outputs
+    // written) only once the previous kernel in the stream has completed
+    grid_dependency_wait();
 #pragma unroll
     for (int s = 0; s < STAGES; ++s) {
       const int64_t t = gw + s * nw;
@@ -240,6 +243,9 @@ __global__ void __launch_bounds__(WARPS * 32, 1)
       }
     }
   }
+  // this warp is done: the next kernel in the stream may be scheduled once
+  // every CTA has signalled
+  grid_dependents_launch();
 }
 
 // ------------------------------------------------------------------ host
@@ -303,7 +309,9 @@ kh_status launch_typed(const CompressRequest& req, cudaStream_t stream) {
   const int64_t want = (tiles + kWarps - 1) / kWarps;
   const int64_t cap = (int64_t)sm_count() * blocks_per_sm[dev & 63];
   const int grid = (int)std::max<int64_t>(1, std::min(want, cap));
-  kern<<<grid, kWarps * 32, C::kSmem, stream>>>(P);
+  if (launch_programmatic(kern, dim3((unsigned)grid), dim3(kWarps * 32), C::kSmem, stream, P) !=
+      cudaSuccess)
+    return KH_ELAUNCH;
   return cudaGetLastError() == cudaSuccess ? KH_OK : KH_ELAUNCH;
 }
 

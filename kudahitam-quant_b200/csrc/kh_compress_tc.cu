@@ -466,17 +466,9 @@ kh_status launch_tc_typed(const CompressRequest& req, cudaStream_t stream) {
   // Programmatic dependent launch: this grid may start while the previous
   // kernel in the stream finishes; its producer waits for that kernel's
   // completion before the first row load.
-  cudaLaunchConfig_t cfg = {};
-  cfg.gridDim = dim3((unsigned)grid);
-  cfg.blockDim = dim3(C::kThreads);
-  cfg.dynamicSmemBytes = C::kSmem;
-  cfg.stream = stream;
-  cudaLaunchAttribute attr[1];
-  attr[0].id = cudaLaunchAttributeProgrammaticStreamSerialization;
-  attr[0].val.programmaticStreamSerializationAllowed = 1;
-  cfg.attrs = attr;
-  cfg.numAttrs = 1;
-  if (cudaLaunchKernelEx(&cfg, kern, P) != cudaSuccess) return KH_ELAUNCH;
+  if (launch_programmatic(kern, dim3((unsigned)grid), dim3(C::kThreads), C::kSmem, stream, P) !=
+      cudaSuccess)
+    return KH_ELAUNCH;
   return cudaGetLastError() == cudaSuccess ? KH_OK : KH_ELAUNCH;
 }
 

@@ -166,6 +166,7 @@ __global__ void __launch_bounds__(D)
     decode_combine_kernel(const float* __restrict__ parts, int n_parts, int64_t gs,
                           int64_t ps, float* __restrict__ out,
                           const __grid_constant__ DecodeParams P) {
+  grid_dependency_wait();  // the records come from the partial kernel
   __shared__ float sh[D];
   const int t = threadIdx.x;
   const int64_t g = blockIdx.x;
@@ -572,6 +573,7 @@ __device__ __forceinline__ float2 block_sum2(float2 v, float* red) {
 template <int D>
 __global__ void __launch_bounds__(256, 2)
     decode_v3_kernel(const __grid_constant__ DecodeParams P) {
+  grid_dependency_wait();  // q and the cache may come from the previous kernel
   using C = V3Cfg<D>;
   constexpr int kP = C::kP;
   constexpr int NT = C::kThreads;
@@ -945,7 +947,10 @@ kh_status launch_decode_partial(const DecodeRequest& r, cudaStream_t stream) {
       std::call_once(once[slot][dev & 63], [&] {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       });
-      kern<<<grid, threads, smem, stream>>>(P);
+      if (path == 3)  // v3 waits for the previous kernel before its first read
+        launch_programmatic(kern, grid, dim3(threads), smem, stream, P);
+      else
+        kern<<<grid, threads, smem, stream>>>(P);
     };
     if (path == 2) {
       if (r.D == 128) launch(decode_v2_kernel<128>, 0, V2Cfg<128>::kSmem, V2Cfg<128>::kThreads);
@@ -967,21 +972,17 @@ kh_status launch_decode_combine(const float* partials, int64_t n_groups, int n_p
   if (dv)
     for (int i = 0; i < D; ++i) P.dk[i] = dv[i];
   if (n_groups > 0x7fffffff) return KH_EINVAL;
-  const unsigned grid = (unsigned)n_groups;
+  const dim3 grid((unsigned)n_groups);
+  auto go = [&](auto kern, int threads) {
+    launch_programmatic(kern, grid, dim3(threads), 0, stream, partials, n_parts, group_stride,
+                        part_stride, out, P);
+  };
   if (D == 128) {
-    if (records)
-      decode_combine_kernel<128, true><<<grid, 128, 0, stream>>>(partials, n_parts, group_stride,
-                                                                part_stride, out, P);
-    else
-      decode_combine_kernel<128, false><<<grid, 128, 0, stream>>>(partials, n_parts, group_stride,
-                                                                 part_stride, out, P);
+    if (records) go(decode_combine_kernel<128, true>, 128);
+    else go(decode_combine_kernel<128, false>, 128);
   } else {
-    if (records)
-      decode_combine_kernel<256, true><<<grid, 256, 0, stream>>>(partials, n_parts, group_stride,
-                                                                part_stride, out, P);
-    else
-      decode_combine_kernel<256, false><<<grid, 256, 0, stream>>>(partials, n_parts, group_stride,
-                                                                 part_stride, out, P);
+    if (records) go(decode_combine_kernel<256, true>, 256);
+    else go(decode_combine_kernel<256, false>, 256);
   }
   return cudaGetLastError() == cudaSuccess ? KH_OK : KH_ELAUNCH;
 }

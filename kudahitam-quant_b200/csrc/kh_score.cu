@@ -167,6 +167,7 @@ struct ScoreTabCfg {
 template <int D, bool RES>
 __global__ void __launch_bounds__(256, 2)
     score_tab_kernel(const __grid_constant__ ScoreParams P) {
+  grid_dependency_wait();  // q and the cache may come from the previous kernel
   using C = ScoreTabCfg<D>;
   constexpr int kP = C::kP;
   constexpr int kW = D / 32;
@@ -305,7 +306,7 @@ kh_status launch_score(const float* q, int64_t n_groups, int n_q, int D,
       std::call_once(once[slot][dev & 63], [&] {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       });
-      kern<<<gridt, 256, smem, stream>>>(P);
+      launch_programmatic(kern, gridt, dim3(256), smem, stream, P);
     };
     const bool r = res != nullptr;
     if (D == 128) {
