@@ -565,7 +565,8 @@ def layers_bench(dev, args) -> dict:
 def decode_bench(dev, args, world: int = 1, rank: int = 0) -> dict:
     """Decode step over the 40k-token compressed cache.  With N ranks the
     sequence is sharded (S/N rows per group on each rank) and the split-K
-    records are combined with one NCCL all-reduce; the time is the max over
+    records are merged per rank and exchanged with one NCCL all-gather; the
+    time is the max over
     ranks (strong scaling: the total S is fixed)."""
     from kudahitam import dist as khdist
     from kudahitam import ops
@@ -611,7 +612,7 @@ def decode_bench(dev, args, world: int = 1, rank: int = 0) -> dict:
     bytes_step = G * DEC_S * DEC_BYTES_PER_ROW  # whole job
     peak, _ = peaks()
     return {"config": "q bf16 [32,16,128]; K and V 2-bit-mode packed, S=40000"
-                      + (f", sequence-sharded over {world} GPUs + one NCCL all-reduce"
+                      + (f", sequence-sharded over {world} GPUs + one NCCL all-gather"
                          if world > 1 else ""),
             "us_per_step": ms * 1e3, "us_per_token": ms * 1e3 / DEC_B,
             "n_splits": n_splits, "scaling": "strong" if world > 1 else None,

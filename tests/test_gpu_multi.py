@@ -2,9 +2,9 @@
 Skipped when fewer than two GPUs are visible.
 
 * sequence-sharded decode: every rank holds S/N cached rows per group, runs
-  the split-K partial kernel into its slots and the records are combined by
-  one all-reduce; the result must equal the single-GPU decode of the whole
-  cache;
+  the split-K partial kernel, merges its splits into one record per query row
+  and the records are exchanged by one all-gather; the result must equal the
+  single-GPU decode of the whole cache;
 * row-sharded compression: ranks compress disjoint batch x head slices with
   no communication; the union must equal the single-GPU result bit for bit."""
 import datetime
