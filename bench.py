@@ -566,8 +566,7 @@ def decode_bench(dev, args, world: int = 1, rank: int = 0) -> dict:
     """Decode step over the 40k-token compressed cache.  With N ranks the
     sequence is sharded (S/N rows per group on each rank) and the split-K
     records are merged per rank and exchanged with one NCCL all-gather; the
-    time is the max over
-    ranks (strong scaling: the total S is fixed)."""
+    time is the max over ranks (strong scaling: the total S is fixed)."""
     from kudahitam import dist as khdist
     from kudahitam import ops
     from kudahitam.codebook import lloyd_max, rademacher
