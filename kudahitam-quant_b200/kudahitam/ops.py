@@ -403,11 +403,23 @@ def decode_workspace_bytes(n_groups: int, n_splits: int, head_dim: int) -> int:
 
 
 def default_splits(n_groups: int, seq_len: int, device) -> int:
-    """About 8 waves of (group, split) blocks at 2 blocks per SM, with at
-    least 1024 rows per split."""
+    """Splits per query row for decode: enough (row, split) blocks for about
+    three waves at two blocks per SM, but no split shorter than 4096 rows.
+    A block's set-up (query transform, byte table, per-segment reductions and
+    fold) is paid once per split, so short splits cost more than the waves
+    they fill.  Measured on one B200 with 512 query rows (D = 128, us for
+    partial + combine; the rule's choice starred):
+
+        S       1 split   2        4        5
+        5000    60.7*     64.8     81.2     85.3
+        10000   107.8     99.6*    114.0    120.3
+        20000   195.7     181.9*   181.6    194.2
+        40000   367.7     339.2*   343.1    339.2
+    """
     sms = torch.cuda.get_device_properties(device).multi_processor_count
-    want = max(1, round(16 * sms / max(n_groups, 1)))
-    return int(max(1, min(want, seq_len // 1024 if seq_len >= 1024 else 1, 1024)))
+    fill = -(-3 * 2 * sms // max(n_groups, 1))  # ceil(3 waves of 2 blocks per SM / rows)
+    by_rows = max(1, seq_len // 4096)
+    return int(max(1, min(fill, by_rows, 1024)))
 
 
 def decode_partial(q: torch.Tensor, k: PackedKV, v: PackedKV, dk, dv, centroids,
