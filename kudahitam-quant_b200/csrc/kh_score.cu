@@ -10,6 +10,7 @@
 //   score = norm (c0 Q + (c1 - c0) M1) + r_norm / sqrt(D) (2 M2 - Q).
 // Two-level codebooks take the table-driven kernel (score_tab_kernel); the
 // 4-level codebook (and KUDAHITAM_SCORE_PATH=direct) the direct one.
+#include <algorithm>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -33,6 +34,7 @@ struct alignas(16) ScoreParams {
   const float* rnorms;
   float* out;
   int64_t seq_len;
+  int64_t chunk;  // cached rows per CTA (table path)
   int n_q;
   Codebook cb;
   float d[256];
@@ -144,15 +146,19 @@ __global__ void __launch_bounds__(kScoreThreads)
 // sums of q~ over the set bits of a plane, so one byte table serves both:
 // T[v][slot] = sum of q~ over the set bits of byte value v at the slot's byte
 // position.  A row costs D/8 lookups per plane instead of D bit-selects.
-// One CTA serves one query row (query j of cache group g) and kRows cached
-// rows, so the query transform and the table are built once per kRows rows.
+// One CTA serves one query row (query j of cache group g) and P.chunk cached
+// rows, so the query transform and the table are built once per chunk.  The
+// host picks chunks like the decode splits: about three waves of CTAs at two
+// per SM, no chunk shorter than 4096 rows, equal chunk lengths.  With 512
+// query rows this matches fixed 8192-row chunks (160 us at 40000 rows on one
+// B200); with few query rows (one sequence of 32 heads) it fills the GPU
+// where 8192-row chunks would launch under one wave.
 // Table rows are 256 bytes apart (slots 0..31 used) so that one byte-permute
 // forms each lookup address (see tab_addr).
 template <int D>
 struct ScoreTabCfg {
   static constexpr int kP = D / 8;
   static constexpr int kThreads = 256;
-  static constexpr int kRows = 8192;   // cached rows per CTA
   static constexpr int kBatch = 2;  // rows per thread per batch
   // batches in the register ring: kRing - 1 batches are loading while one
   // is scored
@@ -182,8 +188,8 @@ __global__ void __launch_bounds__(256, 2)
   const int lane = t & 31;
   const int64_t y = blockIdx.y;      // query row: cache group y / n_q
   const int64_t gk = y / P.n_q;
-  const int64_t s0 = (int64_t)blockIdx.x * C::kRows;
-  const int n = (int)min((int64_t)C::kRows, P.seq_len - s0);
+  const int64_t s0 = (int64_t)blockIdx.x * P.chunk;
+  const int n = (int)min(P.chunk, P.seq_len - s0);
   const int64_t row0 = gk * P.seq_len + s0;
   const float inv_sqrt_d = 1.0f / sqrtf((float)D);
   const float c0 = P.cb.c[0], dc = P.cb.c[1] - P.cb.c[0];
@@ -294,12 +300,18 @@ kh_status launch_score(const float* q, int64_t n_groups, int n_q, int D,
   for (int i = 0; i < D; ++i) P.d[i] = d[i];
   const char* env = getenv("KUDAHITAM_SCORE_PATH");
   if (cb.n_c == 2 && !(env && strcmp(env, "direct") == 0)) {
-    // table-driven path: one CTA per (8192 cached rows, query row)
+    // table-driven path: one CTA per (chunk of cached rows, query row)
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return KH_ECUDA;
-    const int64_t bxt = (seq_len + 8191) / 8192;
     const int64_t rows_q = n_groups * (int64_t)n_q;
-    if (bxt > 0x7fffffff || rows_q >= 65536) return KH_EINVAL;
+    if (rows_q >= 65536) return KH_EINVAL;
+    const int64_t fill = (6 * (int64_t)sm_count() + rows_q - 1) / rows_q;
+    const int64_t chunks = std::max<int64_t>(1, std::min(fill, seq_len / 4096));
+    // equal chunks, rounded up to whole batches of rows (256 threads x 2)
+    P.chunk = ((seq_len + chunks - 1) / chunks + 511) / 512 * 512;
+    if (P.chunk > 0x7fffffff) return KH_EINVAL;  // a CTA's row count is an int
+    const int64_t bxt = (seq_len + P.chunk - 1) / P.chunk;
+    if (bxt > 0x7fffffff) return KH_EINVAL;
     const dim3 gridt((unsigned)bxt, (unsigned)rows_q);
     static std::once_flag once[4][64];
     auto launch = [&](auto kern, int slot, int smem) {
