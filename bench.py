@@ -54,7 +54,7 @@ FALLBACK_HBM_GBS = 6650.0
 NCU_TRAFFIC_BYTES_PER_ROW = (268.480256e6 + 8.786688e6) / 524288
 # Same for the decode step (profiles/decode_v3_q32x16_s40000.md): bytes per
 # cached row of K and V, on the bench's decode workload itself.
-NCU_DECODE_TRAFFIC_BYTES_PER_ROW = (1.745463e9 + 4.798208e6) / (512 * 40000)
+NCU_DECODE_TRAFFIC_BYTES_PER_ROW = (1.725821e9 + 4.288e6) / (512 * 40000)
 
 
 def peaks() -> tuple[float, str]:
