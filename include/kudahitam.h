@@ -239,6 +239,34 @@ int kh_decode_merge(const float* partials, int64_t n_groups, int n_parts,
                     int64_t group_stride, int64_t part_stride, int head_dim,
                     float* merged, void* stream);
 
+/* Sequence-sharded decode with the record exchange fused into the merge, over
+ * peer memory (no counterpart in the reference, which has no decode; this
+ * replaces kh_decode_merge + an all-gather + kh_decode_combine_strided).
+ * Every rank holds a record buffer [world][n_groups][D+2] and a flag array
+ * [world] (uint32, zero before the first call) that all ranks can address
+ * (peer or symmetric memory), and a local counter word (zero before the
+ * first call).
+ * kh_decode_merge_to_peers merges this rank's n_parts split records per
+ * group (strides as in kh_decode_merge) and stores the merged record into
+ * slot [rank] of every rank's record buffer (peer_records[r] = rank r's
+ * buffer, a host array of world device pointers); its last CTA then stores
+ * epoch into slot [rank] of every rank's flag array (peer_flags[r]).
+ * kh_decode_combine_from_peers waits until all world local flags equal
+ * epoch, then writes out[g][D] like kh_decode_combine.  Its wait gives up
+ * after about a second, sets bit 2 of kh_device_error() and writes zeros.
+ * epoch must be non-zero and differ from the flags' current value; callers
+ * alternate two buffer/flag sets between consecutive calls (a rank may be one
+ * call ahead of a peer) and increase epoch every call.  world <= 8. */
+int kh_decode_merge_to_peers(const float* partials, int64_t n_groups, int n_parts,
+                             int64_t group_stride, int64_t part_stride, int head_dim,
+                             float* const* peer_records, uint32_t* const* peer_flags,
+                             int rank, int world, uint32_t epoch, uint32_t* counter,
+                             void* stream);
+
+int kh_decode_combine_from_peers(const float* records, const uint32_t* flags, uint32_t epoch,
+                                 int64_t n_groups, int world, int head_dim,
+                                 const float* d_v_host, float* out, void* stream);
+
 int kh_decode_attn(const float* q, int64_t n_groups, int head_dim,
                    const uint32_t* k_code, const uint32_t* k_res,
                    const float* k_norms, const float* k_rnorms,

@@ -417,6 +417,39 @@ int kh_decode_merge(const float* partials, int64_t n_groups, int n_parts,
                                static_cast<cudaStream_t>(stream));
 }
 
+int kh_decode_merge_to_peers(const float* partials, int64_t n_groups, int n_parts,
+                             int64_t group_stride, int64_t part_stride, int head_dim,
+                             float* const* peer_records, uint32_t* const* peer_flags,
+                             int rank, int world, uint32_t epoch, uint32_t* counter,
+                             void* stream) {
+  if (n_groups < 0 || n_parts < 1 || !valid_head_dim(head_dim)) return KH_EINVAL;
+  if (group_stride < 0 || part_stride < 0) return KH_EINVAL;
+  if (world < 1 || world > 8 || rank < 0 || rank >= world || epoch == 0) return KH_EINVAL;
+  if (n_groups == 0) return KH_OK;
+  if (!partials || !peer_records || !peer_flags || !counter) return KH_EINVAL;
+  for (int p = 0; p < world; ++p) {
+    if (!peer_records[p] || !peer_flags[p]) return KH_EINVAL;
+    if (!aligned4(peer_records[p]) || !aligned4(peer_flags[p])) return KH_EALIGN;
+  }
+  if (!aligned4(partials) || !aligned4(counter)) return KH_EALIGN;
+  return launch_decode_merge_to_peers(partials, n_groups, n_parts, group_stride, part_stride,
+                                      head_dim, peer_records, peer_flags, rank, world, epoch,
+                                      counter, static_cast<cudaStream_t>(stream));
+}
+
+int kh_decode_combine_from_peers(const float* records, const uint32_t* flags, uint32_t epoch,
+                                 int64_t n_groups, int world, int head_dim,
+                                 const float* d_v_host, float* out, void* stream) {
+  if (n_groups < 0 || world < 1 || world > 8 || epoch == 0 || !valid_head_dim(head_dim))
+    return KH_EINVAL;
+  if (!check_d(d_v_host, head_dim)) return KH_EINVAL;
+  if (n_groups == 0) return KH_OK;
+  if (!records || !flags || !out) return KH_EINVAL;
+  if (!aligned4(records) || !aligned4(flags) || !aligned4(out)) return KH_EALIGN;
+  return launch_decode_combine_from_peers(records, flags, epoch, n_groups, world, head_dim,
+                                          d_v_host, out, static_cast<cudaStream_t>(stream));
+}
+
 int kh_decode_attn(const float* q, int64_t n_groups, int head_dim,
                    const uint32_t* k_code, const uint32_t* k_res,
                    const float* k_norms, const float* k_rnorms,

@@ -20,6 +20,7 @@ namespace kh {
 enum : uint32_t {
   kErrWaitTimeout = 1u << 0,   // an mbarrier wait gave up
   kErrBadSegment = 1u << 1,    // tile index fell outside every segment
+  kErrPeerTimeout = 1u << 2,   // a peer's record flag did not arrive in time
 };
 
 // The error word lives in kh_api.cu; kernels receive its address.

@@ -210,6 +210,135 @@ __global__ void __launch_bounds__(D)
 
 
 // ---------------------------------------------------------------------------
+// Sequence-sharded decode: the record exchange fused into the merge, over
+// peer memory.  Every rank's merge kernel stores its merged record of each
+// query row straight into slot [rank] of every rank's record buffer (plain
+// stores to peer addresses over NVLink), fences, and the last CTA to finish
+// raises this call's epoch in slot [rank] of every rank's flag array.  The
+// combine kernel waits (bounded) until all world flags carry the epoch, then
+// merges the world records of its row from local memory.
+constexpr int kMaxPeers = 8;
+
+struct PeerParams {
+  float* rec[kMaxPeers];     // rank r's record buffer [world][n_rows][D+2]
+  uint32_t* flag[kMaxPeers]; // rank r's flag array [world]
+};
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+template <int D>
+__global__ void __launch_bounds__(D)
+    decode_merge_to_peers_kernel(const float* __restrict__ parts, int n_parts, int64_t gs,
+                                 int64_t ps, int64_t n_rows, int rank, int world,
+                                 uint32_t epoch, uint32_t* counter,
+                                 const __grid_constant__ PeerParams Q) {
+  const int t = threadIdx.x;
+  const int64_t g = blockIdx.x;
+  const float* base = parts + g * gs;
+  float M = -INFINITY;
+  for (int r = 0; r < n_parts; ++r) {
+    const float* rec = base + (int64_t)r * ps;
+    if (rec[1] > 0.f) M = fmaxf(M, rec[0]);
+  }
+  float L = 0.f, a = 0.f;
+  for (int r = 0; r < n_parts; ++r) {
+    const float* rec = base + (int64_t)r * ps;
+    if (rec[1] > 0.f) {
+      const float e = expf(rec[0] - M);
+      L += rec[1] * e;
+      a += rec[2 + t] * e;
+    }
+  }
+  const int64_t off = ((int64_t)rank * n_rows + g) * (D + 2);
+  for (int p = 0; p < world; ++p) {
+    float* dst = Q.rec[p] + off;
+    dst[2 + t] = a;
+    if (t == 0) {
+      dst[0] = M;
+      dst[1] = L;
+    }
+  }
+  __threadfence_system();  // this thread's peer stores before the count below
+  __syncthreads();
+  if (t == 0) {
+    const uint32_t done = atomicAdd(counter, 1u);
+    if (done == (uint32_t)(n_rows - 1)) {  // the last CTA: every row is stored
+      atomicExch(counter, 0u);             // ready for the next call
+      __threadfence_system();
+      for (int p = 0; p < world; ++p) st_release_sys(Q.flag[p] + rank, epoch);
+    }
+  }
+}
+
+template <int D>
+__global__ void __launch_bounds__(D)
+    decode_combine_from_peers_kernel(const float* __restrict__ recs, const uint32_t* flags,
+                                     uint32_t epoch, int64_t n_rows, int world,
+                                     float* __restrict__ out, uint32_t* err,
+                                     const __grid_constant__ DecodeParams P) {
+  __shared__ float sh[D];
+  __shared__ int ok;
+  const int t = threadIdx.x;
+  const int64_t g = blockIdx.x;
+  if (t == 0) {
+    int good = 1;
+    const long long t0 = clock64();
+    for (int r = 0; r < world && good; ++r) {
+      while (ld_acquire_sys(flags + r) != epoch) {
+        if (clock64() - t0 > (1ll << 31)) {  // about a second: give up
+          flag_error(err, kErrPeerTimeout);
+          good = 0;
+          break;
+        }
+      }
+    }
+    ok = good;
+  }
+  __syncthreads();
+  if (!ok) {
+    out[g * D + t] = 0.f;
+    return;
+  }
+  // peers' records arrived over NVLink into this GPU's L2: read them there
+  const int64_t ps = n_rows * (D + 2);
+  const float* base = recs + g * (D + 2);
+  float M = -INFINITY;
+  for (int r = 0; r < world; ++r) {
+    const float* rec = base + (int64_t)r * ps;
+    if (__ldcg(rec + 1) > 0.f) M = fmaxf(M, __ldcg(rec));
+  }
+  float L = 0.f, a = 0.f;
+  for (int r = 0; r < world; ++r) {
+    const float* rec = base + (int64_t)r * ps;
+    const float l = __ldcg(rec + 1);
+    if (l > 0.f) {
+      const float e = expf(__ldcg(rec) - M);
+      L += l * e;
+      a += __ldcg(rec + 2 + t) * e;
+    }
+  }
+  sh[t] = a;
+  __syncthreads();
+  for (int h = 1; h < D; h <<= 1) {
+    if (t < D / 2) {
+      const int lo = (t / h) * 2 * h + (t % h);
+      const float x = sh[lo], y = sh[lo + h];
+      sh[lo] = x + y;
+      sh[lo + h] = x - y;
+    }
+    __syncthreads();
+  }
+  out[g * D + t] = L > 0.f ? sh[t] * P.dk[t] / L : 0.f;
+}
+
+// ---------------------------------------------------------------------------
 // Decode v2: table-driven.  Both planes of a row are read as bytes.
 //
 // K side: per CTA (one query) a table holds, for every byte position p of a
@@ -984,6 +1113,46 @@ kh_status launch_decode_combine(const float* partials, int64_t n_groups, int n_p
     if (records) go(decode_combine_kernel<256, true>, 256);
     else go(decode_combine_kernel<256, false>, 256);
   }
+  return cudaGetLastError() == cudaSuccess ? KH_OK : KH_ELAUNCH;
+}
+
+kh_status launch_decode_merge_to_peers(const float* partials, int64_t n_rows, int n_parts,
+                                      int64_t group_stride, int64_t part_stride, int D,
+                                      float* const* peer_records, uint32_t* const* peer_flags,
+                                      int rank, int world, uint32_t epoch, uint32_t* counter,
+                                      cudaStream_t stream) {
+  if (world < 1 || world > kMaxPeers || n_rows > 0x7fffffff) return KH_EINVAL;
+  PeerParams Q;
+  memset(&Q, 0, sizeof(Q));
+  for (int p = 0; p < world; ++p) {
+    Q.rec[p] = peer_records[p];
+    Q.flag[p] = peer_flags[p];
+  }
+  const dim3 grid((unsigned)n_rows);
+  if (D == 128)
+    decode_merge_to_peers_kernel<128><<<grid, 128, 0, stream>>>(
+        partials, n_parts, group_stride, part_stride, n_rows, rank, world, epoch, counter, Q);
+  else
+    decode_merge_to_peers_kernel<256><<<grid, 256, 0, stream>>>(
+        partials, n_parts, group_stride, part_stride, n_rows, rank, world, epoch, counter, Q);
+  return cudaGetLastError() == cudaSuccess ? KH_OK : KH_ELAUNCH;
+}
+
+kh_status launch_decode_combine_from_peers(const float* records, const uint32_t* flags,
+                                           uint32_t epoch, int64_t n_rows, int world, int D,
+                                           const float* dv, float* out, cudaStream_t stream) {
+  if (world < 1 || world > kMaxPeers || n_rows > 0x7fffffff) return KH_EINVAL;
+  DecodeParams P;
+  memset(&P, 0, sizeof(P));
+  for (int i = 0; i < D; ++i) P.dk[i] = dv[i];
+  const dim3 grid((unsigned)n_rows);
+  uint32_t* err = device_error_ptr();
+  if (D == 128)
+    decode_combine_from_peers_kernel<128><<<grid, 128, 0, stream>>>(records, flags, epoch, n_rows,
+                                                                    world, out, err, P);
+  else
+    decode_combine_from_peers_kernel<256><<<grid, 256, 0, stream>>>(records, flags, epoch, n_rows,
+                                                                    world, out, err, P);
   return cudaGetLastError() == cudaSuccess ? KH_OK : KH_ELAUNCH;
 }
 

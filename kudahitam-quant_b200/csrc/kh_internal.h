@@ -101,6 +101,16 @@ kh_status launch_decode_combine(const float* partials, int64_t n_groups, int n_p
                                 const float* dv, bool records, float* out,
                                 cudaStream_t stream);
 
+// Fused record exchange of a sequence-sharded decode (world <= 8 ranks).
+kh_status launch_decode_merge_to_peers(const float* partials, int64_t n_rows, int n_parts,
+                                      int64_t group_stride, int64_t part_stride, int D,
+                                      float* const* peer_records, uint32_t* const* peer_flags,
+                                      int rank, int world, uint32_t epoch, uint32_t* counter,
+                                      cudaStream_t stream);
+kh_status launch_decode_combine_from_peers(const float* records, const uint32_t* flags,
+                                           uint32_t epoch, int64_t n_rows, int world, int D,
+                                           const float* dv, float* out, cudaStream_t stream);
+
 // Device address of the sticky error word on the current device.
 uint32_t* device_error_ptr();
 

@@ -60,14 +60,75 @@ def seq_sharded_workspace_numel(n_rows: int, n_splits: int, world: int, head_dim
     return n_rows * (head_dim + 2) * (n_splits + extra)
 
 
+class PeerRecordExchange:
+    """Buffers for the fused record exchange of a sequence-sharded decode
+    (``kh_decode_merge_to_peers`` / ``kh_decode_combine_from_peers``): one
+    symmetric-memory allocation per rank, addressable by every rank over
+    NVLink, holding two sets (alternating between calls) of a record buffer
+    [world, n_rows, D+2] and a flag array [world], plus a local counter.
+    Collective to create: every rank of the group builds one with the same
+    arguments.  world <= 8."""
+
+    def __init__(self, n_rows: int, head_dim: int, group=None, device=None):
+        import torch.distributed._symmetric_memory as symm
+        world, rank = _world(group)
+        if world > 8:
+            raise ValueError("the peer record exchange supports at most 8 ranks")
+        dev = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+        self.world, self.rank, self.n_rows, self.head_dim = world, rank, n_rows, head_dim
+        self.rec_bytes = world * n_rows * (head_dim + 2) * 4
+        self.flag_off = 2 * self.rec_bytes
+        total = self.flag_off + 2 * world * 4
+        total = (total + 255) // 256 * 256
+        self.buf = symm.empty(total, dtype=torch.uint8, device=dev)
+        self.buf.zero_()
+        self.counter = torch.zeros(1, dtype=torch.int32, device=dev)
+        torch.cuda.synchronize(dev)
+        grp = group if group is not None else dist.group.WORLD
+        self.handle = symm.rendezvous(self.buf, grp)
+        self.handle.barrier()  # every rank's buffer is zero before any peer store
+        self.ptrs = [int(p) for p in self.handle.buffer_ptrs]
+        self.epoch = 0
+
+    def combine(self, local: torch.Tensor, dv, out: torch.Tensor) -> torch.Tensor:
+        """local: this rank's [R, P, D+2] split records; out: [R, D] (any
+        shape of R * D floats).  Merges, exchanges and combines."""
+        import ctypes
+        from . import _lib
+        R, P, gs, ps = ops._record_view(local, self.head_dim)
+        if R != self.n_rows:
+            raise ValueError(f"exchange built for {self.n_rows} rows, got {R}")
+        self.epoch = self.epoch + 1 if self.epoch < 0xFFFFFFFF else 1
+        par = self.epoch & 1
+        w = self.world
+        recs = (ctypes.c_void_p * w)(*[p + par * self.rec_bytes for p in self.ptrs])
+        flags = (ctypes.c_void_p * w)(*[p + self.flag_off + par * w * 4 for p in self.ptrs])
+        dvh = ops._host_f32(dv)
+        dev = local.device
+        with ops._on(dev):
+            st = ops._stream(dev)
+            _lib.call("kh_decode_merge_to_peers", ops._vp(local), R, P, gs, ps, self.head_dim,
+                      ctypes.cast(recs, ctypes.c_void_p), ctypes.cast(flags, ctypes.c_void_p),
+                      self.rank, w, self.epoch, ops._vp(self.counter), st)
+            mine = self.ptrs[self.rank]
+            _lib.call("kh_decode_combine_from_peers", mine + par * self.rec_bytes,
+                      mine + self.flag_off + par * w * 4, self.epoch, R, w, self.head_dim,
+                      ops._vp(dvh), ops._vp(out), st)
+        return out
+
+
 def decode_attention_seq_sharded(q: torch.Tensor, k_local: ops.PackedKV,
                                  v_local: ops.PackedKV, dk, dv, centroids,
                                  sm_scale: Optional[float] = None,
                                  n_splits: Optional[int] = None, group=None,
-                                 partials: Optional[torch.Tensor] = None) -> torch.Tensor:
+                                 partials: Optional[torch.Tensor] = None,
+                                 exchange: Optional[PeerRecordExchange] = None) -> torch.Tensor:
     """Decode attention where each rank holds S_local cached rows per group
     (k_local / v_local: G * S_local rows).  q is [G, D] or [G, n_q, D]
-    (grouped-query heads).  Returns float32 with q's shape on every rank."""
+    (grouped-query heads).  Returns float32 with q's shape on every rank.
+    With ``exchange`` (a PeerRecordExchange of this group and shape) the
+    records cross NVLink inside the merge kernel instead of one NCCL
+    all-gather."""
     world, _ = _world(group)
     G, D = q.shape[0], q.shape[-1]
     R = q.numel() // D  # query rows: G * n_q
@@ -86,6 +147,8 @@ def decode_attention_seq_sharded(q: torch.Tensor, k_local: ops.PackedKV,
     out = torch.empty(q.shape, dtype=torch.float32, device=q.device)
     if world == 1:
         return ops.decode_combine(local, n_splits, dv, out)
+    if exchange is not None:
+        return exchange.combine(local, dv, out)
     off = R * n_splits * rec
     merged = partials[off: off + R * rec].view(R, rec)
     ops.decode_merge(local, merged)

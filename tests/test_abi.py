@@ -111,6 +111,24 @@ def test_other_entry_points_validate():
                                        None) == _lib.KH_EINVAL
     assert L.kh_decode_combine_strided(FAKE, 2, 2, 260, 130, 128, None, FAKE,
                                        None) == _lib.KH_EINVAL  # no d vector
+    two = (ctypes.c_void_p * 2)(0x10000, 0x20000)
+    P2 = ctypes.cast(two, ctypes.c_void_p)
+    assert L.kh_decode_merge_to_peers(FAKE, 2, 2, 260, 130, 128, P2, P2, 0, 9, 1, FAKE,
+                                      None) == _lib.KH_EINVAL  # world > 8
+    assert L.kh_decode_merge_to_peers(FAKE, 2, 2, 260, 130, 128, P2, P2, 2, 2, 1, FAKE,
+                                      None) == _lib.KH_EINVAL  # rank >= world
+    assert L.kh_decode_merge_to_peers(FAKE, 2, 2, 260, 130, 128, P2, P2, 0, 2, 0, FAKE,
+                                      None) == _lib.KH_EINVAL  # epoch 0
+    assert L.kh_decode_merge_to_peers(FAKE, 2, 2, 260, 130, 128, P2, P2, 0, 2, 1, None,
+                                      None) == _lib.KH_EINVAL  # no counter
+    assert L.kh_decode_merge_to_peers(FAKE, 0, 2, 260, 130, 128, P2, P2, 0, 2, 1, FAKE,
+                                      None) == _lib.KH_OK
+    assert L.kh_decode_combine_from_peers(FAKE, FAKE, 0, 2, 2, 128, D128, FAKE,
+                                          None) == _lib.KH_EINVAL  # epoch 0
+    assert L.kh_decode_combine_from_peers(FAKE, FAKE, 1, 2, 2, 128, None, FAKE,
+                                          None) == _lib.KH_EINVAL  # no d vector
+    assert L.kh_decode_combine_from_peers(FAKE, FAKE, 1, 0, 2, 128, D128, FAKE,
+                                          None) == _lib.KH_OK
 
 
 def test_gqa_decode_and_compat_scorer_validate():

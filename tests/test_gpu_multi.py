@@ -5,6 +5,9 @@ Skipped when fewer than two GPUs are visible.
   the split-K partial kernel, merges its splits into one record per query row
   and the records are exchanged by one all-gather; the result must equal the
   single-GPU decode of the whole cache;
+* the same decode with the record exchange fused into the merge kernel over
+  peer memory (symmetric memory, NVLink stores and flags) must equal the
+  all-gather path bit for bit, call after call;
 * row-sharded compression: ranks compress disjoint batch x head slices with
   no communication; the union must equal the single-GPU result bit for bit."""
 import datetime
@@ -52,12 +55,27 @@ def _worker(rank, world, port, q):
                                     c, 1 / math.sqrt(D), n_splits=3 * world)
         torch.cuda.synchronize()
         err = ((got - full).abs().max() / full.abs().max()).item()
+        # the same step with the record exchange fused into the merge over
+        # peer memory: bitwise the NCCL result, over calls that alternate the
+        # two buffer sets
+        from kudahitam import _lib
+        ex = khdist.PeerRecordExchange(G, D, device=dev)
+        peer_same = True
+        for _ in range(5):
+            alt = khdist.decode_attention_seq_sharded(qv, pk, pv, dk, dv, c, 1 / math.sqrt(D),
+                                                      n_splits=3, exchange=ex)
+            torch.cuda.synchronize()
+            peer_same = peer_same and torch.equal(alt, got)
+        peer_same = peer_same and _lib.device_error() == 0
+        del ex
+        torch.cuda.synchronize()
+        dist.barrier()
         # compression shards: no communication, bit-identical to the whole
         ra, rb = khdist.shard_range(G, world, rank)
         mine = ops.compress(k[ra:rb], dk, c)
         ref = ops.compress(k, dk, c).rows(ra * S, rb * S)
         same = torch.equal(mine.code, ref.code) and torch.equal(mine.res, ref.res)
-        q.put(("ok", rank, err, same))
+        q.put(("ok", rank, err, same and peer_same))
     except Exception as e:  # pragma: no cover - reported to the parent
         q.put(("fail", rank, repr(e), False))
     finally:
