@@ -52,7 +52,10 @@ const char* kh_status_string(int status);
 int kh_version(void);
 
 /* Sticky device-side error word of the current device (bounded waits that
- * gave up set a bit).  Synchronous: reads device memory.  0 = no error. */
+ * gave up set a bit).  Synchronous: reads device memory.  0 = no error.
+ * Bit 0: an mbarrier wait of a compressor gave up; bit 1: a tile index fell
+ * outside every segment; bit 2: kh_decode_combine_from_peers stopped waiting
+ * for a peer's flag. */
 int kh_device_error(uint32_t* out_flags);
 int kh_clear_device_error(void);
 
