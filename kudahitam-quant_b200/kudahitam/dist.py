@@ -67,7 +67,9 @@ class PeerRecordExchange:
     NVLink, holding two sets (alternating between calls) of a record buffer
     [world, n_rows, D+2] and a flag array [world], plus a local counter.
     Collective to create: every rank of the group builds one with the same
-    arguments.  world <= 8."""
+    arguments, and every rank must make the same sequence of ``combine``
+    calls.  Release it (``del``) after a device synchronisation and before
+    ``destroy_process_group``.  world <= 8."""
 
     def __init__(self, n_rows: int, head_dim: int, group=None, device=None):
         import torch.distributed._symmetric_memory as symm
