@@ -417,7 +417,12 @@ def default_splits(n_groups: int, seq_len: int, device) -> int:
         40000   367.7     339.2*   343.1    339.2
     """
     sms = torch.cuda.get_device_properties(device).multi_processor_count
-    fill = -(-3 * 2 * sms // max(n_groups, 1))  # ceil(3 waves of 2 blocks per SM / rows)
+    return splits_for(n_groups, seq_len, sms)
+
+
+def splits_for(n_rows: int, seq_len: int, n_sms: int) -> int:
+    """The split rule of ``default_splits`` for a GPU with n_sms SMs."""
+    fill = -(-3 * 2 * n_sms // max(n_rows, 1))  # ceil(3 waves of 2 blocks per SM / rows)
     by_rows = max(1, seq_len // 4096)
     return int(max(1, min(fill, by_rows, 1024)))
 

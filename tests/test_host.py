@@ -63,3 +63,14 @@ def test_lloyd_max_other_dims_sorted_symmetric():
             c = lloyd_max(bits, D).numpy()
             assert np.all(np.diff(c) > 0)
             assert np.allclose(c, -c[::-1], atol=1e-9)
+
+
+def test_decode_split_rule():
+    """The decode split rule on a 148-SM GPU: about three waves of (row,
+    split) blocks at two per SM, no split under 4096 rows, at least one."""
+    from kudahitam.ops import splits_for
+    assert [splits_for(512, s, 148) for s in (5000, 10000, 20000, 40000)] == [1, 2, 2, 2]
+    assert splits_for(32, 40000, 148) == 9      # one sequence: more splits fill the GPU
+    assert splits_for(1024, 131072, 148) == 1   # many rows already fill three waves
+    assert splits_for(512, 100, 148) == 1 and splits_for(0, 0, 148) == 1
+    assert splits_for(1, 10 ** 9, 148) == 888   # capped by the waves, not the 1024 cap
