@@ -45,15 +45,15 @@ DEC_B, DEC_H, DEC_S, DEC_D = 32, 16, 40000, 128
 DEC_BYTES_PER_ROW = 2 * (2 * DEC_D // 8 + 8)  # K and V: 2 planes + 2 norms each
 FALLBACK_HBM_GBS = 6650.0
 
-# dram__bytes_read.sum + dram__bytes_write.sum per compressed row, from the ncu
-# capture in profiles/compress_tc_fp16_d256_2bit.md (524,288 rows of the same
-# row format): 268.48 MB read + 8.79 MB written.  Reads equal the algorithmic
+# dram__bytes_read.sum + dram__bytes_write.sum per compressed row, from an ncu
+# capture of compress_tc_kernel<__half,256> on 524,288 rows of the same row
+# format: 268.48 MB read + 8.79 MB written.  Reads equal the algorithmic
 # bytes; most of the packed output is still in L2 when the kernel ends, so
 # the DRAM write count is below the 72 B/row written.  Traffic grows in
 # proportion to the rows, so it is scaled to a full launch.
 NCU_TRAFFIC_BYTES_PER_ROW = (268.480256e6 + 8.786688e6) / 524288
-# Same for the decode step (profiles/decode_v3_q32x16_s40000.md): bytes per
-# cached row of K and V, on the bench's decode workload itself.
+# Same for the decode step (an ncu capture of decode_v3_kernel<128> on the
+# bench's decode workload itself): bytes per cached row of K and V.
 NCU_DECODE_TRAFFIC_BYTES_PER_ROW = (1.725821e9 + 4.288e6) / (512 * 40000)
 
 
@@ -178,50 +178,84 @@ def max_over_ranks(v: float, world: int) -> float:
     return m(v, device=torch.device("cuda", torch.cuda.current_device()))
 
 
-def cpu_baseline_run(target_s: float = 10.0, max_rows: int = 1 << 22) -> dict:
-    """The oracle port on a bounded sample of the workload, all host threads."""
-    from oracle import oracle as O
-    from kudahitam.codebook import lloyd_max, rademacher
-    rng = np.random.default_rng(2)
-    d = rademacher(D, 1).numpy()
-    c = lloyd_max(1, D).numpy()
+def host_cores() -> int:
+    """Host threads this process may run on (torch.distributed.run sets
+    OMP_NUM_THREADS=1 in every rank; the CPU baseline passes this count to
+    the oracle explicitly instead of inheriting that)."""
+    try:
+        return len(os.sched_getaffinity(0))
+    except (AttributeError, OSError):  # pragma: no cover
+        return os.cpu_count() or 1
 
-    def sample(n):
-        x = rng.standard_normal((n, D)).astype(np.float32)
+
+class CpuSample:
+    """A bounded sample of the workload's fp16 rows for the CPU baseline,
+    generated once (the same distribution: N(0,1) with 2 % Student-t(3)
+    channels) and compressed by the oracle port (KudaHitamCUDA.cu:13-195
+    restated) on every host core."""
+
+    def __init__(self, target_s: float, max_rows: int = 1 << 22):
+        from oracle import oracle as O
+        from kudahitam.codebook import lloyd_max, rademacher
+        self.O = O
+        self.cores = host_cores()
+        self.d = rademacher(D, 1).numpy()
+        self.c = lloyd_max(1, D).numpy()
+        self.rng = np.random.default_rng(2)
+        probe = self._rows(16384)
+        self.run(probe)  # first touch / thread pool start
+        dt = self.run(probe)
+        n = int(min(max_rows, max(16384, 16384 * target_s / max(dt, 1e-6))))
+        self.x = self._rows(n)
+
+    def _rows(self, n: int) -> np.ndarray:
+        x = self.rng.standard_normal((n, D)).astype(np.float32)
         k = round(0.02 * D)
-        ch = rng.choice(D, k, replace=False)
-        x[:, ch] = rng.standard_t(3, size=(n, k))
+        ch = self.rng.choice(D, k, replace=False)
+        x[:, ch] = self.rng.standard_t(3, size=(n, k))
         return x.astype(np.float16)
 
-    n = 16384
-    x = sample(n)
-    t0 = time.perf_counter()
-    O.compress_v8(x, d, c, want=("norms", "rnorms", "signs", "idx"))
-    dt = time.perf_counter() - t0
-    n2 = int(min(max_rows, max(n, n * target_s / max(dt, 1e-6))))
-    x = sample(n2)
-    t0 = time.perf_counter()
-    O.compress_v8(x, d, c, want=("norms", "rnorms", "signs", "idx"))
-    dt = time.perf_counter() - t0
-    return {"value": n2 / dt, "unit": "rows/s", "cores": O.num_threads(), "kind": "port",
-            "sample": f"{n2} fp16 rows of the D=256 2-bit-mode workload, {dt:.2f} s"}
+    def run(self, x=None) -> float:
+        """Seconds to compress the sample (or x) on every host core."""
+        x = self.x if x is None else x
+        t0 = time.perf_counter()
+        self.O.compress_v8(x, self.d, self.c, want=("norms", "rnorms", "signs", "idx"),
+                           n_threads=self.cores)
+        return time.perf_counter() - t0
+
+    def describe(self, value: float, dt: float) -> dict:
+        return {"value": value, "unit": "rows/s", "cores": self.cores, "kind": "port",
+                "sample": f"{self.x.shape[0]} fp16 rows of the D=256 2-bit-mode workload "
+                          f"(same distribution), {dt:.2f} s per pass"}
+
+
+def cpu_baseline_run(target_s: float = 10.0, max_rows: int = 1 << 22) -> dict:
+    """The oracle port on a bounded sample of the workload, all host threads."""
+    smp = CpuSample(target_s, max_rows)
+    dt = smp.run()
+    return smp.describe(smp.x.shape[0] / dt, dt)
 
 
 def run_reference(args, world, rank):
+    """The reference arm: the CPU restatement of the reference kernel on every
+    host core, rank 0 only (other ranks exit without work).  Each step
+    compresses the same bounded sample of the workload (about 2 s)."""
     if rank != 0:
         return
-    cfg = workload_config(1)
-    vals = []
+    cfg = workload_config(world)  # the engine arm's config at this N
+    smp = CpuSample(target_s=2.0)
+    small = smp.x[:16384]
     for _ in range(args.warmup):
-        cpu_baseline_run(target_s=1.0, max_rows=1 << 16)
-    for _ in range(args.steps):
-        vals.append(cpu_baseline_run(target_s=5.0))
-    v = statistics.median([x["value"] for x in vals])
+        smp.run(small)
+    times = [smp.run() for _ in range(args.steps)]
+    t_med = statistics.median(times)
+    v = smp.x.shape[0] / t_med
     line = {"impl": "reference", "metric": METRIC, "value": v, "unit": "rows/s",
             "n_gpus": args.gpus, "steps": args.steps, "warmup": args.warmup,
+            "ms_per_step": t_med * 1e3, "sample_rows_per_step": smp.x.shape[0],
             "higher_is_better": True, "scaling": "weak", "vs_baseline": None,
             "dtype": "f32", "data": "synthetic", "config": cfg,
-            "cpu_baseline": {**vals[-1], "value": v},
+            "cpu_baseline": smp.describe(v, t_med),
             "e2e": {"value": v, "unit": "rows/s", "h2d_bytes_per_step": 0,
                     "d2h_bytes_per_step": 0}}
     gk = reference_kernel_on_gpu(args)

@@ -51,7 +51,10 @@ const char* kh_status_string(int status);
 /* Library version as MAJOR*10000 + MINOR*100 + PATCH. */
 int kh_version(void);
 
-/* Sticky device-side error word of the current device (bounded waits that
+/* Every entry point launches on `stream`, which must belong to the CURRENT
+ * device (as with any CUDA runtime launch).
+ *
+ * Sticky device-side error word of the current device (bounded waits that
  * gave up set a bit).  Synchronous: reads device memory.  0 = no error.
  * Bit 0: an mbarrier wait of a compressor gave up; bit 1: a tile index fell
  * outside every segment; bit 2: kh_decode_combine_from_peers stopped waiting
@@ -293,7 +296,10 @@ int kh_decode_attn(const float* q, int64_t n_groups, int head_dim,
  * kh_decode_workspace_bytes).  Calls on the same device share the array:
  * calls whose GPU work overlaps race, so order them.  The first call on a
  * device resolves the array's address (cudaGetSymbolAddress) and should come
- * before any stream capture.  Allocates nothing (no cudaMalloc / cudaFree).
+ * before any stream capture.  The array is the CURRENT device's: the stream
+ * must belong to the current device, and a stream of another device is
+ * refused with KH_EINVAL.  n_groups == 0 is a no-op (after the size check).
+ * Allocates nothing (no cudaMalloc / cudaFree).
  */
 #define KH_DECODE_STATIC_SCRATCH_BYTES (4 * 1024 * 1024)
 

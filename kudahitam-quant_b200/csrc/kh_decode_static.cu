@@ -24,7 +24,8 @@
 //
 // The first call on a device resolves the array's device address with
 // cudaGetSymbolAddress, with that device current.  Make that first call
-// before any stream capture.
+// before any stream capture.  The stream must belong to the current device
+// (checked: a stream of another device is refused with KH_EINVAL).
 #include <cuda_runtime.h>
 
 #include <mutex>
@@ -47,10 +48,10 @@ std::mutex g_mu;
 float* g_ptr[kMaxDev] = {};
 
 // Device address of the scratch on the current device (set up once per
-// device); nullptr if the runtime call fails.
-float* scratch_ptr() {
-  int dev = 0;
-  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= kMaxDev) return nullptr;
+// device); nullptr if the runtime call fails.  The address belongs to the
+// current device, so the caller first checks that the stream runs there.
+float* scratch_ptr(int dev) {
+  if (dev < 0 || dev >= kMaxDev) return nullptr;
   std::lock_guard<std::mutex> lk(g_mu);
   if (!g_ptr[dev]) {
     void* p = nullptr;
@@ -74,7 +75,18 @@ extern "C" int kh_decode_attn_static(
   if (need < 0) return KH_EINVAL;
   if (need > KH_DECODE_STATIC_SCRATCH_BYTES) return KH_EINVAL;  // too big for the array
   if (n_groups == 0) return KH_OK;
-  float* scratch = kh::scratch_ptr();
+  // The array's address is per device: resolving it for the current device
+  // while the stream belongs to another GPU would hand that GPU's kernels
+  // an address of the wrong device.  Such a call is refused.
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess) return KH_ECUDA;
+  if (stream) {
+    int sdev = -1;
+    if (cudaStreamGetDevice(static_cast<cudaStream_t>(stream), &sdev) != cudaSuccess)
+      return KH_ECUDA;
+    if (sdev != dev) return KH_EINVAL;
+  }
+  float* scratch = kh::scratch_ptr(dev);
   if (!scratch) return KH_ECUDA;
   const int st = kh_decode_partial(q, n_groups, head_dim, k_code, k_res, k_norms, k_rnorms,
                                    v_code, v_res, v_norms, v_rnorms, seq_len, 0, seq_len,

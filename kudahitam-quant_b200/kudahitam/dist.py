@@ -60,6 +60,14 @@ def seq_sharded_workspace_numel(n_rows: int, n_splits: int, world: int, head_dim
     return n_rows * (head_dim + 2) * (n_splits + extra)
 
 
+def next_epoch(epoch: int) -> int:
+    """Epoch of the peer exchange's next call: 1, 2, ..., 0xFFFFFFFF, then 2.
+    0 is reserved (flags start at 0, "never written").  Wrapping to 2 rather
+    than 1 keeps the parity (which buffer/flag set a call uses) alternating
+    across the wrap, so two consecutive calls never share a set."""
+    return epoch + 1 if epoch < 0xFFFFFFFF else 2
+
+
 class PeerRecordExchange:
     """Buffers for the fused record exchange of a sequence-sharded decode
     (``kh_decode_merge_to_peers`` / ``kh_decode_combine_from_peers``): one
@@ -92,15 +100,24 @@ class PeerRecordExchange:
         self.ptrs = [int(p) for p in self.handle.buffer_ptrs]
         self.epoch = 0
 
-    def combine(self, local: torch.Tensor, dv, out: torch.Tensor) -> torch.Tensor:
+    def combine(self, local: torch.Tensor, dv, out: torch.Tensor,
+                checked: bool = False) -> torch.Tensor:
         """local: this rank's [R, P, D+2] split records; out: [R, D] (any
-        shape of R * D floats).  Merges, exchanges and combines."""
+        shape of R * D floats).  Merges, exchanges and combines.
+
+        If a peer's records do not arrive within about a second, the combine
+        kernel stops waiting, writes ZEROS to ``out`` and sets bit 2 of the
+        library's sticky device error word (``_lib.device_error()``); the
+        call itself returns normally, because the wait runs on the GPU after
+        this function has returned.  With ``checked=True`` the call
+        synchronises the stream, reads that word and raises
+        ``PeerTimeoutError`` (clearing the word) when bit 2 is set."""
         import ctypes
         from . import _lib
         R, P, gs, ps = ops._record_view(local, self.head_dim)
         if R != self.n_rows:
             raise ValueError(f"exchange built for {self.n_rows} rows, got {R}")
-        self.epoch = self.epoch + 1 if self.epoch < 0xFFFFFFFF else 1
+        self.epoch = next_epoch(self.epoch)
         par = self.epoch & 1
         w = self.world
         recs = (ctypes.c_void_p * w)(*[p + par * self.rec_bytes for p in self.ptrs])
@@ -116,7 +133,29 @@ class PeerRecordExchange:
             _lib.call("kh_decode_combine_from_peers", mine + par * self.rec_bytes,
                       mine + self.flag_off + par * w * 4, self.epoch, R, w, self.head_dim,
                       ops._vp(dvh), ops._vp(out), st)
+        if checked:
+            check_peer_timeout(dev)
         return out
+
+
+class PeerTimeoutError(RuntimeError):
+    """A peer-memory record exchange stopped waiting for a peer's records
+    (its output holds zeros)."""
+
+
+def check_peer_timeout(device=None) -> None:
+    """Synchronise ``device`` and raise PeerTimeoutError if a peer-memory
+    combine gave up waiting since the device error word was last cleared
+    (bit 2 of ``kh_device_error``); the word is cleared before raising."""
+    from . import _lib
+    dev = torch.device("cuda", torch.cuda.current_device()) if device is None else device
+    with ops._on(dev):
+        torch.cuda.synchronize(dev)
+        if _lib.device_error() & 4:
+            _lib.call("kh_clear_device_error")
+            raise PeerTimeoutError(
+                "a peer's decode records did not arrive within about a second; the "
+                "combined output was set to zeros")
 
 
 def decode_attention_seq_sharded(q: torch.Tensor, k_local: ops.PackedKV,
@@ -124,13 +163,16 @@ def decode_attention_seq_sharded(q: torch.Tensor, k_local: ops.PackedKV,
                                  sm_scale: Optional[float] = None,
                                  n_splits: Optional[int] = None, group=None,
                                  partials: Optional[torch.Tensor] = None,
-                                 exchange: Optional[PeerRecordExchange] = None) -> torch.Tensor:
+                                 exchange: Optional[PeerRecordExchange] = None,
+                                 checked: bool = False) -> torch.Tensor:
     """Decode attention where each rank holds S_local cached rows per group
     (k_local / v_local: G * S_local rows).  q is [G, D] or [G, n_q, D]
     (grouped-query heads).  Returns float32 with q's shape on every rank.
     With ``exchange`` (a PeerRecordExchange of this group and shape) the
     records cross NVLink inside the merge kernel instead of one NCCL
-    all-gather."""
+    all-gather; if a peer never arrives that path returns zeros and flags
+    bit 2 of the device error word, and ``checked=True`` turns that into a
+    PeerTimeoutError (at the cost of a stream synchronisation)."""
     world, _ = _world(group)
     G, D = q.shape[0], q.shape[-1]
     R = q.numel() // D  # query rows: G * n_q
@@ -150,7 +192,7 @@ def decode_attention_seq_sharded(q: torch.Tensor, k_local: ops.PackedKV,
     if world == 1:
         return ops.decode_combine(local, n_splits, dv, out)
     if exchange is not None:
-        return exchange.combine(local, dv, out)
+        return exchange.combine(local, dv, out, checked=checked)
     off = R * n_splits * rec
     merged = partials[off: off + R * rec].view(R, rec)
     ops.decode_merge(local, merged)

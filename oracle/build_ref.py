@@ -7,7 +7,11 @@ for sm_100a, into oracle/_ref/kh_ref.so.  The reference's own build
 into the reference tree.  Does nothing when the reference tree is absent (the
 GPU machines run the prebuilt .so) or the output is newer than its sources.
 
-    python oracle/build_ref.py [REFERENCE_DIR]
+    python oracle/build_ref.py REFERENCE_DIR
+    KUDAHITAM_REFERENCE_DIR=... python oracle/build_ref.py
+
+The reference tree's location is an argument (or the environment variable
+KUDAHITAM_REFERENCE_DIR); without either, nothing is built.
 """
 from __future__ import annotations
 
@@ -19,11 +23,15 @@ import sysconfig
 
 HERE = pathlib.Path(__file__).resolve().parent
 OUT = HERE / "_ref" / "kh_ref.so"
-DEFAULT_REF = pathlib.Path("/root/reference")
+ENV_VAR = "KUDAHITAM_REFERENCE_DIR"
 
 
-def build(ref_dir: pathlib.Path = DEFAULT_REF) -> pathlib.Path | None:
-    src = ref_dir / "KudaHitamCUDA.cu"
+def build(ref_dir: pathlib.Path | str | None = None) -> pathlib.Path | None:
+    if ref_dir is None:
+        ref_dir = os.environ.get(ENV_VAR)
+    if not ref_dir:
+        return OUT if OUT.exists() else None
+    src = pathlib.Path(ref_dir) / "KudaHitamCUDA.cu"
     binding = HERE / "ref_binding.cpp"
     if not src.exists():
         return OUT if OUT.exists() else None
@@ -63,4 +71,4 @@ def build(ref_dir: pathlib.Path = DEFAULT_REF) -> pathlib.Path | None:
 
 
 if __name__ == "__main__":
-    print(build(pathlib.Path(sys.argv[1]) if len(sys.argv) > 1 else DEFAULT_REF))
+    print(build(sys.argv[1] if len(sys.argv) > 1 else None))

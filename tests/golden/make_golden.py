@@ -1,10 +1,12 @@
 """Generate the golden fixtures in this folder from the reference itself.
 
-    python tests/golden/make_golden.py [/path/to/reference]
+    python tests/golden/make_golden.py REFERENCE_DIR
+    KUDAHITAM_REFERENCE_DIR=... python tests/golden/make_golden.py
 
-Runs in a container that has the reference checked out (default
-/root/reference); the fixtures it writes are committed so that tests need no
-reference at run time.  What comes from where:
+Runs where the reference is checked out (its location is the argument, or
+the environment variable KUDAHITAM_REFERENCE_DIR); the fixtures it writes
+are committed so that tests need no reference at run time.  What comes from
+where:
 
 * codebook.npz -- ``KudahitamCompressorV2(D, bits, seed).d`` and
   ``.centroids`` (KudaHitamQuant_full.py:256-275), for several D / bits / seeds.
@@ -84,8 +86,15 @@ def synth_rows(rng, B, H, S, D, kind):
     return x
 
 
-def main(ref: str = "/root/reference") -> None:
+def main(ref: str | None = None) -> None:
+    import os
+
     import torch
+
+    ref = ref or os.environ.get("KUDAHITAM_REFERENCE_DIR")
+    if not ref:
+        raise SystemExit("usage: make_golden.py REFERENCE_DIR "
+                         "(or set KUDAHITAM_REFERENCE_DIR)")
 
     R = load_reference(ref)
 

@@ -87,3 +87,25 @@ def test_seq_sharded_combine_world2():
 def test_seq_sharded_combine_world2_with_empty_splits():
     # 4 rows over 2 ranks x 3 splits: some splits own no rows
     _run(2, S=4)
+
+
+def test_peer_exchange_epoch_parity_alternates_across_the_wrap():
+    from kudahitam.dist import next_epoch
+    e = 0
+    seq = []
+    for _ in range(3):
+        e = next_epoch(e)
+        seq.append(e)
+    assert seq == [1, 2, 3]
+    e = 0xFFFFFFFE
+    seq = []
+    for _ in range(4):
+        e = next_epoch(e)
+        seq.append(e)
+    assert seq == [0xFFFFFFFF, 2, 3, 4]
+    # consecutive epochs never share a buffer/flag set, and 0 never recurs
+    e = 0xFFFFFFF0
+    for _ in range(64):
+        n = next_epoch(e)
+        assert n != 0 and (n & 1) != (e & 1)
+        e = n

@@ -8,6 +8,7 @@ import pytest
 import torch
 
 from kudahitam import _lib, ops
+from kudahitam import dist as khdist
 
 pytestmark = pytest.mark.gpu
 
@@ -29,8 +30,11 @@ def test_peer_flag_wait_times_out_then_combines():
     torch.cuda.synchronize()
     assert _lib.device_error() & 4
     assert torch.all(out == 0)
-    _lib.call("kh_clear_device_error")
+    # the checked form reports the timeout as an exception and clears the word
+    with pytest.raises(khdist.PeerTimeoutError):
+        khdist.check_peer_timeout()
     assert _lib.device_error() == 0
+    khdist.check_peer_timeout()  # nothing pending: no exception
     # flags raised: the combine goes through and matches the strided combine
     flags.fill_(1)
     _lib.call("kh_decode_combine_from_peers", recs.data_ptr(), flags.data_ptr(), 1, R, world, D,
