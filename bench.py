@@ -82,7 +82,7 @@ def synth_kv(seed: int, device) -> tuple[torch.Tensor, torch.Tensor]:
 
 class ClockSampler:
     """SM clock and clock-event (throttle) reasons, sampled through NVML
-    (read-only queries) every 5 ms from a host thread.  Samples carry host
+    (read-only queries) every 0.5 ms from a host thread.  Samples carry host
     timestamps so that the ones taken inside the timed region can be told
     apart from those of the adjacent loaded loops (warm-up and per-launch
     timing of the same kernel)."""
@@ -90,7 +90,7 @@ class ClockSampler:
     REASONS = {"hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20,
                "hw_thermal_slowdown": 0x40, "sw_power_cap": 0x4}
 
-    def __init__(self, index: int, period_s: float = 0.005):
+    def __init__(self, index: int, period_s: float = 0.0005):
         self.index = index
         self.period = period_s
         self.samples: list[tuple[float, float, int]] = []  # (t, MHz, reasons mask)
@@ -229,6 +229,17 @@ class CpuSample:
                           f"(same distribution), {dt:.2f} s per pass"}
 
 
+def all_ranks(v: float, world: int) -> list[float]:
+    """A per-rank scalar from every rank (rank order), for the record."""
+    if world == 1:
+        return [float(v)]
+    import torch.distributed as dist
+    t = torch.tensor([float(v)], dtype=torch.float64, device=torch.cuda.current_device())
+    out = [torch.empty_like(t) for _ in range(world)]
+    dist.all_gather(out, t)
+    return [float(x.item()) for x in out]
+
+
 def cpu_baseline_run(target_s: float = 10.0, max_rows: int = 1 << 22) -> dict:
     """The oracle port on a bounded sample of the workload, all host threads."""
     smp = CpuSample(target_s, max_rows)
@@ -299,6 +310,27 @@ def reference_kernel_on_gpu(args):
            "bytes_per_row": D * 2 + 6 * D + 8, "gbs": moved / (ms / 1e3) / 1e9,
            "frac_of_measured_hbm": moved / (ms / 1e3) / 1e9 / peak,
            "note": "reference kernel v8 with its own launcher, same K and V fp16 rows"}
+
+    # like for like: this engine's compat operator with the same five
+    # reference-layout outputs (compress + materialize), same rows
+    from kudahitam import ops
+    dh, ch = d.cpu(), c.cpu()
+
+    def step_engine():
+        for r in rows:
+            ops.ultra_fused_full_fusion(r, dh, ch)
+
+    for _ in range(3):
+        step_engine()
+    torch.cuda.synchronize()
+    ems = statistics.median(time_loop(step_engine, max(5, min(args.steps, 20)), stream))
+    out["engine_compat_op_same_outputs"] = {
+        "rows_per_s": n / (ems / 1e3), "ms_per_step": ems, "bytes_per_row": D * 2 + 6 * D + 8,
+        "gbs": moved / (ems / 1e3) / 1e9, "frac_of_measured_hbm": moved / (ems / 1e3) / 1e9 / peak,
+        "speedup_vs_reference_kernel": ms / ems,
+        "note": "ops.ultra_fused_full_fusion: the reference's five outputs (idx u8, norms, "
+                "k_mse f32, r_norms, signs i8) from compress + materialize, outputs "
+                "allocated per call like the reference launcher"}
     del k, v, rows
     torch.cuda.empty_cache()
     return out
@@ -345,6 +377,11 @@ def run_engine(args, world, rank, local):
         if rank == 0:
             print(json.dumps({"fp32_1bit": fp32_1bit_bench(dev, args)}), flush=True)
         return
+    if args.only == "cfg5":
+        c5 = cfg5_bench(dev, args, world, rank)
+        if rank == 0:
+            print(json.dumps({"sharded_8gpu_workload": c5}), flush=True)
+        return
     if args.only == "layers":
         lay = layers_bench(dev, args)
         if rank == 0:
@@ -378,6 +415,7 @@ def run_engine(args, world, rank, local):
         torch.cuda.synchronize()
         ms_local = t0.elapsed_time(t1)
         ms = max_over_ranks(ms_local, world)
+        per_rank_ms = all_ranks(ms_local, world)
         rows_all = 2 * ROWS_PER_TENSOR * world * args.steps
         value = rows_all / (ms / 1e3)
     # average launch duration over the timed region (one launch per step,
@@ -391,6 +429,7 @@ def run_engine(args, world, rank, local):
                         if NCU_TRAFFIC_BYTES_PER_ROW else None),
             "algorithmic_bytes": rows_launch * ALG_BYTES_PER_ROW,
             "launch_ms_mean": launch_ms, "launches_timed": args.steps,
+            "launch_ms_mean_per_rank": [t / args.steps for t in per_rank_ms],
             "timing": "CUDA events around the timed region / launches in it",
             "kernel": ("compress_simt_kernel<__half,256,Sym2,RES>"
                        if os.environ.get("KUDAHITAM_COMPRESS_PATH") == "simt"
@@ -434,6 +473,8 @@ def run_engine(args, world, rank, local):
            if args.only == "all" and not args.no_layers and world == 1 else None)
     f32 = fp32_1bit_bench(dev, args) if args.only == "all" and world == 1 else None
     sco = score_bench(dev, args) if args.only == "all" and world == 1 else None
+    torch.cuda.empty_cache()
+    c5 = cfg5_bench(dev, args, world, rank) if args.only == "all" and not args.no_cfg5 else None
 
     line = {"metric": METRIC, "value": value, "unit": "rows/s", "n_gpus": world,
             "steps": args.steps, "warmup": args.warmup, "ms_per_step": ms / args.steps,
@@ -442,7 +483,7 @@ def run_engine(args, world, rank, local):
             "hbm_gbs": achieved, "hbm_frac_of_measured": achieved / peak,
             "hbm_frac_of_spec_8000": achieved / 8000.0,
             "roofline": roof, "e2e": e2e, "decode": dec, "layers_28": lay,
-            "fp32_1bit": f32, "score": sco,
+            "fp32_1bit": f32, "score": sco, "sharded_8gpu_workload": c5,
             "gpu_launches": args.steps, "clocks": clk.summary()}
     if rank == 0 and world == 1 and not args.no_cpu_baseline:
         line["cpu_baseline"] = cpu_baseline_run()
@@ -467,13 +508,11 @@ def score_bench(dev, args) -> dict:
     out = torch.empty(G, 1, S_, device=dev)
     stream = torch.cuda.current_stream(dev)
     dh, ch = ops._host_f32(d), ops._host_f32(c)
+    K = ops.ext()
 
     def step():
-        # the op's own launch, writing into a preallocated output
-        from kudahitam import _lib
-        _lib.call("kh_score", q.data_ptr(), G, 1, Dq, pk.code.data_ptr(), pk.res.data_ptr(),
-                  pk.norms.data_ptr(), pk.rnorms.data_ptr(), S_, dh.data_ptr(),
-                  ch.data_ptr(), 2, out.data_ptr(), stream.cuda_stream)
+        # the operator's own launch, writing into a preallocated output
+        K.score_out(q, pk.code, pk.res, pk.norms, pk.rnorms, S_, dh, ch, out)
 
     for _ in range(3):
         step()
@@ -515,11 +554,20 @@ def fp32_1bit_bench(dev, args) -> dict:
         for _ in range(3):
             step()
         torch.cuda.synchronize()
-        # host cost of one API call (the GPU is idle between short launches)
+        # host cost of one API call (the GPU is idle between short launches),
+        # through ops.compress_many and through the bare operator
         h0 = time.perf_counter()
         for _ in range(20):
             step()
         host_us = (time.perf_counter() - h0) / 20 * 1e6
+        torch.cuda.synchronize()
+        K = ops.ext()
+        dh, ch = ops._host_f32(d), ops._host_f32(c)
+        codes, norms = [o.code for o in outs], [o.norms for o in outs]
+        h0 = time.perf_counter()
+        for _ in range(20):
+            K.compress_many_out(xs, dh, ch, False, codes, [], norms, [])
+        op_host_us = (time.perf_counter() - h0) / 20 * 1e6
         torch.cuda.synchronize()
         per = time_loop(step, 20, stream)
         # the same launch replayed from a CUDA graph: kernel time without the
@@ -544,6 +592,7 @@ def fp32_1bit_bench(dev, args) -> dict:
                          "graph_us_per_step": gms * 1e3,
                          "graph_frac_of_measured_hbm": rows * bpr / (gms / 1e3) / 1e9 / peak,
                          "host_us_per_call": host_us,
+                         "op_host_us_per_call": op_host_us,
                          "l2": "fits in L2" if rows * 512 < 126e6 else "above L2"}
         del xs, outs
     return out
@@ -617,46 +666,179 @@ def decode_bench(dev, args, world: int = 1, rank: int = 0) -> dict:
             x = torch.randn(64, S_loc, DEC_D, device=dev, generator=g).to(torch.bfloat16)
             ops.compress(x, dd, c, out=p.rows(i * S_loc, (i + 64) * S_loc))
     q = torch.randn(G, DEC_D, generator=torch.Generator().manual_seed(4)).to(torch.bfloat16).to(dev)
-    n_splits = ops.default_splits(G, S_loc, dev)
+    dec = decode_timing(dev, args, world, q.float(), pk, pv, dk, dv, c, S_loc, DEC_S)
+    dec["roofline"]["traffic"] = NCU_DECODE_TRAFFIC_BYTES_PER_ROW * G * DEC_S / world
+    dec["roofline"]["kernel"] = "decode_v3_kernel<128> + decode_combine_kernel<128>"
+    return {"config": "q bf16 [32,16,128]; K and V 2-bit-mode packed, S=40000"
+                      + (f", sequence-sharded over {world} GPUs + one NCCL all-gather"
+                         if world > 1 else ""),
+            **dec, "us_per_token": dec["us_per_step"] / DEC_B}
+
+
+CFG5_B, CFG5_H, CFG5_S, CFG5_D = 64, 16, 131072, 128
+CFG5_BLOCK = 16384  # sequence rows per generated block (S / 8: every N in 1, 2, 4, 8 aligns)
+
+
+def cfg5_outlier_channels() -> torch.Tensor:
+    """3 outlier channels per head (scaled x10), the same for K and V and
+    for every batch entry: [16, 3] from a CPU generator seeded 4."""
+    g = torch.Generator().manual_seed(4)
+    return torch.stack([torch.randperm(CFG5_D, generator=g)[:3] for _ in range(CFG5_H)])
+
+
+def cfg5_block(dev, tensor: int, group: int, block: int, ch: torch.Tensor) -> torch.Tensor:
+    """Rows [block * 16384, (block + 1) * 16384) of (batch, head) group
+    `group` of K (tensor 0) or V (tensor 1) of the 8-GPU workload: bf16
+    N(0, 1) with the head's 3 outlier channels x10, from a CUDA generator
+    seeded by (tensor, group, block), so that every rank count generates the
+    same rows."""
+    seed = 4_000_000 + (tensor * CFG5_B * CFG5_H + group) * (CFG5_S // CFG5_BLOCK) + block
+    g = torch.Generator(device=dev).manual_seed(seed)
+    x = torch.randn(CFG5_BLOCK, CFG5_D, device=dev, generator=g)
+    x[:, ch[group % CFG5_H].to(dev)] *= 10.0
+    return x.to(torch.bfloat16)
+
+
+def cfg5_bench(dev, args, world: int, rank: int) -> dict:
+    """The 8-GPU workload: K and V bf16 [64, 16, 131072, 128] (N(0,1), 3
+    outlier channels x10 per head, seeded).
+    * compression sharded by batch x head (1024 groups / N per rank, no
+      communication), 2-bit mode, one batched launch over the rank's K and V
+      per step; weak in nothing: the total work is fixed (strong scaling);
+    * decode attention over the sequence-sharded compressed cache (S / N rows
+      of every group per rank, B = 64: 1024 query rows), records merged per
+      rank and exchanged with one NCCL all-gather; max over ranks."""
+    from kudahitam import dist as khdist
+    from kudahitam import ops
+    from kudahitam.codebook import lloyd_max, rademacher
+    G = CFG5_B * CFG5_H
+    nblk = CFG5_S // CFG5_BLOCK
+    ch = cfg5_outlier_channels()
+    d, c = rademacher(CFG5_D, 1), lloyd_max(1, CFG5_D)
+    peak, _ = peaks()
     stream = torch.cuda.current_stream(dev)
-    qf = q.float()
-    sm = 1 / math.sqrt(DEC_D)
-    if world == 1:
-        ws = torch.empty(ops.decode_workspace_bytes(G, n_splits, DEC_D) // 4, device=dev)
-        out = torch.empty(G, DEC_D, device=dev)
+    out = {"config": "K, V bf16 [64,16,131072,128], 3 outlier channels x10 per head; "
+                     "compression sharded by batch x head, decode sequence-sharded "
+                     "(strong scaling: total work fixed)"}
 
-        def step():
-            ops.decode_partial(qf, pk, pv, dk, dv, c, sm, n_splits, ws, n_splits, 0, S_loc)
-            ops.decode_combine(ws, n_splits, dv, out)
-    else:
-        buf = torch.empty(khdist.seq_sharded_workspace_numel(G, n_splits, world, DEC_D),
-                          device=dev)
+    # ---- compression: this rank's (batch, head) groups, whole sequences
+    g0, g1 = khdist.shard_range(G, world, rank)
+    xs = []
+    for t in range(2):
+        x = torch.empty(g1 - g0, CFG5_S, CFG5_D, device=dev, dtype=torch.bfloat16)
+        for gi in range(g0, g1):
+            for j in range(nblk):
+                x[gi - g0, j * CFG5_BLOCK:(j + 1) * CFG5_BLOCK] = cfg5_block(dev, t, gi, j, ch)
+        xs.append(x)
+    outs = [ops.empty_packed(x.shape, 1, True, dev) for x in xs]
 
-        def step():
-            khdist.decode_attention_seq_sharded(qf, pk, pv, dk, dv, c, sm, n_splits,
-                                                partials=buf)
+    def step():
+        ops.compress_many(xs, d, c, residual=True, outs=outs)
 
     for _ in range(3):
         step()
     torch.cuda.synchronize()
     barrier(world)
-    per = time_loop(step, max(5, min(args.steps, 20)), stream)
-    ms = max_over_ranks(statistics.median(per), world)
-    bytes_step = G * DEC_S * DEC_BYTES_PER_ROW  # whole job
+    n_steps = max(3, min(args.steps, 10))
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record(stream)
+    for _ in range(n_steps):
+        step()
+    e1.record(stream)
+    torch.cuda.synchronize()
+    ms_local = e0.elapsed_time(e1) / n_steps
+    ms = max_over_ranks(ms_local, world)
+    rows_rank = 2 * (g1 - g0) * CFG5_S
+    bpr = CFG5_D * 2 + 2 * CFG5_D // 8 + 8
+    out["compress"] = {
+        "rows_per_step": 2 * G * CFG5_S, "rows_per_rank": rows_rank, "ms_per_step": ms,
+        "rows_per_s": 2 * G * CFG5_S / (ms / 1e3),
+        "frac_of_measured_hbm_per_gpu": rows_rank * bpr / (ms / 1e3) / 1e9 / peak,
+        "per_rank_ms": all_ranks(ms_local, world), "steps": n_steps,
+        "bytes_per_row": bpr}
+    if world > 1:
+        del outs
+    # ---- decode: this rank's sequence shard of every group
+    b0, b1 = khdist.shard_range(nblk, world, rank)
+    S_loc = (b1 - b0) * CFG5_BLOCK
+    if world == 1:
+        pk, pv = outs
+    else:
+        del xs
+        torch.cuda.empty_cache()
+        pk = ops.empty_packed((G, S_loc, CFG5_D), 1, True, dev)
+        pv = ops.empty_packed((G, S_loc, CFG5_D), 1, True, dev)
+        for t, p in ((0, pk), (1, pv)):
+            for gi in range(G):
+                x = torch.cat([cfg5_block(dev, t, gi, j, ch) for j in range(b0, b1)])
+                ops.compress(x, d, c, out=p.rows(gi * S_loc, (gi + 1) * S_loc))
+    q = torch.randn(G, CFG5_D, generator=torch.Generator().manual_seed(44)).to(
+        torch.bfloat16).float().to(dev)
+    dec = decode_timing(dev, args, world, q, pk, pv, d, d, c, S_loc, CFG5_S)
+    out["decode"] = {"config": f"q [64,16,128] vs K, V 2-bit-mode packed, S=131072"
+                               f"{f', {S_loc} rows per group on each of {world} GPUs' if world > 1 else ''}",
+                     **dec, "us_per_token": dec["us_per_step"] / CFG5_B}
+    out["gpus_active"] = world
+    del pk, pv
+    if world == 1:
+        del xs, outs
+    torch.cuda.empty_cache()
+    return out
+
+
+def decode_timing(dev, args, world, q, pk, pv, dk, dv, c, S_loc, S_total) -> dict:
+    """Times decode attention (q [R, D] against R groups of S_loc cached rows
+    on this rank; S_total over all ranks): whole steps, and each phase on its
+    own (partial kernel, local merge, NCCL all-gather, combine), every time
+    the max over ranks of the median of CUDA-event timings."""
+    from kudahitam import dist as khdist
+    from kudahitam import ops
+    R, D = q.shape
+    n_splits = ops.default_splits(R, S_loc, dev)
+    stream = torch.cuda.current_stream(dev)
+    sm = 1 / math.sqrt(D)
+    rec = D + 2
+    buf = torch.empty(khdist.seq_sharded_workspace_numel(R, n_splits, world, D), device=dev)
+    outp = torch.empty(R, D, device=dev)
+    local = buf[: R * n_splits * rec].view(R, n_splits, rec)
+    off = R * n_splits * rec
+    merged = buf[off: off + R * rec].view(R, rec)
+    gathered = buf[off + R * rec: off + R * rec * (1 + world)].view(world, R, rec)
+
+    def step():
+        return khdist.decode_attention_seq_sharded(q, pk, pv, dk, dv, c, sm, n_splits,
+                                                   partials=buf)
+
+    phases = {
+        "partial": lambda: ops.decode_partial(q, pk, pv, dk, dv, c, sm, n_splits, local,
+                                              n_splits, 0, S_loc),
+    }
+    if world > 1:
+        phases["merge"] = lambda: ops.decode_merge(local, merged)
+        phases["all_gather"] = lambda: khdist.gather_records(merged, out=gathered)
+        phases["combine"] = lambda: ops.decode_combine_records(gathered.transpose(0, 1), dv, outp)
+    else:
+        phases["combine"] = lambda: ops.decode_combine(local, n_splits, dv, outp)
+    for _ in range(3):
+        step()
+    torch.cuda.synchronize()
+    barrier(world)
+    n = max(5, min(args.steps, 20))
+    ms = max_over_ranks(statistics.median(time_loop(step, n, stream)), world)
+    phase_us = {}
+    for name, fn in phases.items():
+        barrier(world)
+        phase_us[name] = max_over_ranks(statistics.median(time_loop(fn, n, stream)), world) * 1e3
+    bytes_step = R * S_total * 2 * (2 * D // 8 + 8)  # whole job: K and V, 2 planes + 2 norms
     peak, _ = peaks()
-    return {"config": "q bf16 [32,16,128]; K and V 2-bit-mode packed, S=40000"
-                      + (f", sequence-sharded over {world} GPUs + one NCCL all-gather"
-                         if world > 1 else ""),
-            "us_per_step": ms * 1e3, "us_per_token": ms * 1e3 / DEC_B,
-            "n_splits": n_splits, "scaling": "strong" if world > 1 else None,
+    per_gpu = bytes_step / world / (ms / 1e3) / 1e9
+    return {"us_per_step": ms * 1e3, "n_splits": n_splits, "rows_per_group_per_gpu": S_loc,
+            "scaling": "strong" if world > 1 else None,
+            "phase_us_max_over_ranks": phase_us,
             "gbs": bytes_step / (ms / 1e3) / 1e9,
-            "frac_of_measured_hbm_per_gpu": bytes_step / world / (ms / 1e3) / 1e9 / peak,
-            "roofline": {"bound": "hbm", "achieved": bytes_step / world / (ms / 1e3) / 1e9,
-                         "peak": peak, "unit": "GB/s",
-                         "frac": bytes_step / world / (ms / 1e3) / 1e9 / peak,
-                         "algorithmic_bytes": bytes_step / world,
-                         "traffic": NCU_DECODE_TRAFFIC_BYTES_PER_ROW * G * DEC_S / world,
-                         "kernel": "decode_v3_kernel<128> + decode_combine_kernel<128>"}}
+            "frac_of_measured_hbm_per_gpu": per_gpu / peak,
+            "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": peak, "unit": "GB/s",
+                         "frac": per_gpu / peak, "algorithmic_bytes": bytes_step / world}}
 
 
 def main():
@@ -668,7 +850,10 @@ def main():
     ap.add_argument("--no-cpu-baseline", action="store_true")
     ap.add_argument("--no-layers", action="store_true",
                     help="skip the 28-layer batched compression line (60 GB resident)")
-    ap.add_argument("--only", choices=["all", "compress", "decode", "layers", "fp32", "score"], default="all",
+    ap.add_argument("--no-cfg5", action="store_true",
+                    help="skip the 8-GPU workload line (K, V bf16 [64,16,131072,128])")
+    ap.add_argument("--only", choices=["all", "compress", "decode", "layers", "fp32", "score",
+                                       "cfg5"], default="all",
                     help="run one part (small cases for profiler captures)")
     ap.add_argument("--seq", type=int, default=None,
                     help="override S of the compression workload (profiling only)")

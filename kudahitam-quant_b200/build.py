@@ -1,11 +1,15 @@
 """Build the engine's C-ABI shared library for sm_100a.
 
     python kudahitam-quant_b200/build.py        # -> kudahitam/_lib/libkudahitam.so
+                                                #    kudahitam/_lib/libkh_torch.so
 
 Every ``csrc/*.cu`` file is compiled by nvcc (in parallel, skipped when its
 object is newer than the sources it depends on) and linked into one shared
 library with the CUDA runtime linked statically, so the library travels as a
 single file and binds to whatever CUDA context the caller (PyTorch) created.
+``csrc/kh_torch.cpp`` (the torch.ops.kudahitam operators over that C ABI) is
+compiled by g++ against PyTorch's headers into a second library that links
+the first one (found beside it through its rpath).
 """
 from __future__ import annotations
 
@@ -22,6 +26,7 @@ CSRC = PKG / "csrc"
 INCLUDE = REPO / "include"
 OBJ = PKG / "_build"
 OUT = PKG / "kudahitam" / "_lib" / "libkudahitam.so"
+TORCH_OUT = PKG / "kudahitam" / "_lib" / "libkh_torch.so"
 
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 NVCC_FLAGS = ARCH + ["-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC",
@@ -55,21 +60,46 @@ def _compile(nvcc: str, src: pathlib.Path, verbose: bool) -> pathlib.Path:
     return obj
 
 
-def build(verbose: bool = False) -> pathlib.Path:
+def build_torch_ext(cuda_home: str) -> pathlib.Path:
+    """g++ build of the torch.ops.kudahitam operators (csrc/kh_torch.cpp)."""
+    src = CSRC / "kh_torch.cpp"
+    newest = max(src.stat().st_mtime, OUT.stat().st_mtime,
+                 *[p.stat().st_mtime for p in INCLUDE.glob("*.h")])
+    if TORCH_OUT.exists() and TORCH_OUT.stat().st_mtime >= newest:
+        return TORCH_OUT
+    import torch
+    tdir = pathlib.Path(torch.__file__).resolve().parent
+    abi = int(torch._C._GLIBCXX_USE_CXX11_ABI)
+    cmd = ["g++", "-O2", "-std=c++17", "-fPIC", "-shared", "-Wall", "-Wno-unused-function",
+           f"-D_GLIBCXX_USE_CXX11_ABI={abi}",
+           f"-I{tdir / 'include'}", f"-I{tdir / 'include' / 'torch' / 'csrc' / 'api' / 'include'}",
+           f"-I{cuda_home}/include", f"-I{INCLUDE}", str(src),
+           "-o", str(TORCH_OUT.with_suffix(".so.tmp")),
+           f"-L{tdir / 'lib'}", f"-L{OUT.parent}", "-lkudahitam", "-lc10", "-lc10_cuda",
+           "-ltorch_cpu", "-ltorch", "-Wl,-rpath,$ORIGIN"]
+    r = subprocess.run(cmd, capture_output=True, text=True)
+    if r.returncode != 0:
+        raise RuntimeError(f"building kh_torch.cpp failed:\n{r.stdout}\n{r.stderr}")
+    os.replace(TORCH_OUT.with_suffix(".so.tmp"), TORCH_OUT)
+    return TORCH_OUT
+
+
+def build(verbose: bool = False, torch_ext: bool = True) -> pathlib.Path:
     nvcc = _nvcc()
     OBJ.mkdir(parents=True, exist_ok=True)
     OUT.parent.mkdir(parents=True, exist_ok=True)
     srcs = sorted(CSRC.glob("*.cu"))
     with cf.ThreadPoolExecutor(max_workers=min(len(srcs), os.cpu_count() or 4)) as ex:
         objs = list(ex.map(lambda s: _compile(nvcc, s, verbose), srcs))
-    if OUT.exists() and OUT.stat().st_mtime >= max(o.stat().st_mtime for o in objs):
-        return OUT
-    tmp = OUT.with_suffix(".so.tmp")
-    cmd = [nvcc, *ARCH, "-shared", "-o", str(tmp), *map(str, objs)]
-    r = subprocess.run(cmd, capture_output=True, text=True)
-    if r.returncode != 0:
-        raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
-    os.replace(tmp, OUT)
+    if not (OUT.exists() and OUT.stat().st_mtime >= max(o.stat().st_mtime for o in objs)):
+        tmp = OUT.with_suffix(".so.tmp")
+        cmd = [nvcc, *ARCH, "-shared", "-o", str(tmp), *map(str, objs)]
+        r = subprocess.run(cmd, capture_output=True, text=True)
+        if r.returncode != 0:
+            raise RuntimeError(f"link failed:\n{r.stdout}\n{r.stderr}")
+        os.replace(tmp, OUT)
+    if torch_ext:
+        build_torch_ext(str(pathlib.Path(nvcc).resolve().parent.parent))
     return OUT
 
 

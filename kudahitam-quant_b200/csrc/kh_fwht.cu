@@ -1,5 +1,6 @@
 // kh_fwht.cu -- standalone orthonormal FWHT (the query projection) and the
 // packed-cache materialiser (reference-layout idx / k_mse / signs).
+#include <algorithm>
 #include <cmath>
 
 #include "kh_common.cuh"
@@ -50,66 +51,79 @@ struct alignas(16) MatParams {
   float d[256];
 };
 
-// One warp per row; lane l holds elements l + 32 j, j < D/32 (coalesced
-// writes).  Butterfly stages on element bits 0..4 exchange across lanes,
-// stages on bits 5.. stay in registers.
+// One warp per row, rows strided over a persistent grid; lane l holds
+// elements l + 32 j, j < D/32 (coalesced writes).  Butterfly stages on
+// element bits 0..4 exchange across lanes, stages on bits 5.. stay in
+// registers.  The lane's d values and the centroids are read from the
+// kernel parameters once per thread, into registers: indexing the
+// parameter bank with a lane-dependent index serialises the warp's access,
+// which on every row made this kernel several times slower than its
+// stores.
 template <int D, int NC>
 __global__ void __launch_bounds__(256)
     materialize_kernel(const __grid_constant__ MatParams P) {
   constexpr int J = D / 32;
   constexpr int kWords = (NC == 2) ? D / 32 : D / 16;
   const int lane = threadIdx.x & 31;
-  const int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
-  if (row >= P.n_rows) return;  // whole warp exits together
-
-  const uint32_t* cw = P.code + row * kWords;
-  uint32_t idx[J];
-  float r[J];
+  float dv[J];
 #pragma unroll
-  for (int j = 0; j < J; ++j) {
-    const int e = lane + 32 * j;
-    if (NC == 2) idx[j] = (cw[e >> 5] >> (e & 31)) & 1u;
-    else idx[j] = (cw[e >> 4] >> (2 * (e & 15))) & 3u;
-    r[j] = P.cb.c[idx[j]];
-  }
-  if (P.idx) {
+  for (int j = 0; j < J; ++j) dv[j] = P.d[lane + 32 * j];
+  const float c0 = P.cb.c[0], c1 = P.cb.c[1];
+  const float c2 = NC == 4 ? P.cb.c[2] : 0.f, c3 = NC == 4 ? P.cb.c[3] : 0.f;
+  const float inv_sqrt_d = 1.0f / sqrtf((float)D);
+  const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
+  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+       row < P.n_rows; row += warps) {  // uniform per warp
+    const uint32_t* cw = P.code + row * kWords;
+    uint32_t idx[J];
+    float r[J];
 #pragma unroll
-    for (int j = 0; j < J; ++j) P.idx[row * D + lane + 32 * j] = (uint8_t)idx[j];
-  }
-  if (P.kmse) {
-#pragma unroll
-    for (int h = 1; h < 32; h <<= 1) {
-#pragma unroll
-      for (int j = 0; j < J; ++j) {
-        const float o = __shfl_xor_sync(0xffffffffu, r[j], h);
-        r[j] = (lane & h) ? (o - r[j]) : (r[j] + o);
+    for (int j = 0; j < J; ++j) {
+      const int e = lane + 32 * j;
+      if (NC == 2) {
+        idx[j] = (__ldg(cw + (e >> 5)) >> (e & 31)) & 1u;
+        r[j] = idx[j] ? c1 : c0;
+      } else {
+        idx[j] = (__ldg(cw + (e >> 4)) >> (2 * (e & 15))) & 3u;
+        r[j] = idx[j] < 2 ? (idx[j] ? c1 : c0) : (idx[j] == 2 ? c2 : c3);
       }
     }
+    if (P.idx) {
 #pragma unroll
-    for (int h = 1; h < J; h <<= 1) {
+      for (int j = 0; j < J; ++j) P.idx[row * D + lane + 32 * j] = (uint8_t)idx[j];
+    }
+    if (P.kmse) {
 #pragma unroll
-      for (int j = 0; j < J; ++j) {
-        if ((j & h) == 0) {
-          const float a = r[j], b = r[j + h];
-          r[j] = a + b;
-          r[j + h] = a - b;
+      for (int h = 1; h < 32; h <<= 1) {
+#pragma unroll
+        for (int j = 0; j < J; ++j) {
+          const float o = __shfl_xor_sync(0xffffffffu, r[j], h);
+          r[j] = (lane & h) ? (o - r[j]) : (r[j] + o);
         }
       }
-    }
-    // k_mse = r * m_base * d, m_base = (1/sqrt(D)) * norm (KudaHitamCUDA.cu:142-148)
-    const float m_base = (1.0f / sqrtf((float)D)) * P.norms[row];
 #pragma unroll
-    for (int j = 0; j < J; ++j) {
-      const int e = lane + 32 * j;
-      P.kmse[row * D + e] = r[j] * m_base * P.d[e];
-    }
-  }
-  if (P.signs) {
-    const uint32_t* rw = P.res + row * (D / 32);
+      for (int h = 1; h < J; h <<= 1) {
 #pragma unroll
-    for (int j = 0; j < J; ++j) {
-      const int e = lane + 32 * j;
-      P.signs[row * D + e] = ((rw[e >> 5] >> (e & 31)) & 1u) ? (int8_t)1 : (int8_t)-1;
+        for (int j = 0; j < J; ++j) {
+          if ((j & h) == 0) {
+            const float a = r[j], b = r[j + h];
+            r[j] = a + b;
+            r[j + h] = a - b;
+          }
+        }
+      }
+      // k_mse = r * m_base * d, m_base = (1/sqrt(D)) * norm (KudaHitamCUDA.cu:142-148)
+      const float m_base = inv_sqrt_d * __ldg(P.norms + row);
+#pragma unroll
+      for (int j = 0; j < J; ++j) P.kmse[row * D + lane + 32 * j] = r[j] * m_base * dv[j];
+    }
+    if (P.signs) {
+      const uint32_t* rw = P.res + row * (D / 32);
+#pragma unroll
+      for (int j = 0; j < J; ++j) {
+        const int e = lane + 32 * j;
+        P.signs[row * D + e] = ((__ldg(rw + (e >> 5)) >> (e & 31)) & 1u) ? (int8_t)1 : (int8_t)-1;
+      }
     }
   }
 }
@@ -140,8 +154,9 @@ kh_status launch_materialize(const uint32_t* code, const uint32_t* res,
   P.n_rows = n_rows;
   P.cb = cb;
   for (int i = 0; i < D; ++i) P.d[i] = d[i];
-  const int64_t blocks = (n_rows + 7) / 8;
-  if (blocks > 0x7fffffff) return KH_EINVAL;
+  // persistent grid: 8 blocks of 8 warps per SM, each warp striding over rows
+  const int64_t blocks = std::min<int64_t>((n_rows + 7) / 8, (int64_t)sm_count() * 8);
+  if (blocks <= 0) return KH_OK;
   const unsigned g = (unsigned)blocks;
   if (D == 128) {
     if (cb.n_c == 2) materialize_kernel<128, 2><<<g, 256, 0, stream>>>(P);

@@ -112,27 +112,20 @@ class PeerRecordExchange:
         this function has returned.  With ``checked=True`` the call
         synchronises the stream, reads that word and raises
         ``PeerTimeoutError`` (clearing the word) when bit 2 is set."""
-        import ctypes
-        from . import _lib
         R, P, gs, ps = ops._record_view(local, self.head_dim)
         if R != self.n_rows:
             raise ValueError(f"exchange built for {self.n_rows} rows, got {R}")
         self.epoch = next_epoch(self.epoch)
         par = self.epoch & 1
         w = self.world
-        recs = (ctypes.c_void_p * w)(*[p + par * self.rec_bytes for p in self.ptrs])
-        flags = (ctypes.c_void_p * w)(*[p + self.flag_off + par * w * 4 for p in self.ptrs])
-        dvh = ops._host_f32(dv)
+        K = ops.ext()
+        K.decode_merge_to_peers(local, R, P, gs, ps, self.head_dim,
+                                [p + par * self.rec_bytes for p in self.ptrs],
+                                [p + self.flag_off + par * w * 4 for p in self.ptrs],
+                                self.rank, self.epoch, self.counter)
+        K.decode_combine_from_peers(self.buf, par * self.rec_bytes, self.flag_off + par * w * 4,
+                                    self.epoch, R, w, ops._host_f32(dv), out)
         dev = local.device
-        with ops._on(dev):
-            st = ops._stream(dev)
-            _lib.call("kh_decode_merge_to_peers", ops._vp(local), R, P, gs, ps, self.head_dim,
-                      ctypes.cast(recs, ctypes.c_void_p), ctypes.cast(flags, ctypes.c_void_p),
-                      self.rank, w, self.epoch, ops._vp(self.counter), st)
-            mine = self.ptrs[self.rank]
-            _lib.call("kh_decode_combine_from_peers", mine + par * self.rec_bytes,
-                      mine + self.flag_off + par * w * 4, self.epoch, R, w, self.head_dim,
-                      ops._vp(dvh), ops._vp(out), st)
         if checked:
             check_peer_timeout(dev)
         return out

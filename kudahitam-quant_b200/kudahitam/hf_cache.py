@@ -12,12 +12,19 @@ compressed cache is not wired (:671, :676-677).  This module is that wiring:
 * ``attend(query)`` is one decode step straight from the packed cache
   (grouped-query heads share their KV head, nothing is expanded);
   ``scores(query)`` gives the reference's asymmetric scores.
-* ``update`` implements the transformers cache contract for models that run
-  their own attention: it returns dequantised K and V for every cached
-  token, K as k_mse + r_norm / D * d (.) H sign (the reference's score
-  estimator as a vector, so q . K_hat equals its scores) and V as
-  k_mse + r_norm sqrt(2/pi) / D * d (.) H sign (the decode step's V_hat).
-  That path trades the memory saving for compatibility; ``attend`` keeps it.
+* ``update`` implements the transformers cache contract.  On the first
+  call (prefill into an empty layer) it returns the incoming K and V
+  themselves: the prompt attends to itself exactly, and only the packed
+  copy is kept.  On a one-token decode step of a cache made with
+  ``packed_attention=True`` it returns a ``PackedAttention`` handle, and the
+  attention function registered as ``attn_implementation="kudahitam"``
+  (``register_attention``) attends from the packed bytes with the decode
+  kernel: generation never dequantises the cache.  Otherwise (chunked
+  prefill, or a model running its own attention) it returns dequantised K
+  and V for every cached token, K as k_mse + r_norm / D * d (.) H sign (the
+  reference's score estimator as a vector, so q . K_hat equals its scores)
+  and V as k_mse + r_norm sqrt(2/pi) / D * d (.) H sign (the decode step's
+  V_hat); that path trades the memory saving for compatibility.
 
 The layer class derives from transformers' ``CacheLayerMixin`` when
 transformers is installed (the cache container requires it); the packed
@@ -111,6 +118,60 @@ class PackedSeq:
                             take(p.res), take(p.rnorms).view(-1))
 
 
+class PackedAttention:
+    """Returned by ``KudahitamLayer.update`` as both K and V on a one-token
+    decode step of a cache with ``packed_attention=True``: the layer whose
+    packed cache the attention function reads.  ``shape`` is that of the
+    dequantised K it stands for ([B, H_kv, length, D])."""
+
+    def __init__(self, layer: "KudahitamLayer"):
+        self.layer = layer
+
+    @property
+    def shape(self):
+        s = self.layer.k
+        return (s.B, s.H, s.length, s.D)
+
+    def dequantized(self) -> tuple[torch.Tensor, torch.Tensor]:
+        return self.layer.dequantized()
+
+
+def kudahitam_attention(module, query: torch.Tensor, key, value, attention_mask,
+                        scaling: Optional[float] = None, dropout: float = 0.0, **kwargs):
+    """transformers attention function (``attn_implementation="kudahitam"``).
+
+    A ``PackedAttention`` key (a one-token decode step) runs the decode
+    kernel over the layer's packed K and V: query [B, H_q, 1, D] ->
+    [B, 1, H_q, D], no dequantisation, grouped-query heads read their KV
+    head without expansion.  The packed path attends to every cached token,
+    so a mask that hides some of them (left padding in a batch) falls back
+    to dequantised K and V.  Tensor K and V (prefill) go to PyTorch's
+    scaled-dot-product attention."""
+    from transformers.integrations.sdpa_attention import sdpa_attention_forward
+    if isinstance(key, PackedAttention):
+        hides = attention_mask is not None and (
+            (attention_mask.dtype == torch.bool and not bool(attention_mask.all())) or
+            (attention_mask.dtype != torch.bool and bool((attention_mask < 0).any())))
+        if query.shape[2] == 1 and not hides:
+            out = key.layer.attend(query[:, :, 0], sm_scale=scaling)  # float32 [B, H_q, D]
+            return out.to(query.dtype).unsqueeze(1), None
+        key, value = key.dequantized()
+    return sdpa_attention_forward(module, query, key, value, attention_mask, scaling=scaling,
+                                  dropout=dropout, **kwargs)
+
+
+def register_attention(name: str = "kudahitam") -> str:
+    """Register ``kudahitam_attention`` (and PyTorch SDPA's mask builder) with
+    transformers under ``name``; load a model with
+    ``attn_implementation=name`` and give it ``KudahitamCache(...,
+    packed_attention=True)``."""
+    from transformers import AttentionInterface
+    from transformers.masking_utils import AttentionMaskInterface, sdpa_mask
+    AttentionInterface.register(name, kudahitam_attention)
+    AttentionMaskInterface.register(name, sdpa_mask)
+    return name
+
+
 class KudahitamLayer(_LayerBase):
     """One layer's compressed K and V (transformers ``CacheLayerMixin``
     contract: update / get_seq_length / get_mask_sizes / ...)."""
@@ -119,9 +180,10 @@ class KudahitamLayer(_LayerBase):
     is_compileable = False
 
     def __init__(self, head_dim: int, seed_k: int = 0, seed_v: int = 1,
-                 initial_capacity: int = 256):
+                 initial_capacity: int = 256, packed_attention: bool = False):
         super().__init__()
         self.head_dim = head_dim
+        self.packed_attention = packed_attention
         self.d_k, self.d_v = rademacher(head_dim, seed_k), rademacher(head_dim, seed_v)
         self.c = lloyd_max(1, head_dim)
         self.initial_capacity = initial_capacity
@@ -152,8 +214,18 @@ class KudahitamLayer(_LayerBase):
         self.v.append(value_states, self.d_v, self.c)
 
     def update(self, key_states: torch.Tensor, value_states: torch.Tensor, *args, **kwargs):
-        """Append, then return dequantised K and V of every cached token."""
+        """Append (compress) the new tokens, then return what the model's
+        attention reads: the new K and V themselves when the layer was empty
+        (prefill attends to itself), a ``PackedAttention`` handle on a
+        one-token step with ``packed_attention``, else dequantised K and V
+        of every cached token."""
+        first = self.get_seq_length() == 0
         self.append(key_states, value_states)
+        if first:
+            return key_states, value_states
+        if self.packed_attention and key_states.shape[-2] == 1:
+            h = PackedAttention(self)
+            return h, h
         return self.dequantized()
 
     def dequantized(self) -> tuple[torch.Tensor, torch.Tensor]:
@@ -219,12 +291,13 @@ class KudahitamLayer(_LayerBase):
 
 
 def KudahitamCache(num_layers: Optional[int] = None, head_dim: int = 128, seed: int = 0,
-                   initial_capacity: int = 256):
+                   initial_capacity: int = 256, packed_attention: bool = False):
     """A transformers ``Cache`` whose layers are ``KudahitamLayer``s (layer
     l uses seeds 2 seed + 2 l and 2 seed + 2 l + 1 for its K and V
-    diagonals).  Pass it as ``past_key_values``; call
-    ``cache.layers[l].attend(q)`` from a custom attention for the packed
-    decode path."""
+    diagonals).  Pass it as ``past_key_values``.  With
+    ``packed_attention=True`` (and a model loaded with the attention
+    registered by ``register_attention``) decode steps attend from the
+    packed bytes; ``cache.layers[l].attend(q)`` does the same directly."""
     from transformers.cache_utils import Cache
 
     class _KudahitamCache(Cache):
@@ -240,7 +313,7 @@ def KudahitamCache(num_layers: Optional[int] = None, head_dim: int = 128, seed: 
             l = self._made
             self._made += 1
             return KudahitamLayer(head_dim, 2 * seed + 2 * l, 2 * seed + 2 * l + 1,
-                                  initial_capacity)
+                                  initial_capacity, packed_attention)
 
         def attend(self, layer_idx: int, query: torch.Tensor, **kw) -> torch.Tensor:
             return self.layers[layer_idx].attend(query, **kw)

@@ -1,13 +1,15 @@
-"""Torch-facing operators over the C ABI.
+"""Torch-facing operators: Python wrappers of ``torch.ops.kudahitam.*``.
 
-Each op takes CUDA tensors, allocates its outputs with PyTorch's caching
-allocator, and launches on the tensor's device and its current stream.  There
-is no CPU path: CPU inputs raise ``ValueError`` and a missing engine raises
-``NativeLibraryError``.
+The operators are registered by the engine's torch extension
+(``_lib/libkh_torch.so``, built from ``csrc/kh_torch.cpp``), a thin layer over
+the C ABI: each takes CUDA tensors, allocates its outputs with PyTorch's
+caching allocator and launches on the tensors' device and its current
+stream.  There is no CPU path: CPU inputs raise ``ValueError`` and a missing
+engine raises ``NativeLibraryError``.  (``_lib`` binds the same C ABI with
+ctypes for the pure-C tests.)
 """
 from __future__ import annotations
 
-import ctypes
 import math
 from dataclasses import dataclass
 from typing import Optional, Sequence
@@ -20,12 +22,25 @@ _DTYPE_CODE = {torch.float32: _lib.KH_F32, torch.float16: _lib.KH_F16,
                torch.bfloat16: _lib.KH_BF16}
 
 HEAD_DIMS = (128, 256)
-_MAX_SEGMENTS = 64  # kh_max_segments(); checked against the library by the tests
 
 
-def _vp(t: Optional[torch.Tensor]) -> Optional[int]:
-    """Device or host address of a tensor for a void* argument (None = NULL)."""
-    return None if t is None else t.data_ptr()
+_EXT = None
+
+
+def ext():
+    """``torch.ops.kudahitam`` (loads the engine's torch extension once)."""
+    global _EXT
+    if _EXT is None:
+        path = _lib.library_path().parent / "libkh_torch.so"
+        if not path.exists():
+            raise _lib.NativeLibraryError(
+                f"{path} not found: build it with `python kudahitam-quant_b200/build.py`")
+        try:
+            torch.ops.load_library(str(path))
+        except OSError as e:  # pragma: no cover
+            raise _lib.NativeLibraryError(f"cannot load {path}: {e}") from e
+        _EXT = torch.ops.kudahitam
+    return _EXT
 
 
 def _host_f32(t) -> torch.Tensor:
@@ -70,24 +85,6 @@ def _require_cuda(*ts: Optional[torch.Tensor]) -> torch.device:
         elif t.device != dev:
             raise ValueError(f"tensors on different devices: {dev} vs {t.device}")
     return dev
-
-
-def _rows(x: torch.Tensor) -> tuple[torch.Tensor, int]:
-    """[N, D] view with unit inner stride and a 16-byte row pitch (copies
-    only when the layout does not allow it)."""
-    D = x.shape[-1]
-    if x.is_contiguous() and x.data_ptr() % 16 == 0 and (D * x.element_size()) % 16 == 0:
-        return x.view(-1, D), D  # the common case: used in place
-    x2 = x.reshape(-1, D)
-    elt = x2.element_size()
-    ok = (x2.stride(-1) == 1 and x2.data_ptr() % 16 == 0
-          and (x2.shape[0] <= 1 or (x2.stride(0) * elt) % 16 == 0))
-    if not ok:
-        # a fresh allocation is 256-byte aligned (contiguous() would return a
-        # misaligned tensor unchanged)
-        x2 = torch.empty(x2.shape, dtype=x2.dtype, device=x2.device).copy_(x2)
-    stride = x2.stride(0) if x2.shape[0] > 1 else D
-    return x2, stride
 
 
 @dataclass
@@ -176,14 +173,14 @@ def compress(x: torch.Tensor, d, centroids, residual: bool = True,
     if D not in HEAD_DIMS:
         raise ValueError(f"head_dim must be 128 or 256, got {D}")
     dh, ch = _host_f32(d), _host_f32(centroids)
-    n_c, bits = _check_codebook(ch)
-    x2, stride = _rows(x)
+    _, bits = _check_codebook(ch)
     if out is None:
-        out = empty_packed(x.shape, bits, residual, dev)
-    with _on(dev):
-        _lib.call("kh_compress", _vp(x2), _DTYPE_CODE[x.dtype], x2.shape[0], D, stride,
-                  _vp(dh), _vp(ch), n_c, int(residual), _vp(out.code), _vp(out.res),
-                  _vp(out.norms), _vp(out.rnorms), _stream(dev))
+        r = ext().compress(x, dh, ch, residual)
+        shape = tuple(int(s) for s in x.shape)
+        if residual:
+            return PackedKV(shape, bits, r[0], r[1], r[2], r[3])
+        return PackedKV(shape, bits, r[0], r[1])
+    ext().compress_out(x, dh, ch, residual, out.code, out.res, out.norms, out.rnorms)
     return out
 
 
@@ -308,38 +305,20 @@ def compress_many(xs: Sequence[torch.Tensor], d, centroids, residual: bool = Tru
     kh_max_segments() tensors."""
     if not xs:
         return []
-    dev = _require_cuda(*xs)
-    dt = xs[0].dtype
-    D = xs[0].shape[-1]
-    if any(t.dtype != dt or t.shape[-1] != D for t in xs):
-        raise ValueError("compress_many needs one dtype and one head_dim")
-    if dt not in _DTYPE_CODE or D not in HEAD_DIMS:
-        raise ValueError("unsupported dtype / head_dim")
+    if not xs[0].is_cuda:
+        raise ValueError("kudahitam ops run on CUDA tensors only (no CPU path)")
+    # devices, dtypes, head dims and buffer sizes are checked by the operator
     dh, ch = _host_f32(d), _host_f32(centroids)
-    n_c, bits = _check_codebook(ch)
-    outs = list(outs) if outs is not None else [empty_packed(t.shape, bits, residual, dev)
-                                                for t in xs]
-    rows = [_rows(t) for t in xs]
-    maxseg = _MAX_SEGMENTS
-    with _on(dev):
-        stream = _stream(dev)
-        for i0 in range(0, len(xs), maxseg):
-            sl = range(i0, min(len(xs), i0 + maxseg))
-            n = len(sl)
-            P = ctypes.c_uint64 * n
-            args = [
-                P(*[rows[i][0].data_ptr() for i in sl]),
-                P(*[rows[i][0].shape[0] for i in sl]),
-                P(*[rows[i][1] for i in sl]),
-                P(*[outs[i].code.data_ptr() for i in sl]),
-                P(*[(outs[i].res.data_ptr() if residual else 0) for i in sl]),
-                P(*[outs[i].norms.data_ptr() for i in sl]),
-                P(*[(outs[i].rnorms.data_ptr() if residual else 0) for i in sl]),
-            ]
-            # the arrays are int64 / pointer tables: pass their addresses
-            _lib.call("kh_compress_batched", n, *[ctypes.addressof(a) for a in args],
-                      _DTYPE_CODE[dt], D, dh.data_ptr(), ch.data_ptr(), n_c, int(residual),
-                      stream)
+    if outs is None:
+        _, bits = _check_codebook(ch)
+        outs = [empty_packed(t.shape, bits, residual, xs[0].device) for t in xs]
+    # one launch per kh_max_segments() tensors, inside the operator
+    if residual:
+        ext().compress_many_out(xs, dh, ch, True, [o.code for o in outs], [o.res for o in outs],
+                                [o.norms for o in outs], [o.rnorms for o in outs])
+    else:
+        ext().compress_many_out(xs, dh, ch, False, [o.code for o in outs], [],
+                                [o.norms for o in outs], [])
     return outs
 
 
@@ -349,10 +328,7 @@ def fwht_(x: torch.Tensor) -> torch.Tensor:
     dev = _require_cuda(x)
     if x.dtype != torch.float32 or not x.is_contiguous():
         raise ValueError("fwht_ needs a contiguous float32 tensor")
-    D = x.shape[-1]
-    with _on(dev):
-        _lib.call("kh_fwht_inplace", _vp(x), x.numel() // D if D else 0, D, _stream(dev))
-    return x
+    return ext().fwht_(x)
 
 
 def fwht(x: torch.Tensor) -> torch.Tensor:
@@ -364,17 +340,12 @@ def materialize(p: PackedKV, d, centroids, idx: bool = True, kmse: bool = True,
                 signs: bool = True) -> dict:
     """Reference-layout tensors from a packed cache: idx uint8 [N, D],
     k_mse float32 [N, D], signs int8 [N, D]."""
-    dev = p.device
-    D, n = p.head_dim, p.n_rows
+    _require_cuda(p.code)
     dh, ch = _host_f32(d), _host_f32(centroids)
-    n_c = ch.numel()
-    o_idx = torch.empty((n, D), dtype=torch.uint8, device=dev) if idx else None
-    o_k = torch.empty((n, D), dtype=torch.float32, device=dev) if kmse else None
-    o_s = torch.empty((n, D), dtype=torch.int8, device=dev) if (signs and p.res is not None) else None
-    with _on(dev):
-        _lib.call("kh_materialize", _vp(p.code), _vp(p.res), _vp(p.norms), n, D, _vp(dh),
-                  _vp(ch), n_c, _vp(o_idx), _vp(o_k), _vp(o_s), _stream(dev))
-    return {"idx": o_idx, "kmse": o_k, "signs": o_s}
+    o_idx, o_k, o_s = ext().materialize(p.code, p.res, p.norms, p.head_dim, dh, ch, idx, kmse,
+                                        signs)
+    return {"idx": o_idx if idx else None, "kmse": o_k if kmse else None,
+            "signs": o_s if (signs and p.res is not None) else None}
 
 
 def score(q: torch.Tensor, p: PackedKV, d, centroids, seq_len: Optional[int] = None
@@ -382,20 +353,15 @@ def score(q: torch.Tensor, p: PackedKV, d, centroids, seq_len: Optional[int] = N
     """Asymmetric scores of q [G, nq, D] against G groups of seq_len cached
     rows each (rows of group g are rows [g*seq_len, (g+1)*seq_len) of p).
     Returns float32 [G, nq, seq_len]."""
-    dev = _require_cuda(q, p.norms)
+    _require_cuda(q, p.norms)
     G, nq, D = q.shape
     if D != p.head_dim:
         raise ValueError("query head_dim does not match the cache")
     S = p.n_rows // max(G, 1) if seq_len is None else int(seq_len)
     if G * S != p.n_rows:
         raise ValueError(f"{p.n_rows} cached rows do not split into {G} groups of {S}")
-    qf = q.to(torch.float32).contiguous()
     dh, ch = _host_f32(d), _host_f32(centroids)
-    out = torch.empty((G, nq, S), dtype=torch.float32, device=dev)
-    with _on(dev):
-        _lib.call("kh_score", _vp(qf), G, nq, D, _vp(p.code), _vp(p.res), _vp(p.norms),
-                  _vp(p.rnorms), S, _vp(dh), _vp(ch), ch.numel(), _vp(out), _stream(dev))
-    return out
+    return ext().score(q, p.code, p.res, p.norms, p.rnorms, S, dh, ch)
 
 
 def decode_workspace_bytes(n_groups: int, n_splits: int, head_dim: int) -> int:
@@ -435,7 +401,7 @@ def decode_partial(q: torch.Tensor, k: PackedKV, v: PackedKV, dk, dv, centroids,
     per cache group) or [G, n_q, D] (grouped-query attention: n_q query heads
     share each cache group; records cover G * n_q query rows).  Rows of cache
     group g are rows [g * seq_len + seq_begin, g * seq_len + seq_end)."""
-    dev = _require_cuda(q, k.norms, v.norms, partials)
+    _require_cuda(q, k.norms, v.norms, partials)
     if q.dim() == 2:
         G, D = q.shape
         n_q = 1
@@ -444,27 +410,22 @@ def decode_partial(q: torch.Tensor, k: PackedKV, v: PackedKV, dk, dv, centroids,
     seq_end = seq_len if seq_end is None else seq_end
     if not (k.residual and v.residual):
         raise ValueError("decode attention needs caches compressed with the residual plane")
-    qf = q.to(torch.float32).contiguous()
-    dkh, dvh, ch = _host_f32(dk), _host_f32(dv), _host_f32(centroids)
-    with _on(dev):
-        _lib.call("kh_decode_partial_gqa", _vp(qf), G, n_q, D, _vp(k.code), _vp(k.res),
-                  _vp(k.norms), _vp(k.rnorms), _vp(v.code), _vp(v.res), _vp(v.norms),
-                  _vp(v.rnorms), seq_len, seq_begin, seq_end, _vp(dkh), _vp(dvh), _vp(ch),
-                  ch.numel(), float(sm_scale), n_splits, _vp(partials), part_stride,
-                  part_offset, _stream(dev))
+    qf = q if (q.dtype == torch.float32 and q.is_contiguous()) else \
+        q.to(torch.float32).contiguous()
+    dkh, ch = _host_f32(dk), _host_f32(centroids)
+    ext().decode_partial(qf, k.code, k.res, k.norms, k.rnorms, v.code, v.res, v.norms,
+                         v.rnorms, seq_len, seq_begin, seq_end, dkh, ch, float(sm_scale),
+                         n_splits, partials, part_stride, part_offset)
     return partials
 
 
 def decode_combine(partials: torch.Tensor, n_parts: int, dv, out: torch.Tensor) -> torch.Tensor:
     """Merge split-K records into out ([R, D] or [G, n_q, D]: one row per
     query row of the records)."""
-    dev = _require_cuda(partials, out)
+    _require_cuda(partials, out)
     D = out.shape[-1]
     R = out.numel() // D if D else 0
-    dvh = _host_f32(dv)
-    with _on(dev):
-        _lib.call("kh_decode_combine", _vp(partials), R, n_parts, D, _vp(dvh), _vp(out),
-                  _stream(dev))
+    ext().decode_combine(partials, R, n_parts, n_parts * (D + 2), D + 2, _host_f32(dv), out)
     return out
 
 
@@ -482,28 +443,25 @@ def _record_view(records: torch.Tensor, D: int):
 def decode_combine_records(records: torch.Tensor, dv, out: torch.Tensor) -> torch.Tensor:
     """decode_combine over a strided [R, P, D+2] record view (for example the
     transpose of records gathered as [world, R, D+2])."""
-    dev = _require_cuda(records, out)
+    _require_cuda(records, out)
     D = out.shape[-1]
     R, P, gs, ps = _record_view(records, D)
     if out.numel() != R * D:
         raise ValueError(f"out holds {out.numel()} values, records describe {R} x {D}")
-    dvh = _host_f32(dv)
-    with _on(dev):
-        _lib.call("kh_decode_combine_strided", _vp(records), R, P, gs, ps, D, _vp(dvh),
-                  _vp(out), _stream(dev))
+    ext().decode_combine(records, R, P, gs, ps, _host_f32(dv), out)
     return out
 
 
 def decode_merge(records: torch.Tensor, merged: torch.Tensor) -> torch.Tensor:
     """Merge the P records of each row of a [R, P, D+2] view into one record
     per row: merged [R, D+2], still in the rotated domain."""
-    dev = _require_cuda(records, merged)
+    _require_cuda(records, merged)
     D = merged.shape[-1] - 2
     R, P, gs, ps = _record_view(records, D)
     if merged.numel() != R * (D + 2) or not merged.is_contiguous():
         raise ValueError(f"merged must be a contiguous float32 [{R}, {D + 2}]")
-    with _on(dev):
-        _lib.call("kh_decode_merge", _vp(records), R, P, gs, ps, D, _vp(merged), _stream(dev))
+    if R:
+        ext().decode_merge(records, R, P, gs, ps, merged)
     return merged
 
 
@@ -530,9 +488,15 @@ def decode_attention(q: torch.Tensor, k: PackedKV, v: PackedKV, dk, dv, centroid
         sm_scale = 1.0 / math.sqrt(D)
     if n_splits is None:
         n_splits = default_splits(G * n_q, L, dev)
+    if not (k.residual and v.residual):
+        raise ValueError("decode attention needs caches compressed with the residual plane")
+    if workspace is None:
+        return ext().decode_attention(q, k.code, k.res, k.norms, k.rnorms, v.code, v.res,
+                                      v.norms, v.rnorms, S, L, _host_f32(dk), _host_f32(dv),
+                                      _host_f32(centroids), float(sm_scale), n_splits)
     need = decode_workspace_bytes(G * n_q, n_splits, D)
-    if workspace is None or workspace.numel() * workspace.element_size() < need:
-        workspace = torch.empty(max(need // 4, 1), dtype=torch.float32, device=dev)
+    if workspace.numel() * workspace.element_size() < need:
+        raise ValueError(f"workspace holds fewer than the {need} bytes needed")
     out = torch.empty(q.shape, dtype=torch.float32, device=dev)
     decode_partial(q, k, v, dk, dv, centroids, sm_scale, n_splits, workspace, n_splits, 0, S,
                    0, L)
@@ -544,9 +508,12 @@ def ultra_fused_full_fusion(x: torch.Tensor, d, centroids):
     (KudaHitamCUDA.cu:197-231): (idx uint8 [N, D], norms [N, 1],
     k_mse float32 [N, D], r_norms [N, 1], signs int8 [N, D]).  Accepts
     fp16 (like the reference) and also fp32 / bf16."""
-    p = compress(x, d, centroids, residual=True)
-    m = materialize(p, d, centroids)
-    return m["idx"], p.norms.view(-1, 1), m["kmse"], p.rnorms.view(-1, 1), m["signs"]
+    _require_cuda(x)
+    if x.dtype not in _DTYPE_CODE:
+        raise TypeError(f"unsupported dtype {x.dtype}")
+    if x.shape[-1] not in HEAD_DIMS:
+        raise ValueError(f"head_dim must be 128 or 256, got {x.shape[-1]}")
+    return tuple(ext().ultra_fused_full_fusion(x, _host_f32(d), _host_f32(centroids)))
 
 
 def fused_asymmetric_attention(q: torch.Tensor, k_packed: torch.Tensor, signs: torch.Tensor,
@@ -560,7 +527,7 @@ def fused_asymmetric_attention(q: torch.Tensor, k_packed: torch.Tensor, signs: t
     Returns float32 [H, S]:  sum_i q~_i c[i][v_i] k_norm + k_norm * scale *
     (q . signs) * r_norm  with q~ = H(q (.) d)/sqrt(D).  Inputs of another
     dtype are converted; non-contiguous inputs are copied."""
-    dev = _require_cuda(q, k_packed, signs, d_vec, k_norms, r_norms, centroids)
+    _require_cuda(q, k_packed, signs, d_vec, k_norms, r_norms, centroids)
     H, D = q.shape
     S = k_norms.shape[1]
     nib = 0 <= layer_id < 8 and ((int(active_mask) & 0xFF) >> layer_id) & 1
@@ -570,17 +537,7 @@ def fused_asymmetric_attention(q: torch.Tensor, k_packed: torch.Tensor, signs: t
     if signs.shape != (H, S, D) or r_norms.shape != (H, S) or centroids.shape != (D, 16):
         raise ValueError("signs [H, S, D], r_norms [H, S] and centroids [D, 16] expected")
 
-    def prep(t, dt):
-        t = t.to(dt)
-        return t.contiguous() if t.data_ptr() % 16 == 0 else torch.empty_like(t).copy_(t)
-
-    qh, sg = prep(q, torch.float16), prep(signs, torch.float16)
-    kp = prep(k_packed, torch.uint8)
-    dv, kn, rn, cb = (prep(t, torch.float32) for t in (d_vec, k_norms, r_norms, centroids))
-    out = torch.empty((H, S), dtype=torch.float32, device=dev)
-    with _on(dev):
-        _lib.call("kh_score_packed_compat", _vp(qh), H, D, S, _vp(kp), _vp(sg), _vp(dv),
-                  _vp(kn), _vp(rn), _vp(cb), int(layer_id), int(active_mask) & 0xFF,
-                  float(scale), _vp(out), _stream(dev))
-    return out
+    return ext().fused_asymmetric_attention(q, k_packed, signs, d_vec, k_norms, r_norms,
+                                            centroids, int(layer_id), int(active_mask),
+                                            float(scale))
 

@@ -155,3 +155,24 @@ def test_gqa_decode_and_compat_scorer_validate():
     assert compat(kp=ctypes.c_void_p(0x10002)) == _lib.KH_EALIGN
     assert compat(q=ctypes.c_void_p(0x10001)) == _lib.KH_EALIGN
     assert compat(c=None) == _lib.KH_EINVAL
+
+
+TORCH_OPS = ["compress", "compress_out", "compress_many_out", "fwht_", "materialize", "score",
+             "score_out", "decode_partial", "decode_combine", "decode_merge", "decode_attention",
+             "decode_merge_to_peers", "decode_combine_from_peers", "ultra_fused_full_fusion",
+             "fused_asymmetric_attention"]
+
+
+def test_torch_extension_registers_every_operator():
+    """torch.ops.kudahitam.* (the thin torch extension over this ABI) loads,
+    registers every operator, and has no CPU kernel: CPU tensors fail in the
+    dispatcher."""
+    import torch
+
+    from kudahitam import ops
+    K = ops.ext()
+    for name in TORCH_OPS:
+        assert hasattr(K, name), name
+    assert "Tensor(a!) code" in str(K.compress_out.default._schema)
+    with pytest.raises(NotImplementedError):
+        K.compress(torch.randn(4, 128), torch.ones(128), torch.tensor([-0.1, 0.1]), True)

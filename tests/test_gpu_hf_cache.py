@@ -113,3 +113,50 @@ def test_generate_with_a_tiny_model():
         gen = model.generate(ids[:, :50], past_key_values=KudahitamCache(head_dim=128),
                              max_new_tokens=5, do_sample=False)
         assert gen.shape == (1, 55)
+
+
+def test_generate_attends_from_the_packed_cache(monkeypatch):
+    """With attn_implementation="kudahitam" and packed_attention=True, every
+    decode step of generate() attends from the packed bytes through the
+    decode kernel: the cache is never dequantised (counted), prefill
+    attends to the prompt exactly, and the logits stay close to an
+    uncompressed run of the same model."""
+    transformers = pytest.importorskip("transformers")
+    from kudahitam import hf_cache
+    name = hf_cache.register_attention()
+    cfg = transformers.LlamaConfig(hidden_size=256, intermediate_size=512, num_hidden_layers=2,
+                                   num_attention_heads=4, num_key_value_heads=2, head_dim=128,
+                                   vocab_size=512, max_position_embeddings=4096)
+    torch.manual_seed(0)
+    model = transformers.LlamaForCausalLM(cfg).cuda().to(torch.bfloat16).eval()
+    ref_model = transformers.LlamaForCausalLM(cfg).cuda().to(torch.bfloat16).eval()
+    ref_model.load_state_dict(model.state_dict())
+    model.set_attn_implementation(name)
+    calls = {"dequantize": 0, "attend": 0}
+    real_deq, real_attend = hf_cache.PackedSeq.dequantize, hf_cache.KudahitamLayer.attend
+
+    def deq(self, *a, **k):
+        calls["dequantize"] += 1
+        return real_deq(self, *a, **k)
+
+    def att(self, *a, **k):
+        calls["attend"] += 1
+        return real_attend(self, *a, **k)
+
+    monkeypatch.setattr(hf_cache.PackedSeq, "dequantize", deq)
+    monkeypatch.setattr(hf_cache.KudahitamLayer, "attend", att)
+    ids = torch.randint(0, 512, (1, 400), device="cuda")
+    new = 8
+    with torch.no_grad():
+        cache = hf_cache.KudahitamCache(head_dim=128, packed_attention=True)
+        gen = model.generate(ids, past_key_values=cache, max_new_tokens=new, do_sample=False,
+                             min_new_tokens=new)
+        assert gen.shape == (1, 400 + new)
+        assert calls["dequantize"] == 0
+        assert calls["attend"] == 2 * (new - 1)  # every decode step of both layers
+        # one more step by hand: logits from the packed cache vs uncompressed
+        logits = model(gen[:, -1:], past_key_values=cache, use_cache=True).logits[:, -1].float()
+        full = ref_model(gen, use_cache=False).logits[:, -1].float()
+        cos = torch.nn.functional.cosine_similarity(full, logits).item()
+        assert cos >= 0.9, cos
+        assert calls["dequantize"] == 0
