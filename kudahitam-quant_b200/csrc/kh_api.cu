@@ -338,7 +338,6 @@ int kh_decode_partial_gqa(const float* q, int64_t n_groups, int n_q, int head_di
   DecodeRequest r;
   memset(&r, 0, sizeof(r));
   if (!make_codebook(centroids_host, n_centroids, &r.cb)) return KH_EINVAL;
-  if (n_centroids != 2) return KH_ENOTSUP;  // decode supports the bits=1 codebook
   if (!check_d(d_k_host, head_dim)) return KH_EINVAL;
   if (n_groups == 0) return KH_OK;
   if (!q || !partials) return KH_EINVAL;

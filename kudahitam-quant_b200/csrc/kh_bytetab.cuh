@@ -16,6 +16,8 @@
 
 #include <cuda_runtime.h>
 
+#include "kh_common.cuh"
+
 namespace kh {
 
 // Calls f(std::integral_constant<int, I>) for I = 0 .. N-1, fully unrolled.
@@ -121,6 +123,53 @@ __device__ __forceinline__ uint32_t tab_addr(uint32_t x, uint32_t slots) {
   uint32_t r;
   asm("prmt.b32 %0, %1, %2, %3;" : "=r"(r) : "r"(x), "r"(slots), "n"(sel));
   return r;
+}
+
+// L2 eviction-priority policies (createpolicy) and loads that carry one.
+// Streams read once are loaded evict-first; values read again by the same
+// CTA later (decode's V norms, phase 1 then phase 2) evict-last, so the
+// rows streaming past in between do not push them out of L2.
+// (l2_policy_evict_first is in kh_common.cuh, with the TMA helpers.)
+__device__ __forceinline__ uint64_t l2_policy_evict_last() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_last.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ float ldg_policy(const float* p, uint64_t pol) {
+  float v;
+  asm("ld.global.nc.L2::cache_hint.f32 %0, [%1], %2;" : "=f"(v) : "l"(p), "l"(pol));
+  return v;
+}
+__device__ __forceinline__ uint32_t ldg_policy(const uint32_t* p, uint64_t pol) {
+  uint32_t v;
+  asm("ld.global.nc.L2::cache_hint.u32 %0, [%1], %2;" : "=r"(v) : "l"(p), "l"(pol));
+  return v;
+}
+__device__ __forceinline__ uint4 ldg_policy(const uint4* p, uint64_t pol) {
+  uint4 v;
+  asm("ld.global.nc.L2::cache_hint.v4.u32 {%0, %1, %2, %3}, [%4], %5;"
+      : "=r"(v.x), "=r"(v.y), "=r"(v.z), "=r"(v.w)
+      : "l"(p), "l"(pol));
+  return v;
+}
+
+// load_plane with an L2 policy (see load_plane below for the layouts).
+template <int D>
+__device__ __forceinline__ void load_plane_policy(const uint32_t* __restrict__ plane, int wr,
+                                                  uint64_t pol, uint32_t (&w)[D / 32]) {
+  if constexpr (D == 128) {
+    const uint4 v = ldg_policy(reinterpret_cast<const uint4*>(plane), pol);
+    w[0] = v.x;
+    w[1] = v.y;
+    w[2] = v.z;
+    w[3] = v.w;
+  } else {
+    constexpr int kW = D / 32;
+    static_for<kW>([&](auto ic) {
+      constexpr int i = decltype(ic)::value;
+      w[i] = ldg_policy(plane + ((i + wr) & (kW - 1)), pol);
+    });
+  }
 }
 
 // Row-per-thread table lookups read a plane in two steps, so that the

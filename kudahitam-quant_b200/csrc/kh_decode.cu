@@ -12,6 +12,7 @@
 //             acc_i = sum_s e^{logit_s - m} (a_s c[idx_si] + b_s sign_si)
 // Accumulation stays in the rotated domain; one FWHT per group in the
 // combine step.  A partial record is (m, l, acc[0..D-1]).
+#include <algorithm>
 #include <cmath>
 #include <cstdlib>
 #include <cstring>
@@ -36,6 +37,12 @@ struct alignas(16) DecodeParams {
   int n_splits;
   int n_q;  // queries per cache group (grouped-query attention); blockIdx.y = query row
   float c0, c1;
+  float cb[4];  // the codebook (2 or 4 levels)
+  // decode v3 work split: CTA b serves query j = b mod n_q of every cache
+  // group in the flattened range [set W, (set + 1) W) of (cache group,
+  // sequence row), set = b / n_q; W = 0: the sequence range is empty
+  int64_t W;
+  int64_t n_groups_kv;
   float dk[256];
 };
 
@@ -56,13 +63,17 @@ __device__ __forceinline__ float block_reduce(float v, float* red, bool is_max) 
 }
 
 // Block of D threads: thread t scores row (blk + t) and owns accumulator t.
-template <int D>
+// NC = 2: the bits=1 codebook (one bit per element); NC = 4: the bits=2
+// codebook, 2-bit indices, element e at bits 2 (e & 15) of word e >> 4.
+// This direct kernel is the datapath of the 4-level codebook.
+template <int D, int NC>
 __global__ void __launch_bounds__(D)
     decode_partial_kernel(const __grid_constant__ DecodeParams P) {
-  constexpr int W = D / 32;
+  constexpr int W = D / 32;                      // residual-plane words
+  constexpr int WC = NC == 2 ? D / 32 : D / 16;  // code-plane words
   __shared__ float qt[D];
   __shared__ float w1[D], w2[D];
-  __shared__ uint32_t vc[D][W + 1], vr[D][W + 1];
+  __shared__ uint32_t vc[D][WC + 1], vr[D][W + 1];
   __shared__ float red[32];
 
   const int t = threadIdx.x;
@@ -74,6 +85,10 @@ __global__ void __launch_bounds__(D)
   const int64_t s1 = P.seq_begin + len * (split + 1) / P.n_splits;
   const float inv_sqrt_d = 1.0f / sqrtf((float)D);
   const float qjl = 0.7978845608028654f / (float)D;  // sqrt(2/pi) / D
+  const float cv0 = P.cb[0], cv1 = P.cb[1], cv2 = P.cb[2], cv3 = P.cb[3];
+  auto cval = [=](uint32_t idx) -> float {  // c[idx] without dynamic indexing
+    return idx < 2 ? (idx ? cv1 : cv0) : (idx == 2 ? cv2 : cv3);
+  };
 
   // q~ = H(q (.) d) / sqrt(D)
   qt[t] = P.q[g * D + t] * P.dk[t];
@@ -100,47 +115,65 @@ __global__ void __launch_bounds__(D)
     if (valid) {
       const int64_t row = gk * P.seq_len + s;
       float m1 = 0.f, m2 = 0.f;
+      if constexpr (NC == 2) {
 #pragma unroll
-      for (int w = 0; w < W; ++w) {
-        const uint32_t c = P.k_code[row * W + w];
-        const uint32_t r = P.k_res[row * W + w];
+        for (int w = 0; w < W; ++w) {
+          const uint32_t c = P.k_code[row * W + w];
+          const uint32_t r = P.k_res[row * W + w];
 #pragma unroll
-        for (int k = 0; k < 32; ++k) {
-          const float qv = qt[32 * w + k];
-          m1 += ((c >> k) & 1u) ? qv : 0.f;
-          m2 += ((r >> k) & 1u) ? qv : 0.f;
+          for (int k = 0; k < 32; ++k) {
+            const float qv = qt[32 * w + k];
+            m1 += ((c >> k) & 1u) ? qv : 0.f;
+            m2 += ((r >> k) & 1u) ? qv : 0.f;
+          }
+        }
+        m1 = P.c0 * Q + (P.c1 - P.c0) * m1;  // <q~, c[idx]>
+      } else {
+#pragma unroll 1
+        for (int w = 0; w < WC; ++w) {
+          const uint32_t c = P.k_code[row * WC + w];
+#pragma unroll
+          for (int k = 0; k < 16; ++k) m1 += qt[16 * w + k] * cval((c >> (2 * k)) & 3u);
+        }
+#pragma unroll 1
+        for (int w = 0; w < W; ++w) {
+          const uint32_t r = P.k_res[row * W + w];
+#pragma unroll
+          for (int k = 0; k < 32; ++k) m2 += ((r >> k) & 1u) ? qt[32 * w + k] : 0.f;
         }
       }
-      const float score =
-          P.k_norms[row] * (P.c0 * Q + (P.c1 - P.c0) * m1) +
-          inv_sqrt_d * (2.f * m2 - Q) * P.k_rnorms[row];
+      const float score = P.k_norms[row] * m1 + inv_sqrt_d * (2.f * m2 - Q) * P.k_rnorms[row];
       logit = score * P.sm_scale;
       va = P.v_norms[row] * inv_sqrt_d;
       vb = P.v_rnorms[row] * qjl;
 #pragma unroll
-      for (int w = 0; w < W; ++w) {
-        vc[t][w] = P.v_code[row * W + w];
-        vr[t][w] = P.v_res[row * W + w];
-      }
+      for (int w = 0; w < WC; ++w) vc[t][w] = P.v_code[row * WC + w];
+#pragma unroll
+      for (int w = 0; w < W; ++w) vr[t][w] = P.v_res[row * W + w];
     } else {
 #pragma unroll
-      for (int w = 0; w < W; ++w) vc[t][w] = vr[t][w] = 0u;
+      for (int w = 0; w < WC; ++w) vc[t][w] = 0u;
+#pragma unroll
+      for (int w = 0; w < W; ++w) vr[t][w] = 0u;
     }
     const float m_blk = block_reduce<D>(logit, red, true);
     const float m_new = fmaxf(m_run, m_blk);
     const float alpha = expf(m_run - m_new);  // 0 on the first block
     const float p = valid ? expf(logit - m_new) : 0.f;
     const float l_blk = block_reduce<D>(p, red, false);
-    // constant part: sum_s p (a c0 - b)
-    const float base = block_reduce<D>(p * (va * P.c0 - vb), red, false);
-    w1[t] = p * va * (P.c1 - P.c0);
+    // constant part: sum_s p (a c0 - b) (NC = 2), sum_s -p b (NC = 4)
+    const float base = block_reduce<D>(p * ((NC == 2 ? va * P.c0 : 0.f) - vb), red, false);
+    w1[t] = NC == 2 ? p * va * (P.c1 - P.c0) : p * va;
     w2[t] = 2.f * p * vb;
     __syncthreads();
     float a = acc * alpha + base;
     const int wi = t >> 5, bi = t & 31;
     const int nrow = (int)(s1 - blk < D ? s1 - blk : D);
     for (int j = 0; j < nrow; ++j) {
-      a += ((vc[j][wi] >> bi) & 1u) ? w1[j] : 0.f;
+      if constexpr (NC == 2)
+        a += ((vc[j][wi] >> bi) & 1u) ? w1[j] : 0.f;
+      else
+        a += cval((vc[j][t >> 4] >> (2 * (t & 15))) & 3u) * w1[j];
       a += ((vr[j][wi] >> bi) & 1u) ? w2[j] : 0.f;
     }
     acc = a;
@@ -665,16 +698,18 @@ struct RowKV {
 };
 
 
+// Phase-1 loads: K planes and norms are read once (evict-first); the V
+// norms are read again by phase 2 of the same segment (evict-last).
 template <int D>
 __device__ __forceinline__ void load_k_row(const DecodeParams& P, int64_t row, int wr, int bs,
-                                           RowKV<D>& a) {
+                                           uint64_t once, uint64_t again, RowKV<D>& a) {
   constexpr int kW = D / 32;
-  load_plane<D>(P.k_code + row * kW, wr, a.c);
-  load_plane<D>(P.k_res + row * kW, wr, a.r);
-  a.n = __ldg(P.k_norms + row);
-  a.rn = __ldg(P.k_rnorms + row);
-  a.vn = __ldg(P.v_norms + row);
-  a.vrn = __ldg(P.v_rnorms + row);
+  load_plane_policy<D>(P.k_code + row * kW, wr, once, a.c);
+  load_plane_policy<D>(P.k_res + row * kW, wr, once, a.r);
+  a.n = ldg_policy(P.k_norms + row, once);
+  a.rn = ldg_policy(P.k_rnorms + row, once);
+  a.vn = ldg_policy(P.v_norms + row, again);
+  a.vrn = ldg_policy(P.v_rnorms + row, again);
 }
 
 template <int NT>
@@ -727,37 +762,12 @@ __global__ void __launch_bounds__(256, 2)
 
   const int t = threadIdx.x;
   const int lane = t & 31;
-  const int64_t g = blockIdx.y;      // query row (q, partial records)
-  const int64_t gk = g / P.n_q;      // cache group it reads
-  const int split = blockIdx.x;
-  const int64_t len = P.seq_end - P.seq_begin;
-  const int64_t s0 = P.seq_begin + len * split / P.n_splits;
-  const int64_t s1 = P.seq_begin + len * (split + 1) / P.n_splits;
   const float inv_sqrt_d = 1.0f / sqrtf((float)D);
   const float qjl = 0.7978845608028654f / (float)D;  // sqrt(2/pi) / D
   const float dc = P.c1 - P.c0;
   const float lscale = P.sm_scale * kLog2e;
   const float c0dc = P.c0 / dc;
   const float wa = inv_sqrt_d * dc, wb = 2.f * qjl;  // V weight = p (wa |v| + wb r_norm)
-
-  // q~ = H(q (.) d) / sqrt(D)
-  for (int i = t; i < D; i += NT) qt[i] = P.q[g * D + i] * P.dk[i];
-  __syncthreads();
-  for (int h = 1; h < D; h <<= 1) {
-    for (int b = t; b < D / 2; b += NT) {
-      const int lo = (b / h) * 2 * h + (b % h);
-      const float a = qt[lo], c = qt[lo + h];
-      qt[lo] = a + c;
-      qt[lo + h] = a - c;
-    }
-    __syncthreads();
-  }
-  float qpart = 0.f;
-  for (int i = t; i < D; i += NT) {
-    qt[i] *= inv_sqrt_d;
-    qpart += qt[i];
-  }
-  const float Q = block_sum<NT>(qpart, red);  // (its barriers also publish qt)
 
   // lane constants: byte k of a rotated plane is plane byte (k + rr) mod kP,
   // looked up in slot ((k + lane) mod kP) + kP (lane / kP)
@@ -790,7 +800,57 @@ __global__ void __launch_bounds__(256, 2)
     slot4y[m] = slot4[m] ^ 0x40404040u;  // 4 * (slot +- 16) in every byte
   });
 
+  // Work split.  The (cache group, sequence row) pairs of the call are laid
+  // out group after group, L rows each, and cut into ranges of W pairs, one
+  // per CTA set (n_q CTAs: one per query of the group, running side by side
+  // so the group's rows are read from L2 after the first).  A CTA takes the
+  // pieces of its range one group at a time; a group's pieces are its
+  // records, numbered from the first set that covers it, and the set that
+  // ends the group marks its unused record slots empty (l = 0).  Every CTA
+  // gets the same number of rows whatever the group count, so no wave of
+  // CTAs runs part-full.
+  const int64_t L = P.seq_end - P.seq_begin;
+  if (P.W == 0) {  // empty range: every record of query row blockIdx.x is empty
+    if (t == 0)
+      for (int p = 0; p < P.n_splits; ++p) {
+        float* e = P.partials +
+                   ((int64_t)blockIdx.x * P.part_stride + P.part_offset + p) * (D + 2);
+        e[0] = -INFINITY;
+        e[1] = 0.f;
+      }
+    return;
+  }
+  const int jq = (int)(blockIdx.x % (unsigned)P.n_q);
+  const int64_t set = blockIdx.x / (unsigned)P.n_q;
+  const int64_t wbeg = set * P.W;
+  const int64_t wend = min(wbeg + P.W, P.n_groups_kv * L);
+  for (int64_t gk = wbeg / L; gk * L < wend; ++gk) {
+  const int64_t g = gk * P.n_q + jq;  // query row (q, partial records)
+  const int64_t s0 = P.seq_begin + max(wbeg - gk * L, (int64_t)0);
+  const int64_t s1 = P.seq_begin + min(wend - gk * L, L);
+  const int64_t rpart = set - gk * L / P.W;  // this piece's record slot
+
+  // q~ = H(q (.) d) / sqrt(D)
+  for (int i = t; i < D; i += NT) qt[i] = P.q[g * D + i] * P.dk[i];
+  __syncthreads();
+  for (int h = 1; h < D; h <<= 1) {
+    for (int b = t; b < D / 2; b += NT) {
+      const int lo = (b / h) * 2 * h + (b % h);
+      const float a = qt[lo], c = qt[lo + h];
+      qt[lo] = a + c;
+      qt[lo + h] = a - c;
+    }
+    __syncthreads();
+  }
+  float qpart = 0.f;
+  for (int i = t; i < D; i += NT) {
+    qt[i] *= inv_sqrt_d;
+    qpart += qt[i];
+  }
+  const float Q = block_sum<NT>(qpart, red);  // (its barriers also publish qt)
+
   float m_run = -INFINITY, l_run = 0.f, c_run = 0.f, acc = 0.f;
+  const uint64_t pol_once = l2_policy_evict_first(), pol_again = l2_policy_evict_last();
 
   for (int64_t c0 = s0; c0 < s1; c0 += C::kSeg) {
     const int n = (int)min((int64_t)C::kSeg, s1 - c0);
@@ -811,7 +871,7 @@ __global__ void __launch_bounds__(256, 2)
 #pragma unroll
         for (int u = 0; u < B; ++u) {
           const int ii = t + (bi * B + u) * NT;
-          load_k_row<D>(P, row0 + (ii < n ? ii : 0), wr, bs, dst[u]);
+          load_k_row<D>(P, row0 + (ii < n ? ii : 0), wr, bs, pol_once, pol_again, dst[u]);
         }
       };
       auto score_batch = [&](const RowKV<D>(&src)[B], int bi) {
@@ -875,10 +935,10 @@ __global__ void __launch_bounds__(256, 2)
       for (int u = 0; u < B; ++u) {
         const int ii = t + (bi * B + u) * NT;
         const int64_t row = row0 + (ii < n ? ii : 0);
-        load_plane<D>(vx + row * (D / 32), wr, dst[u].c);
-        load_plane<D>(vy + row * (D / 32), wr, dst[u].r);
-        dst[u].n = __ldg(vxn + row);
-        dst[u].rn = __ldg(vyn + row);
+        load_plane_policy<D>(vx + row * (D / 32), wr, pol_once, dst[u].c);
+        load_plane_policy<D>(vy + row * (D / 32), wr, pol_once, dst[u].r);
+        dst[u].n = ldg_policy(vxn + row, pol_once);
+        dst[u].rn = ldg_policy(vyn + row, pol_once);
       }
     };
     static_for<C::kRing - 1>([&](auto jc) { load_vbatch(va[decltype(jc)::value], decltype(jc)::value); });
@@ -1035,11 +1095,22 @@ __global__ void __launch_bounds__(256, 2)
     __syncthreads();  // fold reads done before the next segment's table
   }
 
-  float* rec = P.partials + (g * P.part_stride + P.part_offset + split) * (D + 2);
-  if (t < D) rec[2 + t] = c_run + acc;
-  if (t == 0) {
-    rec[0] = m_run * kLn2;  // natural-log units for the combine step
-    rec[1] = l_run;
+  if (rpart < P.n_splits) {  // the host sizes W so that it always is
+    float* rec = P.partials + (g * P.part_stride + P.part_offset + rpart) * (D + 2);
+    if (t < D) rec[2 + t] = c_run + acc;
+    if (t == 0) {
+      rec[0] = m_run * kLn2;  // natural-log units for the combine step
+      rec[1] = l_run;
+    }
+  }
+  if (s1 == P.seq_end && t == 0) {  // this set ends the group: empty the unused slots
+    for (int64_t p = rpart + 1; p < P.n_splits; ++p) {
+      float* e = P.partials + (g * P.part_stride + P.part_offset + p) * (D + 2);
+      e[0] = -INFINITY;
+      e[1] = 0.f;
+    }
+  }
+  __syncthreads();  // q~ and the reduction scratch are rewritten by the next piece
   }
 }
 
@@ -1060,13 +1131,44 @@ kh_status launch_decode_partial(const DecodeRequest& r, cudaStream_t stream) {
   P.n_q = r.n_q;
   P.c0 = r.cb.c[0];
   P.c1 = r.cb.c[1];
+  for (int i = 0; i < 4; ++i) P.cb[i] = r.cb.c[i];
   for (int i = 0; i < r.D; ++i) P.dk[i] = r.dk[i];
   const dim3 grid((unsigned)r.n_splits, (unsigned)(r.n_groups * r.n_q));
   const char* env = getenv("KUDAHITAM_DECODE_PATH");
-  const int path = (env && strcmp(env, "v1") == 0) ? 1 : (env && strcmp(env, "v2") == 0) ? 2 : 3;
+  int path = (env && strcmp(env, "v1") == 0) ? 1 : (env && strcmp(env, "v2") == 0) ? 2 : 3;
+  if (r.cb.n_c == 4) path = 1;  // the 4-level codebook runs the direct kernel
+  // v3 work split (see decode_v3_kernel): ranges of W (cache group, row)
+  // pairs, one CTA set of n_q CTAs each.  W balances the pairs over one
+  // wave of CTAs at two per SM, and is at least L / (n_splits - 1) so that
+  // no group spans more than n_splits ranges (its record slots); with one
+  // record per row, one range per group.
+  const int64_t L = r.seq_end - r.seq_begin;
+  P.n_groups_kv = r.n_groups;
+  int64_t n_cta = 0;
+  if (L == 0) {
+    P.W = 0;
+    n_cta = r.n_groups * r.n_q;
+  } else if (r.n_splits == 1) {
+    P.W = L;
+    n_cta = r.n_groups * r.n_q;
+  } else {
+    const int64_t total = r.n_groups * L;
+    const int64_t sets = std::max<int64_t>(1, 2 * (int64_t)sm_count() / r.n_q);
+    const int64_t w_bal = std::max<int64_t>(512, (total + sets - 1) / sets);
+    const int64_t w_min = (L + r.n_splits - 2) / (r.n_splits - 1);
+    P.W = std::max(w_bal, w_min);
+    n_cta = (total + P.W - 1) / P.W * r.n_q;
+  }
+  if (n_cta > 0x7fffffff) return KH_EINVAL;
+  const dim3 grid3((unsigned)n_cta);
   if (path == 1) {
-    if (r.D == 128) decode_partial_kernel<128><<<grid, 128, 0, stream>>>(P);
-    else decode_partial_kernel<256><<<grid, 256, 0, stream>>>(P);
+    if (r.cb.n_c == 4) {
+      if (r.D == 128) decode_partial_kernel<128, 4><<<grid, 128, 0, stream>>>(P);
+      else decode_partial_kernel<256, 4><<<grid, 256, 0, stream>>>(P);
+    } else {
+      if (r.D == 128) decode_partial_kernel<128, 2><<<grid, 128, 0, stream>>>(P);
+      else decode_partial_kernel<256, 2><<<grid, 256, 0, stream>>>(P);
+    }
   } else {
     // the shared-memory opt-in is a per-device function attribute
     int dev = 0;
@@ -1077,7 +1179,7 @@ kh_status launch_decode_partial(const DecodeRequest& r, cudaStream_t stream) {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
       });
       if (path == 3)  // v3 waits for the previous kernel before its first read
-        launch_programmatic(kern, grid, dim3(threads), smem, stream, P);
+        launch_programmatic(kern, grid3, dim3(threads), smem, stream, P);
       else
         kern<<<grid, threads, smem, stream>>>(P);
     };

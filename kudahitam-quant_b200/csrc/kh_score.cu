@@ -8,8 +8,10 @@
 // so for a two-level codebook, with M1 = sum_{idx_i=1} q~_i,
 // M2 = sum_{sign_i=+1} q~_i and Q = sum_i q~_i:
 //   score = norm (c0 Q + (c1 - c0) M1) + r_norm / sqrt(D) (2 M2 - Q).
-// Two-level codebooks take the table-driven kernel (score_tab_kernel); the
-// 4-level codebook (and KUDAHITAM_SCORE_PATH=direct) the direct one.
+// Two-level codebooks take the table-driven kernel (score_tab_kernel), the
+// 4-level codebook at D = 128 its 2-bit-plane variant (score_tab2b_kernel);
+// the 4-level codebook at D = 256 (and KUDAHITAM_SCORE_PATH=direct) the
+// direct one.
 #include <algorithm>
 #include <cmath>
 #include <cstdlib>
@@ -280,6 +282,162 @@ __global__ void __launch_bounds__(256, 2)
   }
 }
 
+// Table-driven scores for the 4-level (bits=2) codebook at D = 128.  The
+// code plane holds 2-bit indices, 4 elements per byte (32 bytes per row), so
+// its table folds the centroids in: T2[v][p] = sum_{k<4} q~[4p+k]
+// c[(v >> 2k) & 3], and a row's  <q~, c[idx]>  is 32 lookups.  The residual
+// plane keeps the 1-bit table (sum of q~ over set bits, 16 positions in two
+// copies).  Both tables share the 64-word table rows: T2 in entries 0..31
+// (one copy, lane l looks up position (k + l) mod 32 at step k), the
+// residual table in entries 32..63.  score = norm * M_code +
+// r_norm / sqrt(D) (2 M_res - Q).
+template <bool RES>
+__global__ void __launch_bounds__(256, 2)
+    score_tab2b_kernel(const __grid_constant__ ScoreParams P) {
+  grid_dependency_wait();  // q and the cache may come from the previous kernel
+  constexpr int D = 128;
+  constexpr int kPC = 32, kWC = 8;  // code plane: byte positions, words
+  constexpr int kPR = 16, kWR = 4;  // residual plane
+  constexpr int NT = 256;
+  constexpr int B = 2;
+  constexpr int kRing = 3;
+  extern __shared__ __align__(16) unsigned char smem_s[];
+  unsigned char* tabb = smem_s;
+  float* tab = reinterpret_cast<float*>(smem_s);
+  float* qt = tab + 256 * 64;
+  float* red = qt + D;
+
+  const int t = threadIdx.x;
+  const int lane = t & 31;
+  const int64_t y = blockIdx.y;
+  const int64_t gk = y / P.n_q;
+  const int64_t s0 = (int64_t)blockIdx.x * P.chunk;
+  const int n = (int)min(P.chunk, P.seq_len - s0);
+  const int64_t row0 = gk * P.seq_len + s0;
+  const float inv_sqrt_d = 1.0f / sqrtf((float)D);
+
+  for (int i = t; i < D; i += NT) qt[i] = P.q[y * D + i] * P.d[i];
+  __syncthreads();
+  for (int h = 1; h < D; h <<= 1) {
+    for (int b = t; b < D / 2; b += NT) {
+      const int lo = (b / h) * 2 * h + (b % h);
+      const float a = qt[lo], c = qt[lo + h];
+      qt[lo] = a + c;
+      qt[lo + h] = a - c;
+    }
+    __syncthreads();
+  }
+  float qpart = 0.f;
+  for (int i = t; i < D; i += NT) {
+    qt[i] *= inv_sqrt_d;
+    qpart += qt[i];
+  }
+  const float Q = block_sum<NT>(qpart, red);  // (its barriers also publish qt)
+  {
+    // T2: thread (position p = t mod 32, w = t / 32) fills the byte values
+    // v = w + 8 kk: low nibble w + 8 (kk & 1), high nibble kk >> 1
+    const int p = t & 31, w = t >> 5;
+    const float c[4] = {P.cb.c[0], P.cb.c[1], P.cb.c[2], P.cb.c[3]};
+    const float q0 = qt[4 * p], q1 = qt[4 * p + 1], q2 = qt[4 * p + 2], q3 = qt[4 * p + 3];
+    float lo[2];
+#pragma unroll
+    for (int h = 0; h < 2; ++h) {
+      const int v = w + 8 * h;
+      lo[h] = q0 * c[v & 3] + q1 * c[(v >> 2) & 3];
+    }
+    static_for<32>([&](auto kc) {
+      constexpr int kk = decltype(kc)::value, hv = kk >> 1;
+      const float hi = q2 * c[hv & 3] + q3 * c[(hv >> 2) & 3];
+      tab[(w + 8 * kk) * 64 + p] = lo[kk & 1] + hi;
+    });
+  }
+  if constexpr (RES) build_byte_table<D>(tab + 32, qt, t);
+  __syncthreads();
+
+  // code plane: rotation by lane bytes (of 32), slots 0..31
+  const int wrc = lane >> 2, bsc = 8 * (lane & 3);
+  uint32_t slotc[kPC / 4];
+  static_for<kPC / 4>([&](auto mc) {
+    constexpr int m = decltype(mc)::value;
+    uint32_t v = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v |= (4u * (uint32_t)((4 * m + j + lane) % kPC)) << (8 * j);
+    slotc[m] = v;
+  });
+  // residual plane: rotation by lane mod 16, two copies (slots 32 + ...)
+  const int rr = lane % kPR;
+  const int wrr = rr >> 2, bsr = 8 * (rr & 3);
+  uint32_t slotr[kPR / 4];
+  static_for<kPR / 4>([&](auto mc) {
+    constexpr int m = decltype(mc)::value;
+    uint32_t v = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      v |= (4u * (uint32_t)(((4 * m + j + lane) % kPR) + kPR * (lane / kPR))) << (8 * j);
+    slotr[m] = v;
+  });
+  const unsigned char* tabr = tabb + 128;  // entries 32..63 of each table row
+
+  struct Row {
+    uint32_t c[kWC], r[RES ? kWR : 1];
+    float n, rn;
+  };
+  const int nb = (n + NT * B - 1) / (NT * B);
+  auto load_batch = [&](Row (&dst)[B], int bi) {
+#pragma unroll
+    for (int u = 0; u < B; ++u) {
+      const int ii = t + (bi * B + u) * NT;
+      const int64_t row = row0 + (ii < n ? ii : 0);
+      load_plane<256>(P.code + row * kWC, wrc, dst[u].c);  // 32-byte plane, words rotated
+      dst[u].n = __ldg(P.norms + row);
+      if constexpr (RES) {
+        load_plane<128>(P.res + row * kWR, wrr, dst[u].r);
+        dst[u].rn = __ldg(P.rnorms + row);
+      }
+    }
+  };
+  auto score_batch = [&](const Row (&src)[B], int bi) {
+#pragma unroll
+    for (int u = 0; u < B; ++u) {
+      float2 m = make_float2(0.f, 0.f);
+      uint32_t rc[kWC];
+      rotate_plane<256>(src[u].c, wrc, bsc, rc);
+      static_for<kPC>([&](auto kc) {
+        constexpr int k = decltype(kc)::value;
+        const float x = *reinterpret_cast<const float*>(
+            tabb + tab_addr<k & 3>(rc[k >> 2], slotc[k >> 2]));
+        if constexpr (k & 1) m.y += x; else m.x += x;
+      });
+      float sc = src[u].n * (m.x + m.y);
+      if constexpr (RES) {
+        uint32_t rs[kWR];
+        rotate_plane<128>(src[u].r, wrr, bsr, rs);
+        float2 mr = make_float2(0.f, 0.f);
+        static_for<kPR>([&](auto kc) {
+          constexpr int k = decltype(kc)::value;
+          const float x = *reinterpret_cast<const float*>(
+              tabr + tab_addr<k & 3>(rs[k >> 2], slotr[k >> 2]));
+          if constexpr (k & 1) mr.y += x; else mr.x += x;
+        });
+        sc += inv_sqrt_d * (2.f * (mr.x + mr.y) - Q) * src[u].rn;
+      }
+      const int ii = t + (bi * B + u) * NT;
+      if (ii < n) P.out[y * P.seq_len + s0 + ii] = sc;
+    }
+  };
+  Row a[kRing][B];
+  static_for<kRing - 1>([&](auto jc) { load_batch(a[decltype(jc)::value], decltype(jc)::value); });
+  for (int bi = 0; bi < nb; bi += kRing) {
+    static_for<kRing>([&](auto jc) {
+      constexpr int j = decltype(jc)::value;
+      if (bi + j < nb) {
+        load_batch(a[(j + kRing - 1) % kRing], bi + j + kRing - 1);
+        score_batch(a[j], bi + j);
+      }
+    });
+  }
+}
+
 }  // namespace
 
 kh_status launch_score(const float* q, int64_t n_groups, int n_q, int D,
@@ -299,7 +457,8 @@ kh_status launch_score(const float* q, int64_t n_groups, int n_q, int D,
   P.cb = cb;
   for (int i = 0; i < D; ++i) P.d[i] = d[i];
   const char* env = getenv("KUDAHITAM_SCORE_PATH");
-  if (cb.n_c == 2 && !(env && strcmp(env, "direct") == 0)) {
+  const bool direct = env && strcmp(env, "direct") == 0;
+  if (!direct && (cb.n_c == 2 || D == 128)) {
     // table-driven path: one CTA per (chunk of cached rows, query row)
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return KH_ECUDA;
@@ -313,7 +472,7 @@ kh_status launch_score(const float* q, int64_t n_groups, int n_q, int D,
     const int64_t bxt = (seq_len + P.chunk - 1) / P.chunk;
     if (bxt > 0x7fffffff) return KH_EINVAL;
     const dim3 gridt((unsigned)bxt, (unsigned)rows_q);
-    static std::once_flag once[4][64];
+    static std::once_flag once[6][64];
     auto launch = [&](auto kern, int slot, int smem) {
       std::call_once(once[slot][dev & 63], [&] {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -321,7 +480,10 @@ kh_status launch_score(const float* q, int64_t n_groups, int n_q, int D,
       launch_programmatic(kern, gridt, dim3(256), smem, stream, P);
     };
     const bool r = res != nullptr;
-    if (D == 128) {
+    if (cb.n_c == 4) {  // D == 128
+      if (r) launch(score_tab2b_kernel<true>, 4, ScoreTabCfg<128>::kSmem);
+      else launch(score_tab2b_kernel<false>, 5, ScoreTabCfg<128>::kSmem);
+    } else if (D == 128) {
       if (r) launch(score_tab_kernel<128, true>, 0, ScoreTabCfg<128>::kSmem);
       else launch(score_tab_kernel<128, false>, 1, ScoreTabCfg<128>::kSmem);
     } else {

@@ -173,7 +173,7 @@ def decode_attention_seq_sharded(q: torch.Tensor, k_local: ops.PackedKV,
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(D)
     if n_splits is None:
-        n_splits = ops.default_splits(R, S_loc, q.device)
+        n_splits = ops.default_splits(R, S_loc, q.device, 1 if q.dim() == 2 else q.shape[1])
     rec = D + 2
     need = seq_sharded_workspace_numel(R, n_splits, world, D)
     if partials is None or partials.numel() < need:

@@ -368,29 +368,31 @@ def decode_workspace_bytes(n_groups: int, n_splits: int, head_dim: int) -> int:
     return int(_lib.lib().kh_decode_workspace_bytes(n_groups, n_splits, head_dim))
 
 
-def default_splits(n_groups: int, seq_len: int, device) -> int:
-    """Splits per query row for decode: enough (row, split) blocks for about
-    three waves at two blocks per SM, but no split shorter than 4096 rows.
-    A block's set-up (query transform, byte table, per-segment reductions and
-    fold) is paid once per split, so short splits cost more than the waves
-    they fill.  Measured on one B200 with 512 query rows (D = 128, us for
-    partial + combine; the rule's choice starred):
+def default_splits(n_groups: int, seq_len: int, device, n_q: int = 1) -> int:
+    """Records per query row for decode (the ``n_splits`` argument), for
+    n_groups query rows (n_q per cache group) of seq_len cached rows.
 
-        S       1 split   2        4        5
-        5000    60.7*     64.8     81.2     85.3
-        10000   107.8     99.6*    114.0    120.3
-        20000   195.7     181.9*   181.6    194.2
-        40000   367.7     339.2*   343.1    339.2
-    """
+    The decode kernel cuts the call's (cache group, row) pairs into equal
+    ranges, one wave of CTAs at two per SM, whatever the group count; a
+    group spanning several ranges gets one record per range.  This rule
+    returns how many records the longest group can need at that range
+    length (2 when the ranges are at least a group long), so the kernel
+    runs balanced.  (The earlier one-CTA-per-(row, split) grid ran 1.73
+    waves for 512 query rows on 148 SMs.)"""
     sms = torch.cuda.get_device_properties(device).multi_processor_count
-    return splits_for(n_groups, seq_len, sms)
+    return splits_for(n_groups, seq_len, sms, n_q)
 
 
-def splits_for(n_rows: int, seq_len: int, n_sms: int) -> int:
-    """The split rule of ``default_splits`` for a GPU with n_sms SMs."""
-    fill = -(-3 * 2 * n_sms // max(n_rows, 1))  # ceil(3 waves of 2 blocks per SM / rows)
-    by_rows = max(1, seq_len // 4096)
-    return int(max(1, min(fill, by_rows, 1024)))
+def splits_for(n_rows: int, seq_len: int, n_sms: int, n_q: int = 1) -> int:
+    """The rule of ``default_splits`` for a GPU with n_sms SMs; mirrors the
+    decode launcher's range length (kh_decode.cu: one wave of CTA sets of
+    n_q CTAs at two CTAs per SM, at least 512 rows per range)."""
+    if seq_len <= 0 or n_rows <= 0:
+        return 1
+    groups = max(1, n_rows // max(n_q, 1))
+    sets = max(1, 2 * n_sms // max(n_q, 1))
+    w_bal = max(512, -(-groups * seq_len // sets))
+    return int(min(1024, -(-seq_len // w_bal) + 1))
 
 
 def decode_partial(q: torch.Tensor, k: PackedKV, v: PackedKV, dk, dv, centroids,
@@ -487,7 +489,7 @@ def decode_attention(q: torch.Tensor, k: PackedKV, v: PackedKV, dk, dv, centroid
     if sm_scale is None:
         sm_scale = 1.0 / math.sqrt(D)
     if n_splits is None:
-        n_splits = default_splits(G * n_q, L, dev)
+        n_splits = default_splits(G * n_q, L, dev, n_q)
     if not (k.residual and v.residual):
         raise ValueError("decode attention needs caches compressed with the residual plane")
     if workspace is None:

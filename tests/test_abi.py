@@ -95,8 +95,8 @@ def test_other_entry_points_validate():
                                100, 50, 10, D128, D128, C2, 2, 0.1, 2, FAKE, 2, 0,
                                None) == _lib.KH_EINVAL  # seq_end < seq_begin
     assert L.kh_decode_partial(FAKE, 2, 128, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE,
-                               100, 0, 100, D128, D128, _f([-0.1, -0.05, 0.05, 0.1]), 4, 0.1,
-                               2, FAKE, 2, 0, None) == _lib.KH_ENOTSUP
+                               100, 0, 100, D128, D128, _f([-0.1, 0.05, -0.05, 0.1]), 4, 0.1,
+                               2, FAKE, 2, 0, None) == _lib.KH_EINVAL  # unsorted codebook
     assert L.kh_decode_attn(FAKE, 2, 128, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 100,
                             D128, D128, C2, 2, 0.1, 4, FAKE, 16, FAKE,
                             None) == _lib.KH_EINVAL  # workspace too small

@@ -287,7 +287,7 @@ def _group_rows(raw, g: int) -> torch.Tensor:
     return raw[g // 64][g % 64].cpu()
 
 
-@pytest.mark.parametrize("bits", [1])
+@pytest.mark.parametrize("bits", [1, 2])
 def test_decode_at_40k_context_sampled(bits):
     dev = torch.device("cuda")
     q, dk, dv, c, raw, pk = _decode_cache(dev, bits)

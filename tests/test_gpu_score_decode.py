@@ -68,13 +68,14 @@ def test_scores_match_oracle(D, bits, residual):
     assert max(errs) < 1e-4, f"engine vs oracle: {errs}"
 
 
-@pytest.mark.parametrize("residual", [True, False])
-def test_table_scores_span_several_ctas_and_equal_direct_kernel(residual, monkeypatch):
+@pytest.mark.parametrize("bits,residual", [(1, True), (1, False), (2, True)])
+def test_table_scores_span_several_ctas_and_equal_direct_kernel(bits, residual, monkeypatch):
     """Groups longer than one table CTA (8192 rows) with a ragged tail, two
-    queries per group: the table-driven kernel against the direct
-    bit-select kernel and against the reference formula on the same cache."""
+    queries per group: the table-driven kernel (the 2-bit-plane variant for
+    the bits=2 codebook) against the direct bit-select kernel and against
+    the reference formula on the same cache."""
     D, G, S, nq = 128, 2, 2 * 8192 + 1234, 2
-    d, c = rademacher(D, 4).numpy(), lloyd_max(1, D).numpy()
+    d, c = rademacher(D, 4).numpy(), lloyd_max(bits, D).numpy()
     x = K.synth((1, G, S, D), dtype=torch.bfloat16, seed=12)
     q = torch.randn(G, nq, D, generator=torch.Generator().manual_seed(2)).cuda()
     p = ops.compress(x.cuda(), d, c, residual=residual)
@@ -173,6 +174,32 @@ def test_decode_attention_matches_oracle(D, S, decode_path):
                     rk["rnorms"].reshape(G, S), rv["kmse"].reshape(G, S, D),
                     rv["signs"].reshape(G, S, D), rv["rnorms"].reshape(G, S), dk, dv, sm)
     for n_splits in (1, 3, 16):
+        got = ops.decode_attention(q.cuda(), pk, pv, dk, dv, c, sm, n_splits=n_splits)
+        got = got.cpu().numpy()
+        for gi in range(G):
+            assert K.normwise(got[gi], want[gi]) < 1e-3, (n_splits, gi)
+
+
+@pytest.mark.parametrize("D", [128, 256])
+@pytest.mark.parametrize("S", [1, 300, 2000])
+def test_decode_bits2_codebook_matches_oracle(D, S):
+    """The 4-level (bits=2) codebook: 2-bit code plane plus the residual
+    plane, V reconstructed with c[idx] from four levels (the direct decode
+    kernel), against the oracle's fp64 decode of its own compression."""
+    G = 4
+    dk, dv = rademacher(D, 10).numpy(), rademacher(D, 11).numpy()
+    c = lloyd_max(2, D).numpy()
+    k = K.synth((1, G, S, D), dtype=torch.bfloat16, seed=S + 1)
+    v = K.synth((1, G, S, D), dtype=torch.bfloat16, seed=S + 2)
+    q = torch.randn(G, D, generator=torch.Generator().manual_seed(S)).to(torch.bfloat16)
+    pk, pv = ops.compress(k.cuda(), dk, c), ops.compress(v.cuda(), dv, c)
+    assert pk.bits == 2
+    sm = 1.0 / math.sqrt(D)
+    rk, rv = O.compress_v8(k, dk, c), O.compress_v8(v, dv, c)
+    want = O.decode(q.float().numpy(), rk["kmse"].reshape(G, S, D), rk["signs"].reshape(G, S, D),
+                    rk["rnorms"].reshape(G, S), rv["kmse"].reshape(G, S, D),
+                    rv["signs"].reshape(G, S, D), rv["rnorms"].reshape(G, S), dk, dv, sm)
+    for n_splits in (1, 3):
         got = ops.decode_attention(q.cuda(), pk, pv, dk, dv, c, sm, n_splits=n_splits)
         got = got.cpu().numpy()
         for gi in range(G):
