@@ -279,8 +279,8 @@ def reference_kernel_on_gpu(args):
     """For context: the reference's own CUDA kernel v8 (KudaHitamCUDA.cu:13-231,
     built from the reference source into oracle/_ref) on this GPU, on the same
     K and V rows, through its own launcher (which allocates the 6D+8 bytes per
-    row of reference-layout outputs each call).  None without a GPU or that
-    build."""
+    row of reference-layout outputs each call), beside this engine's compat
+    operator on the same rows.  None without a GPU or that build."""
     if not torch.cuda.is_available():
         return None
     from oracle import oracle as O
@@ -310,30 +310,45 @@ def reference_kernel_on_gpu(args):
            "bytes_per_row": D * 2 + 6 * D + 8, "gbs": moved / (ms / 1e3) / 1e9,
            "frac_of_measured_hbm": moved / (ms / 1e3) / 1e9 / peak,
            "note": "reference kernel v8 with its own launcher, same K and V fp16 rows"}
+    del rows
+    eng = engine_compat_timing(args, k, v)
+    eng["speedup_vs_reference_kernel"] = ms / eng["ms_per_step"]
+    out["engine_compat_op_same_outputs"] = eng
+    del k, v
+    torch.cuda.empty_cache()
+    return out
 
-    # like for like: this engine's compat operator with the same five
-    # reference-layout outputs (compress + materialize), same rows
+
+def engine_compat_timing(args, k=None, v=None) -> dict:
+    """This engine's compat operator with the reference kernel's five
+    outputs (ops.ultra_fused_full_fusion: compress + materialize) on the
+    bench's K and V fp16 rows, outputs allocated per call like the
+    reference launcher."""
     from kudahitam import ops
-    dh, ch = d.cpu(), c.cpu()
+    from kudahitam.codebook import lloyd_max, rademacher
+    dev = torch.device("cuda", torch.cuda.current_device())
+    if k is None:
+        k, v = synth_kv(2, dev)
+    rows = [t.reshape(-1, D).contiguous() for t in (k, v)]
+    dh, ch = rademacher(D, 1), lloyd_max(1, D)
+    stream = torch.cuda.current_stream(dev)
 
-    def step_engine():
+    def step():
         for r in rows:
             ops.ultra_fused_full_fusion(r, dh, ch)
 
     for _ in range(3):
-        step_engine()
+        step()
     torch.cuda.synchronize()
-    ems = statistics.median(time_loop(step_engine, max(5, min(args.steps, 20)), stream))
-    out["engine_compat_op_same_outputs"] = {
-        "rows_per_s": n / (ems / 1e3), "ms_per_step": ems, "bytes_per_row": D * 2 + 6 * D + 8,
-        "gbs": moved / (ems / 1e3) / 1e9, "frac_of_measured_hbm": moved / (ems / 1e3) / 1e9 / peak,
-        "speedup_vs_reference_kernel": ms / ems,
-        "note": "ops.ultra_fused_full_fusion: the reference's five outputs (idx u8, norms, "
-                "k_mse f32, r_norms, signs i8) from compress + materialize, outputs "
-                "allocated per call like the reference launcher"}
-    del k, v, rows
-    torch.cuda.empty_cache()
-    return out
+    ms = statistics.median(time_loop(step, max(5, min(args.steps, 20)), stream))
+    n = 2 * rows[0].shape[0]
+    peak, _ = peaks()
+    moved = n * (D * 2 + 6 * D + 8)
+    return {"rows_per_s": n / (ms / 1e3), "ms_per_step": ms, "bytes_per_row": D * 2 + 6 * D + 8,
+            "gbs": moved / (ms / 1e3) / 1e9, "frac_of_measured_hbm": moved / (ms / 1e3) / 1e9 / peak,
+            "note": "ops.ultra_fused_full_fusion: the reference's five outputs (idx u8, norms, "
+                    "k_mse f32, r_norms, signs i8) from compress + materialize, outputs "
+                    "allocated per call like the reference launcher"}
 
 
 def workload_config(world: int) -> dict:
@@ -376,6 +391,10 @@ def run_engine(args, world, rank, local):
     if args.only == "fp32":
         if rank == 0:
             print(json.dumps({"fp32_1bit": fp32_1bit_bench(dev, args)}), flush=True)
+        return
+    if args.only == "compat":
+        if rank == 0:
+            print(json.dumps({"compat": engine_compat_timing(args)}), flush=True)
         return
     if args.only == "cfg5":
         c5 = cfg5_bench(dev, args, world, rank)
@@ -865,7 +884,7 @@ def main():
     ap.add_argument("--no-cfg5", action="store_true",
                     help="skip the 8-GPU workload line (K, V bf16 [64,16,131072,128])")
     ap.add_argument("--only", choices=["all", "compress", "decode", "layers", "fp32", "score",
-                                       "cfg5"], default="all",
+                                       "cfg5", "compat"], default="all",
                     help="run one part (small cases for profiler captures)")
     ap.add_argument("--seq", type=int, default=None,
                     help="override S of the compression workload (profiling only)")

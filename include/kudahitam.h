@@ -116,6 +116,8 @@ int kh_fwht_inplace(float* x, int64_t n_rows, int head_dim, void* stream);
  * output tensors: idx uint8[n,D], k_mse float[n,D], signs int8[n,D]
  * (KudaHitamCUDA.cu:105-111, :141-149, :189-194).  Any output may be NULL;
  * signs needs res_bits.  k_mse = norm * d (.) H(c[idx]) / sqrt(D).
+ * out_idx and out_signs must be 8-byte aligned (each lane stores 4 or 8 of
+ * a row's bytes at once), out_kmse 4-byte aligned.
  */
 int kh_materialize(const uint32_t* code_bits, const uint32_t* res_bits,
                    const float* norms, int64_t n_rows, int head_dim,

@@ -1138,10 +1138,14 @@ kh_status launch_decode_partial(const DecodeRequest& r, cudaStream_t stream) {
   int path = (env && strcmp(env, "v1") == 0) ? 1 : (env && strcmp(env, "v2") == 0) ? 2 : 3;
   if (r.cb.n_c == 4) path = 1;  // the 4-level codebook runs the direct kernel
   // v3 work split (see decode_v3_kernel): ranges of W (cache group, row)
-  // pairs, one CTA set of n_q CTAs each.  W balances the pairs over one
-  // wave of CTAs at two per SM, and is at least L / (n_splits - 1) so that
-  // no group spans more than n_splits ranges (its record slots); with one
-  // record per row, one range per group.
+  // pairs, one CTA set of n_q CTAs each.  W cuts the pairs into up to four
+  // waves of CTAs at two per SM (the hardware then hands a finished CTA's
+  // slot to the next range, so a slow SM costs at most a quarter wave; one
+  // wave of long CTAs measured 17 % slower per step on the 131072-row
+  // workload), but no range under 8192 pairs (a range pays the query
+  // transform and one table build per segment); and W is at least
+  // L / (n_splits - 1) so that no group spans more than n_splits ranges
+  // (its record slots).  With one record per row, one range per group.
   const int64_t L = r.seq_end - r.seq_begin;
   P.n_groups_kv = r.n_groups;
   int64_t n_cta = 0;
@@ -1153,8 +1157,9 @@ kh_status launch_decode_partial(const DecodeRequest& r, cudaStream_t stream) {
     n_cta = r.n_groups * r.n_q;
   } else {
     const int64_t total = r.n_groups * L;
-    const int64_t sets = std::max<int64_t>(1, 2 * (int64_t)sm_count() / r.n_q);
-    const int64_t w_bal = std::max<int64_t>(512, (total + sets - 1) / sets);
+    const int64_t slots = std::max<int64_t>(1, 2 * (int64_t)sm_count() / r.n_q);
+    const int64_t sets = std::max<int64_t>(1, std::min<int64_t>(4 * slots, (total + 8191) / 8192));
+    const int64_t w_bal = (total + sets - 1) / sets;
     const int64_t w_min = (L + r.n_splits - 2) / (r.n_splits - 1);
     P.W = std::max(w_bal, w_min);
     n_cta = (total + P.W - 1) / P.W * r.n_q;

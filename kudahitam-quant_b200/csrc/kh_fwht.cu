@@ -88,9 +88,27 @@ __global__ void __launch_bounds__(256)
         r[j] = idx[j] < 2 ? (idx[j] ? c1 : c0) : (idx[j] == 2 ? c2 : c3);
       }
     }
+    // idx and signs: lane l writes elements [E l, E (l + 1)), E = D / 32,
+    // as one 4- or 8-byte store (the kmse below keeps the butterfly's
+    // element-per-lane order, one coalesced 128-byte store per j)
+    constexpr int E = D / 32;
     if (P.idx) {
+      uint32_t w[E / 4];
+      if (NC == 2) {
+        const uint32_t bits = (__ldg(cw + (E * lane >> 5)) >> ((E * lane) & 31)) & ((1u << E) - 1);
 #pragma unroll
-      for (int j = 0; j < J; ++j) P.idx[row * D + lane + 32 * j] = (uint8_t)idx[j];
+        for (int h = 0; h < E / 4; ++h)  // 4 bits -> 4 bytes of 0 / 1 (no carries)
+          w[h] = (((bits >> (4 * h)) & 0xFu) * 0x00204081u) & 0x01010101u;
+      } else {
+        const uint32_t f = __ldg(cw + (E * lane >> 4)) >> (2 * ((E * lane) & 15));
+#pragma unroll
+        for (int h = 0; h < E / 4; ++h)
+          w[h] = ((f >> (8 * h)) & 3u) | (((f >> (8 * h + 2)) & 3u) << 8) |
+                 (((f >> (8 * h + 4)) & 3u) << 16) | (((f >> (8 * h + 6)) & 3u) << 24);
+      }
+      uint8_t* dst = P.idx + row * D + E * lane;
+      if constexpr (E == 4) *reinterpret_cast<uint32_t*>(dst) = w[0];
+      else *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
     }
     if (P.kmse) {
 #pragma unroll
@@ -119,11 +137,16 @@ __global__ void __launch_bounds__(256)
     }
     if (P.signs) {
       const uint32_t* rw = P.res + row * (D / 32);
+      const uint32_t bits = (__ldg(rw + (E * lane >> 5)) >> ((E * lane) & 31)) & ((1u << E) - 1);
+      uint32_t w[E / 4];
 #pragma unroll
-      for (int j = 0; j < J; ++j) {
-        const int e = lane + 32 * j;
-        P.signs[row * D + e] = ((__ldg(rw + (e >> 5)) >> (e & 31)) & 1u) ? (int8_t)1 : (int8_t)-1;
+      for (int h = 0; h < E / 4; ++h) {
+        const uint32_t e = (((bits >> (4 * h)) & 0xFu) * 0x00204081u) & 0x01010101u;
+        w[h] = 0xFFFFFFFFu ^ (e * 0xFEu);  // per byte: bit 1 -> +1, bit 0 -> -1 (0xFF)
       }
+      int8_t* dst = P.signs + row * D + E * lane;
+      if constexpr (E == 4) *reinterpret_cast<uint32_t*>(dst) = w[0];
+      else *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
     }
   }
 }

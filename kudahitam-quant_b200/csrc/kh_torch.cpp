@@ -65,22 +65,26 @@ int dtype_code(at::ScalarType s) {
   return -1;
 }
 
-// [N, D] rows with unit inner stride and a 16-byte row pitch: x itself when
-// its layout allows, else an aligned contiguous copy.  Returns the pitch in
-// elements.
-std::pair<Tensor, int64_t> rows_of(const Tensor& x) {
+// The rows of x as the C ABI reads them: N rows of D elements with unit
+// inner stride and a 16-byte row pitch.  x itself when its layout allows
+// (no tensor is created on this common path), else an aligned contiguous
+// copy kept alive in `keep`.
+struct Rows {
+  const void* ptr;
+  int64_t n, pitch;
+  Tensor keep;
+};
+Rows rows_of(const Tensor& x) {
   const int64_t D = x.size(-1);
   const int64_t elt = x.element_size();
-  const auto aligned = [](const Tensor& t) {
-    return (reinterpret_cast<uintptr_t>(t.data_ptr()) & 15) == 0;
-  };
-  if (x.is_contiguous() && aligned(x) && (D * elt) % 16 == 0)
-    return {x.view({-1, D}), D};
+  const auto aligned = [](const void* p) { return (reinterpret_cast<uintptr_t>(p) & 15) == 0; };
+  if (x.is_contiguous() && aligned(x.data_ptr()) && (D * elt) % 16 == 0)
+    return {x.data_ptr(), D ? x.numel() / D : 0, D, Tensor()};
   Tensor r = x.reshape({-1, D});
-  const bool ok = r.stride(-1) == 1 && aligned(r) &&
+  const bool ok = r.stride(-1) == 1 && aligned(r.data_ptr()) &&
                   (r.size(0) <= 1 || (r.stride(0) * elt) % 16 == 0);
   if (!ok) r = at::empty(r.sizes(), r.options()).copy_(r);  // fresh: 256-byte aligned
-  return {r, r.size(0) > 1 ? r.stride(0) : D};
+  return {r.data_ptr(), r.size(0), r.size(0) > 1 ? r.stride(0) : D, r};
 }
 
 int64_t code_words(int64_t D, int bits) { return bits == 1 ? D / 32 : D / 16; }
@@ -121,8 +125,8 @@ void compress_out(const Tensor& x, const Tensor& d, const Tensor& c, bool residu
   const int dt = dtype_code(x.scalar_type());
   const float* ch = host_c(c);
   const float* dh = host_f32(d, D, "d");
-  auto [r, pitch] = rows_of(x);
-  const int64_t n = r.size(0);
+  const Rows r = rows_of(x);
+  const int64_t n = r.n;
   TORCH_CHECK(code.numel() == n * code_words(D, bits_of(c)) && norms.numel() == n,
               "output buffers do not match ", n, " rows");
   check_buf(code, x.device(), "code");
@@ -134,7 +138,7 @@ void compress_out(const Tensor& x, const Tensor& d, const Tensor& c, bool residu
                     res->numel() == n * (D / 32) && rnorms->numel() == n,
                 "2-bit mode needs res [N, D/32] and rnorms [N]");
   c10::cuda::CUDAGuard guard(x.device());
-  check(kh_compress(r.data_ptr(), dt, n, (int)D, pitch, dh, ch, (int)c.numel(), residual ? 1 : 0,
+  check(kh_compress(r.ptr, dt, n, (int)D, r.pitch, dh, ch, (int)c.numel(), residual ? 1 : 0,
                     u32(code), residual ? u32(*res) : nullptr, norms.data_ptr<float>(),
                     residual ? rnorms->data_ptr<float>() : nullptr, stream_of(x)),
         "kh_compress");
@@ -174,7 +178,7 @@ void compress_many_out(at::TensorList xs, const Tensor& d, const Tensor& c, bool
   const float* ch = host_c(c);
   const float* dh = host_f32(d, D, "d");
   const int bits = bits_of(c);
-  std::vector<Tensor> keep(n);  // row views (and copies) alive for the call
+  std::vector<Tensor> keep(n);  // aligned copies (if any) alive for the call
   std::vector<const void*> xp(n);
   std::vector<int64_t> rows(n), pitch(n);
   std::vector<uint32_t*> cp(n), rp(n, nullptr);
@@ -182,11 +186,11 @@ void compress_many_out(at::TensorList xs, const Tensor& d, const Tensor& c, bool
   for (size_t i = 0; i < n; ++i) {
     TORCH_CHECK(xs[i].device() == dev && xs[i].scalar_type() == st && xs[i].size(-1) == D,
                 "compress_many needs tensors of one device, dtype and head_dim");
-    auto [r, p] = rows_of(xs[i]);
-    keep[i] = r;
-    xp[i] = r.data_ptr();
-    rows[i] = r.size(0);
-    pitch[i] = p;
+    const Rows r = rows_of(xs[i]);
+    keep[i] = r.keep;
+    xp[i] = r.ptr;
+    rows[i] = r.n;
+    pitch[i] = r.pitch;
     TORCH_CHECK(code[i].numel() == rows[i] * code_words(D, bits) && norms[i].numel() == rows[i],
                 "output buffers of tensor ", i, " do not match its rows");
     check_buf(code[i], dev, "code");

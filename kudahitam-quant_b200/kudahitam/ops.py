@@ -373,25 +373,27 @@ def default_splits(n_groups: int, seq_len: int, device, n_q: int = 1) -> int:
     n_groups query rows (n_q per cache group) of seq_len cached rows.
 
     The decode kernel cuts the call's (cache group, row) pairs into equal
-    ranges, one wave of CTAs at two per SM, whatever the group count; a
-    group spanning several ranges gets one record per range.  This rule
-    returns how many records the longest group can need at that range
-    length (2 when the ranges are at least a group long), so the kernel
-    runs balanced.  (The earlier one-CTA-per-(row, split) grid ran 1.73
-    waves for 512 query rows on 148 SMs.)"""
+    ranges, up to four waves of CTAs at two per SM and no range under 8192
+    pairs, whatever the group count; a group spanning several ranges gets
+    one record per range.  This rule returns how many records the longest
+    group can need at that range length, so the kernel runs balanced.  (The
+    earlier one-CTA-per-(row, split) grid ran 1.73 waves for 512 query rows
+    on 148 SMs.)"""
     sms = torch.cuda.get_device_properties(device).multi_processor_count
     return splits_for(n_groups, seq_len, sms, n_q)
 
 
 def splits_for(n_rows: int, seq_len: int, n_sms: int, n_q: int = 1) -> int:
     """The rule of ``default_splits`` for a GPU with n_sms SMs; mirrors the
-    decode launcher's range length (kh_decode.cu: one wave of CTA sets of
-    n_q CTAs at two CTAs per SM, at least 512 rows per range)."""
+    decode launcher's range length (kh_decode.cu: up to four waves of CTA
+    sets of n_q CTAs at two CTAs per SM, at least 8192 pairs per range)."""
     if seq_len <= 0 or n_rows <= 0:
         return 1
     groups = max(1, n_rows // max(n_q, 1))
-    sets = max(1, 2 * n_sms // max(n_q, 1))
-    w_bal = max(512, -(-groups * seq_len // sets))
+    total = groups * seq_len
+    slots = max(1, 2 * n_sms // max(n_q, 1))
+    sets = max(1, min(4 * slots, -(-total // 8192)))
+    w_bal = -(-total // sets)
     return int(min(1024, -(-seq_len // w_bal) + 1))
 
 

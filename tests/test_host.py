@@ -66,19 +66,20 @@ def test_lloyd_max_other_dims_sorted_symmetric():
 
 
 def test_decode_split_rule():
-    """Records per query row on a 148-SM GPU: the kernel balances (group,
-    row) pairs over one wave of 296 CTAs; a group longer than a range needs
-    one record per range it touches, plus one."""
+    """Records per query row on a 148-SM GPU: the kernel cuts (group, row)
+    pairs into ranges over up to four waves of 296 CTAs, none under 8192
+    pairs; a group gets one record per range it touches."""
     from kudahitam.ops import splits_for
-    assert [splits_for(512, s, 148) for s in (5000, 10000, 20000, 40000)] == [2, 2, 2, 2]
-    assert splits_for(32, 40000, 148) == 11      # one sequence of 32 heads: ranges < a group
-    assert splits_for(1024, 131072, 148) == 2
+    assert [splits_for(512, s, 148) for s in (5000, 10000, 20000, 40000)] == [2, 3, 4, 4]
+    assert splits_for(32, 40000, 148) == 6       # one sequence of 32 heads
+    assert splits_for(1024, 131072, 148) == 3
     assert splits_for(512, 100, 148) == 2 and splits_for(0, 0, 148) == 1
-    assert splits_for(1, 10 ** 9, 148) == 297
-    assert splits_for(64, 4096, 148, n_q=8) == 6  # 8 groups, 37 sets of 8 CTAs
-    # the rule's range is never shorter than L / (n - 1): a group spans at most n ranges
+    assert splits_for(1, 10 ** 9, 148) == 1024   # capped
+    assert splits_for(64, 4096, 148, n_q=8) == 2  # 8 groups: 4 ranges of 8192
+    # the launcher's range is never shorter than L / (n - 1): a group spans at most n ranges
     for R, L, nq in ((512, 40000, 1), (32, 40000, 1), (7, 12345, 1), (64, 9000, 4)):
         n = splits_for(R, L, 148, nq)
-        sets = max(1, 2 * 148 // nq)
-        w = max(512, -(-(R // nq) * L // sets))
+        total = (R // nq) * L
+        sets = max(1, min(4 * (2 * 148 // nq), -(-total // 8192)))
+        w = -(-total // sets)
         assert -(-L // w) + 1 <= n
