@@ -699,6 +699,24 @@ def decode_bench(dev, args, world: int = 1, rank: int = 0) -> dict:
     dec = decode_timing(dev, args, world, q.float(), pk, pv, dk, dv, c, S_loc, DEC_S)
     dec["roofline"]["traffic"] = NCU_DECODE_TRAFFIC_BYTES_PER_ROW * G * DEC_S / world
     dec["roofline"]["kernel"] = "decode_v3_kernel<128> + decode_combine_kernel<128>"
+    if world == 1:
+        # the same decode over caches of the 4-level (bits=2) codebook: 2-bit
+        # code plane, 56 B per cached row and tensor
+        del pk, pv
+        c2 = lloyd_max(2, DEC_D)
+        g2 = torch.Generator(device=dev).manual_seed(5)
+        pk = ops.empty_packed((G, S_loc, DEC_D), 2, True, dev)
+        pv = ops.empty_packed((G, S_loc, DEC_D), 2, True, dev)
+        for p, dd in ((pk, dk), (pv, dv)):
+            for i in range(0, G, 64):
+                x = torch.randn(64, S_loc, DEC_D, device=dev, generator=g2).to(torch.bfloat16)
+                ops.compress(x, dd, c2, out=p.rows(i * S_loc, (i + 64) * S_loc))
+        d2 = decode_timing(dev, args, world, q.float(), pk, pv, dk, dv, c2, S_loc, DEC_S,
+                           bytes_per_row=2 * (DEC_D // 16 * 4 + DEC_D // 8 + 8))
+        d2["roofline"]["kernel"] = "decode_b2_kernel + decode_combine_kernel<128>"
+        dec["bits2_codebook"] = {k: d2[k] for k in ("us_per_step", "n_splits",
+                                                    "phase_us_max_over_ranks", "roofline")}
+        del pk, pv
     return {"config": "q bf16 [32,16,128]; K and V 2-bit-mode packed, S=40000"
                       + (f", sequence-sharded over {world} GPUs + one NCCL all-gather"
                          if world > 1 else ""),
@@ -816,7 +834,8 @@ def cfg5_bench(dev, args, world: int, rank: int) -> dict:
     return out
 
 
-def decode_timing(dev, args, world, q, pk, pv, dk, dv, c, S_loc, S_total) -> dict:
+def decode_timing(dev, args, world, q, pk, pv, dk, dv, c, S_loc, S_total,
+                  bytes_per_row: int = None) -> dict:
     """Times decode attention (q [R, D] against R groups of S_loc cached rows
     on this rank; S_total over all ranks): whole steps, and each phase on its
     own (partial kernel, local merge, NCCL all-gather, combine), every time
@@ -860,12 +879,38 @@ def decode_timing(dev, args, world, q, pk, pv, dk, dv, c, S_loc, S_total) -> dic
     for name, fn in phases.items():
         barrier(world)
         phase_us[name] = max_over_ranks(statistics.median(time_loop(fn, n, stream)), world) * 1e3
-    bytes_step = R * S_total * 2 * (2 * D // 8 + 8)  # whole job: K and V, 2 planes + 2 norms
+    peer = None
+    if world > 1:
+        # the same step with the records exchanged inside the merge kernel
+        # over peer (symmetric) memory instead of the NCCL all-gather
+        ex = khdist.PeerRecordExchange(R, D, device=dev)
+
+        def step_peer():
+            return khdist.decode_attention_seq_sharded(q, pk, pv, dk, dv, c, sm, n_splits,
+                                                       partials=buf, exchange=ex)
+
+        for _ in range(3):
+            step_peer()
+        torch.cuda.synchronize()
+        khdist.check_peer_timeout(dev)
+        barrier(world)
+        pms = max_over_ranks(statistics.median(time_loop(step_peer, n, stream)), world)
+        torch.cuda.synchronize()
+        khdist.check_peer_timeout(dev)
+        barrier(world)
+        del ex
+        peer = {"us_per_step": pms * 1e3,
+                "note": "kh_decode_merge_to_peers + kh_decode_combine_from_peers (plain "
+                        "stores to every rank's symmetric buffer, epoch flags) in place of "
+                        "merge + NCCL all-gather + combine"}
+    if bytes_per_row is None:
+        bytes_per_row = 2 * (2 * D // 8 + 8)  # K and V: 2 one-bit planes + 2 norms each
+    bytes_step = R * S_total * bytes_per_row  # whole job
     peak, _ = peaks()
     per_gpu = bytes_step / world / (ms / 1e3) / 1e9
     return {"us_per_step": ms * 1e3, "n_splits": n_splits, "rows_per_group_per_gpu": S_loc,
             "scaling": "strong" if world > 1 else None,
-            "phase_us_max_over_ranks": phase_us,
+            "phase_us_max_over_ranks": phase_us, "peer_exchange": peer,
             "gbs": bytes_step / (ms / 1e3) / 1e9,
             "frac_of_measured_hbm_per_gpu": per_gpu / peak,
             "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": peak, "unit": "GB/s",

@@ -1114,6 +1114,373 @@ __global__ void __launch_bounds__(256, 2)
   }
 }
 
+// ---------------------------------------------------------------------------
+// Decode for the 4-level (bits=2) codebook at D = 128: the v3 scheme (same
+// work ranges, segments, logits, fixed-point V histograms) with a 2-bit code
+// plane of 32 bytes per row (4 elements per byte, element 4p + k at bits 2k
+// of byte p).
+//   K table  entries 0..31 of each 64-word row: T2[v][p] =
+//            sum_{k<4} q~[4p + k] c[(v >> 2k) & 3] (one copy; lane l looks up
+//            position (k + l) mod 32 at step k); entries 32..63: the 1-bit
+//            residual table (16 positions, two copies).
+//   score    norm * sum_p T2 + r_norm / sqrt(D) (2 M_res - Q).
+//   V        the code plane's histogram H2[v][p] takes w = p_s |v_s| / sqrt(D)
+//            per row (entries 0..31), the residual plane's as in v3
+//            (entries 32..63, two copies); the fold gives, per element,
+//            the four sums S_val = sum over byte values whose field is val,
+//            and acc_e = sum_val c[val] S_val + the residual plane's share.
+// Logits live in their own array; after phase 2 it holds the fold partials.
+struct B2Cfg {
+  static constexpr int kD = 128;
+  static constexpr int kPC = 32, kWC = 8;  // code plane: byte positions, words
+  static constexpr int kPR = 16, kWR = 4;  // residual plane
+  static constexpr int kThreads = 256;
+  static constexpr int kSeg = 6144;        // rows per segment (24 KB of logits)
+  static constexpr int kRing = 3;          // batches (one row each) in the register ring
+  static constexpr int kTabWords = 256 * 64;
+  static constexpr int kFoldCode = 8 * 32 * 16;  // [bin group][position][field][value]
+  static constexpr int kFoldRes = 8 * 32 * 8;    // [bin group][slot][bit]
+  static_assert(kFoldCode + kFoldRes <= kSeg, "fold partials overlay the logits");
+  // tab [256][64] | logits / fold [kSeg] | q~ [128] | reduction scratch [64]
+  static constexpr int kSmem = (kTabWords + kSeg + kD + 64) * 4;
+};
+
+struct RowB2 {
+  uint32_t c[B2Cfg::kWC], r[B2Cfg::kWR];
+  float n, rn;
+};
+
+__global__ void __launch_bounds__(256, 2)
+    decode_b2_kernel(const __grid_constant__ DecodeParams P) {
+  grid_dependency_wait();  // q and the cache may come from the previous kernel
+  using C = B2Cfg;
+  constexpr int D = C::kD;
+  constexpr int NT = C::kThreads;
+  constexpr float kLog2e = 1.4426950408889634f;
+  constexpr float kLn2 = 0.6931471805599453f;
+  extern __shared__ __align__(16) unsigned char smem_b2[];
+  unsigned char* tabb = smem_b2;
+  float* tab = reinterpret_cast<float*>(smem_b2);
+  float* lg = tab + C::kTabWords;                       // [kSeg] logits, then fold partials
+  int* cf = reinterpret_cast<int*>(lg);                 // [8][32][16]
+  int* rf = cf + C::kFoldCode;                          // [8][32][8]
+  float* qt = lg + C::kSeg;                             // [D]
+  float* red = qt + D;                                  // [64]
+
+  const int t = threadIdx.x;
+  const int lane = t & 31;
+  const float inv_sqrt_d = 1.0f / sqrtf((float)D);
+  const float qjl = 0.7978845608028654f / (float)D;  // sqrt(2/pi) / D
+  const float lscale = P.sm_scale * kLog2e;
+  const float wb = 2.f * qjl;  // V weight = p (|v| / sqrt(D) + wb r_norm)
+  const float cv0 = P.cb[0], cv1 = P.cb[1], cv2 = P.cb[2], cv3 = P.cb[3];
+
+  // lane constants: code plane rotated by lane bytes (of 32), slots 0..31;
+  // residual plane rotated by lane mod 16, slots 32 + pos + 16 (lane / 16)
+  const int wrc = lane >> 2, bsc = 8 * (lane & 3);
+  uint32_t slotc[C::kPC / 4];
+  static_for<C::kPC / 4>([&](auto mc) {
+    constexpr int m = decltype(mc)::value;
+    uint32_t v = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j) v |= (4u * (uint32_t)((4 * m + j + lane) % C::kPC)) << (8 * j);
+    slotc[m] = v;
+  });
+  const int rr = lane % C::kPR;
+  const int wrr = rr >> 2, bsr = 8 * (rr & 3);
+  uint32_t slotr[C::kPR / 4];
+  static_for<C::kPR / 4>([&](auto mc) {
+    constexpr int m = decltype(mc)::value;
+    uint32_t v = 0;
+#pragma unroll
+    for (int j = 0; j < 4; ++j)
+      v |= (4u * (uint32_t)(((4 * m + j + lane) % C::kPR) + C::kPR * (lane / C::kPR))) << (8 * j);
+    slotr[m] = v;
+  });
+  const unsigned char* tabr = tabb + 128;  // entries 32..63 of each table row
+
+  // work split: as decode_v3_kernel
+  const int64_t L = P.seq_end - P.seq_begin;
+  if (P.W == 0) {
+    if (t == 0)
+      for (int p = 0; p < P.n_splits; ++p) {
+        float* e = P.partials +
+                   ((int64_t)blockIdx.x * P.part_stride + P.part_offset + p) * (D + 2);
+        e[0] = -INFINITY;
+        e[1] = 0.f;
+      }
+    return;
+  }
+  const int jq = (int)(blockIdx.x % (unsigned)P.n_q);
+  const int64_t set = blockIdx.x / (unsigned)P.n_q;
+  const int64_t wbeg = set * P.W;
+  const int64_t wend = min(wbeg + P.W, P.n_groups_kv * L);
+  const uint64_t pol_once = l2_policy_evict_first(), pol_again = l2_policy_evict_last();
+  for (int64_t gk = wbeg / L; gk * L < wend; ++gk) {
+    const int64_t g = gk * P.n_q + jq;
+    const int64_t s0 = P.seq_begin + max(wbeg - gk * L, (int64_t)0);
+    const int64_t s1 = P.seq_begin + min(wend - gk * L, L);
+    const int64_t rpart = set - gk * L / P.W;
+
+    for (int i = t; i < D; i += NT) qt[i] = P.q[g * D + i] * P.dk[i];
+    __syncthreads();
+    for (int h = 1; h < D; h <<= 1) {
+      for (int b = t; b < D / 2; b += NT) {
+        const int lo = (b / h) * 2 * h + (b % h);
+        const float a = qt[lo], c = qt[lo + h];
+        qt[lo] = a + c;
+        qt[lo + h] = a - c;
+      }
+      __syncthreads();
+    }
+    float qpart = 0.f;
+    for (int i = t; i < D; i += NT) {
+      qt[i] *= inv_sqrt_d;
+      qpart += qt[i];
+    }
+    const float Q = block_sum<NT>(qpart, red);  // (its barriers also publish qt)
+
+    float m_run = -INFINITY, l_run = 0.f, c_run = 0.f, acc = 0.f;
+    for (int64_t c0 = s0; c0 < s1; c0 += C::kSeg) {
+      const int n = (int)min((int64_t)C::kSeg, s1 - c0);
+      const int64_t row0 = gk * P.seq_len + c0;
+      const int nb = (n + NT - 1) / NT;  // batches of one row per thread
+
+      // K tables: T2 (thread (position t mod 32, group t / 32) fills the byte
+      // values t / 32 + 8 kk), then the residual table in entries 32..63
+      {
+        const int p = t & 31, w = t >> 5;
+        const float q0 = qt[4 * p], q1 = qt[4 * p + 1], q2 = qt[4 * p + 2], q3 = qt[4 * p + 3];
+        auto cvv = [&](int i) {  // c[i] without a local array
+          return i < 2 ? (i ? cv1 : cv0) : (i == 2 ? cv2 : cv3);
+        };
+        float lo[2];
+#pragma unroll
+        for (int h = 0; h < 2; ++h) {
+          const int v = w + 8 * h;
+          lo[h] = q0 * cvv(v & 3) + q1 * cvv((v >> 2) & 3);
+        }
+        static_for<32>([&](auto kc) {
+          constexpr int kk = decltype(kc)::value, hv = kk >> 1;
+          const float hi = q2 * cvv(hv & 3) + q3 * cvv((hv >> 2) & 3);
+          tab[(w + 8 * kk) * 64 + p] = lo[kk & 1] + hi;
+        });
+      }
+      build_byte_table<D>(tab + 32, qt, t);
+      __syncthreads();
+
+      // ---------------- phase 1: logits and online sums of p and V weights
+      float mt = -INFINITY;
+      float2 sums = make_float2(0.f, 0.f);
+      {
+        struct RowK2 {
+          RowB2 k;
+          float vn, vrn;
+        };
+        RowK2 a[C::kRing];
+        auto load = [&](RowK2& dst, int bi) {
+          const int ii = t + bi * NT;
+          const int64_t row = row0 + (ii < n ? ii : 0);
+          load_plane_policy<256>(P.k_code + row * C::kWC, wrc, pol_once, dst.k.c);  // 32-byte plane
+          load_plane_policy<128>(P.k_res + row * C::kWR, wrr, pol_once, dst.k.r);
+          dst.k.n = ldg_policy(P.k_norms + row, pol_once);
+          dst.k.rn = ldg_policy(P.k_rnorms + row, pol_once);
+          dst.vn = ldg_policy(P.v_norms + row, pol_again);
+          dst.vrn = ldg_policy(P.v_rnorms + row, pol_again);
+        };
+        auto score = [&](const RowK2& src, int bi) {
+          uint32_t rc[C::kWC], rs[C::kWR];
+          rotate_plane<256>(src.k.c, wrc, bsc, rc);
+          rotate_plane<128>(src.k.r, wrr, bsr, rs);
+          float2 mc = make_float2(0.f, 0.f), mr = make_float2(0.f, 0.f);
+          static_for<C::kPC>([&](auto kc) {
+            constexpr int k = decltype(kc)::value;
+            const float x = *reinterpret_cast<const float*>(
+                tabb + tab_addr<k & 3>(rc[k >> 2], slotc[k >> 2]));
+            if constexpr (k & 1) mc.y += x; else mc.x += x;
+          });
+          static_for<C::kPR>([&](auto kc) {
+            constexpr int k = decltype(kc)::value;
+            const float x = *reinterpret_cast<const float*>(
+                tabr + tab_addr<k & 3>(rs[k >> 2], slotr[k >> 2]));
+            if constexpr (k & 1) mr.y += x; else mr.x += x;
+          });
+          const float sc = src.k.n * (mc.x + mc.y) +
+                           inv_sqrt_d * (2.f * (mr.x + mr.y) - Q) * src.k.rn;
+          const int ii = t + bi * NT;
+          const float l2 = ii < n ? sc * lscale : -INFINITY;
+          if (ii < n) lg[ii] = l2;
+          if (l2 > -INFINITY) {
+            const float mb = fmaxf(mt, l2);
+            const float scl = exp2f(mt - mb);  // 0 while mt is -inf
+            const float p = exp2f(l2 - mb);
+            sums.x = sums.x * scl + p;
+            sums.y = sums.y * scl + p * (src.vn * inv_sqrt_d + src.vrn * wb);
+            mt = mb;
+          }
+        };
+        static_for<C::kRing - 1>([&](auto jc) { load(a[decltype(jc)::value], decltype(jc)::value); });
+        for (int bi = 0; bi < nb; bi += C::kRing) {
+          static_for<C::kRing>([&](auto jc) {
+            constexpr int j = decltype(jc)::value;
+            if (bi + j < nb) {
+              load(a[(j + C::kRing - 1) % C::kRing], bi + j + C::kRing - 1);
+              score(a[j], bi + j);
+            }
+          });
+        }
+      }
+      RowB2 va[C::kRing];
+      auto load_v = [&](RowB2& dst, int bi) {
+        const int ii = t + bi * NT;
+        const int64_t row = row0 + (ii < n ? ii : 0);
+        load_plane_policy<256>(P.v_code + row * C::kWC, wrc, pol_once, dst.c);
+        load_plane_policy<128>(P.v_res + row * C::kWR, wrr, pol_once, dst.r);
+        dst.n = ldg_policy(P.v_norms + row, pol_once);
+        dst.rn = ldg_policy(P.v_rnorms + row, pol_once);
+      };
+      static_for<C::kRing - 1>([&](auto jc) { load_v(va[decltype(jc)::value], decltype(jc)::value); });
+      const float m_seg = block_max<NT>(mt, red);  // also: phase-1 table reads done
+      const float m_new = fmaxf(m_run, m_seg);
+      const float alpha = exp2f(m_run - m_new);  // 0 on the first segment
+      m_run = m_new;
+      {
+        int4* z = reinterpret_cast<int4*>(tabb);
+        for (int e = t; e < C::kTabWords / 4; e += NT) z[e] = make_int4(0, 0, 0, 0);
+      }
+      {
+        const float r = mt > -INFINITY ? exp2f(mt - m_new) : 0.f;
+        sums.x *= r;
+        sums.y *= r;
+      }
+      const float2 tot = block_sum2<NT>(sums, red);  // barriers also order the zeroing
+      const float l_c = tot.x;
+      const float scale_inv = tot.y > 0.f ? 1073741824.0f / tot.y : 0.f;
+      const float scale = tot.y / 1073741824.0f;
+
+      // ---------------- phase 2: scatter V bytes with fixed-point weights
+      float csum = 0.f;  // the residual plane's constant term, in quanta
+      const float k1 = inv_sqrt_d * scale_inv, k2 = wb * scale_inv;
+      {
+        auto scatter = [&](const RowB2& src, int bi) {
+          const int ii = t + bi * NT;
+          const bool ok = ii < n;
+          const float p = ok ? exp2f(lg[ok ? ii : 0] - m_new) : 0.f;
+          const int fx = __float2int_rn(p * src.n * k1);
+          const int fy = __float2int_rn(p * src.rn * k2);
+          csum += -0.5f * (float)fy;
+          uint32_t rc[C::kWC], rs[C::kWR];
+          rotate_plane<256>(src.c, wrc, bsc, rc);
+          rotate_plane<128>(src.r, wrr, bsr, rs);
+          static_for<C::kPC>([&](auto kc) {
+            constexpr int k = decltype(kc)::value;
+            atomicAdd(reinterpret_cast<int*>(tabb + tab_addr<k & 3>(rc[k >> 2], slotc[k >> 2])),
+                      fx);
+          });
+          static_for<C::kPR>([&](auto kc) {
+            constexpr int k = decltype(kc)::value;
+            atomicAdd(reinterpret_cast<int*>(const_cast<unsigned char*>(tabr) +
+                                             tab_addr<k & 3>(rs[k >> 2], slotr[k >> 2])),
+                      fy);
+          });
+        };
+        for (int bi = 0; bi < nb; bi += C::kRing) {
+          static_for<C::kRing>([&](auto jc) {
+            constexpr int j = decltype(jc)::value;
+            if (bi + j < nb) {
+              load_v(va[(j + C::kRing - 1) % C::kRing], bi + j + C::kRing - 1);
+              scatter(va[j], bi + j);
+            }
+          });
+        }
+      }
+      const float c_c = block_sum<NT>(csum, red) * scale;  // also fences the histograms
+
+      // ---------------- fold (the logits are no longer needed: partials
+      // overlay them)
+      {
+        const int* hi = reinterpret_cast<const int*>(tabb);
+        const int slot = t & 31, w = t >> 5;
+        // code plane: position slot, byte values 32 w + j
+        int s0[4] = {0, 0, 0, 0}, s1[4] = {0, 0, 0, 0}, lo16 = 0, hi16 = 0;
+        static_for<32>([&](auto jc) {
+          constexpr int j = decltype(jc)::value;
+          const int h = hi[(32 * w + j) * 64 + slot];
+          s0[j & 3] += h;
+          s1[(j >> 2) & 3] += h;
+          if constexpr (j < 16) lo16 += h; else hi16 += h;
+        });
+        const int T = lo16 + hi16;
+        int4* o = reinterpret_cast<int4*>(cf + (w * 32 + slot) * 16);
+        o[0] = make_int4(s0[0], s0[1], s0[2], s0[3]);  // field 0 (bits 0-1)
+        o[1] = make_int4(s1[0], s1[1], s1[2], s1[3]);  // field 1 (bits 2-3)
+        const int v2 = 2 * (w & 1);                    // field 2: bit 4 of j, bit 5 of v
+        o[2] = make_int4(v2 == 0 ? lo16 : 0, v2 == 0 ? hi16 : 0, v2 == 2 ? lo16 : 0,
+                         v2 == 2 ? hi16 : 0);
+        const int v3 = w >> 1;                         // field 3: bits 6-7 of v
+        o[3] = make_int4(v3 == 0 ? T : 0, v3 == 1 ? T : 0, v3 == 2 ? T : 0, v3 == 3 ? T : 0);
+        // residual plane: slot (position slot mod 16, copy slot / 16), subset
+        // sums per bit of the byte value
+        int sb[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+        int tt = 0;
+        static_for<32>([&](auto jc) {
+          constexpr int j = decltype(jc)::value;
+          const int h = hi[(32 * w + j) * 64 + 32 + slot];
+          tt += h;
+          if (j & 1) sb[0] += h;
+          if (j & 2) sb[1] += h;
+          if (j & 4) sb[2] += h;
+          if (j & 8) sb[3] += h;
+          if (j & 16) sb[4] += h;
+        });
+        sb[5] = (w & 1) ? tt : 0;
+        sb[6] = (w & 2) ? tt : 0;
+        sb[7] = (w & 4) ? tt : 0;
+        int4* rp = reinterpret_cast<int4*>(rf + (w * 32 + slot) * 8);
+        rp[0] = make_int4(sb[0], sb[1], sb[2], sb[3]);
+        rp[1] = make_int4(sb[4], sb[5], sb[6], sb[7]);
+      }
+      __syncthreads();
+      if (t < D) {
+        const int p = t >> 2, k = t & 3;
+        int sv[4] = {0, 0, 0, 0};
+#pragma unroll
+        for (int w = 0; w < 8; ++w)
+#pragma unroll
+          for (int v = 0; v < 4; ++v) sv[v] += cf[(w * 32 + p) * 16 + 4 * k + v];
+        float a = cv0 * (float)sv[0] + cv1 * (float)sv[1] + cv2 * (float)sv[2] +
+                  cv3 * (float)sv[3];
+        const int pos = t >> 3, b = t & 7;
+        int sr = 0;  // one plane: a subset sum of one histogram, < 2^31
+#pragma unroll
+        for (int w = 0; w < 8; ++w) sr += rf[(w * 32 + pos) * 8 + b] + rf[(w * 32 + 16 + pos) * 8 + b];
+        a += (float)sr;
+        acc = acc * alpha + a * scale;
+      }
+      l_run = l_run * alpha + l_c;
+      c_run = c_run * alpha + c_c;
+      __syncthreads();  // fold reads done before the next segment's table and logits
+    }
+
+    if (rpart < P.n_splits) {
+      float* rec = P.partials + (g * P.part_stride + P.part_offset + rpart) * (D + 2);
+      if (t < D) rec[2 + t] = c_run + acc;
+      if (t == 0) {
+        rec[0] = m_run * kLn2;  // natural-log units for the combine step
+        rec[1] = l_run;
+      }
+    }
+    if (s1 == P.seq_end && t == 0) {
+      for (int64_t p = rpart + 1; p < P.n_splits; ++p) {
+        float* e = P.partials + (g * P.part_stride + P.part_offset + p) * (D + 2);
+        e[0] = -INFINITY;
+        e[1] = 0.f;
+      }
+    }
+    __syncthreads();
+  }
+}
+
 }  // namespace
 
 kh_status launch_decode_partial(const DecodeRequest& r, cudaStream_t stream) {
@@ -1136,10 +1503,11 @@ kh_status launch_decode_partial(const DecodeRequest& r, cudaStream_t stream) {
   const dim3 grid((unsigned)r.n_splits, (unsigned)(r.n_groups * r.n_q));
   const char* env = getenv("KUDAHITAM_DECODE_PATH");
   int path = (env && strcmp(env, "v1") == 0) ? 1 : (env && strcmp(env, "v2") == 0) ? 2 : 3;
-  if (r.cb.n_c == 4) path = 1;  // the 4-level codebook runs the direct kernel
+  // the 4-level codebook: the table kernel at D = 128, the direct one at D = 256
+  if (r.cb.n_c == 4 && (r.D == 256 || path != 3)) path = 1;
   // v3 work split (see decode_v3_kernel): ranges of W (cache group, row)
-  // pairs, one CTA set of n_q CTAs each.  W cuts the pairs into up to four
-  // waves of CTAs at two per SM (the hardware then hands a finished CTA's
+  // pairs, one CTA set of n_q CTAs each.  W cuts the pairs into one to four
+  // whole waves of CTAs at two per SM (the hardware then hands a finished CTA's
   // slot to the next range, so a slow SM costs at most a quarter wave; one
   // wave of long CTAs measured 17 % slower per step on the 131072-row
   // workload), but no range under 8192 pairs (a range pays the query
@@ -1158,7 +1526,8 @@ kh_status launch_decode_partial(const DecodeRequest& r, cudaStream_t stream) {
   } else {
     const int64_t total = r.n_groups * L;
     const int64_t slots = std::max<int64_t>(1, 2 * (int64_t)sm_count() / r.n_q);
-    const int64_t sets = std::max<int64_t>(1, std::min<int64_t>(4 * slots, (total + 8191) / 8192));
+    const int64_t waves = std::min<int64_t>(4, total / (8192 * slots));
+    const int64_t sets = waves >= 1 ? waves * slots : std::max<int64_t>(1, (total + 8191) / 8192);
     const int64_t w_bal = (total + sets - 1) / sets;
     const int64_t w_min = (L + r.n_splits - 2) / (r.n_splits - 1);
     P.W = std::max(w_bal, w_min);
@@ -1178,7 +1547,7 @@ kh_status launch_decode_partial(const DecodeRequest& r, cudaStream_t stream) {
     // the shared-memory opt-in is a per-device function attribute
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return KH_ECUDA;
-    static std::once_flag once[4][64];
+    static std::once_flag once[5][64];
     auto launch = [&](auto kern, int slot, int smem, int threads) {
       std::call_once(once[slot][dev & 63], [&] {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -1191,6 +1560,8 @@ kh_status launch_decode_partial(const DecodeRequest& r, cudaStream_t stream) {
     if (path == 2) {
       if (r.D == 128) launch(decode_v2_kernel<128>, 0, V2Cfg<128>::kSmem, V2Cfg<128>::kThreads);
       else launch(decode_v2_kernel<256>, 1, V2Cfg<256>::kSmem, V2Cfg<256>::kThreads);
+    } else if (r.cb.n_c == 4) {
+      launch(decode_b2_kernel, 4, B2Cfg::kSmem, B2Cfg::kThreads);
     } else {
       if (r.D == 128) launch(decode_v3_kernel<128>, 2, V3Cfg<128>::kSmem, V3Cfg<128>::kThreads);
       else launch(decode_v3_kernel<256>, 3, V3Cfg<256>::kSmem, V3Cfg<256>::kThreads);

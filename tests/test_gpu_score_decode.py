@@ -181,11 +181,12 @@ def test_decode_attention_matches_oracle(D, S, decode_path):
 
 
 @pytest.mark.parametrize("D", [128, 256])
-@pytest.mark.parametrize("S", [1, 300, 2000])
-def test_decode_bits2_codebook_matches_oracle(D, S):
+@pytest.mark.parametrize("S", [1, 300, 2000, 13000])
+def test_decode_bits2_codebook_matches_oracle(D, S, monkeypatch):
     """The 4-level (bits=2) codebook: 2-bit code plane plus the residual
-    plane, V reconstructed with c[idx] from four levels (the direct decode
-    kernel), against the oracle's fp64 decode of its own compression."""
+    plane, V reconstructed with c[idx] from four levels (the table kernel at
+    D = 128, the direct kernel at D = 256), against the oracle's fp64 decode
+    of its own compression; at D = 128 also against the direct kernel."""
     G = 4
     dk, dv = rademacher(D, 10).numpy(), rademacher(D, 11).numpy()
     c = lloyd_max(2, D).numpy()
@@ -204,6 +205,12 @@ def test_decode_bits2_codebook_matches_oracle(D, S):
         got = got.cpu().numpy()
         for gi in range(G):
             assert K.normwise(got[gi], want[gi]) < 1e-3, (n_splits, gi)
+        if D == 128:
+            monkeypatch.setenv("KUDAHITAM_DECODE_PATH", "v1")  # the direct kernel
+            direct = ops.decode_attention(q.cuda(), pk, pv, dk, dv, c, sm, n_splits=n_splits)
+            monkeypatch.delenv("KUDAHITAM_DECODE_PATH")
+            for gi in range(G):
+                assert K.normwise(got[gi], direct.cpu().numpy()[gi]) < 1e-4, (n_splits, gi)
 
 
 @pytest.mark.parametrize("sm_mult", [1.0, 12.0])

@@ -80,6 +80,8 @@ def test_decode_split_rule():
     for R, L, nq in ((512, 40000, 1), (32, 40000, 1), (7, 12345, 1), (64, 9000, 4)):
         n = splits_for(R, L, 148, nq)
         total = (R // nq) * L
-        sets = max(1, min(4 * (2 * 148 // nq), -(-total // 8192)))
+        slots = 2 * 148 // nq
+        waves = min(4, total // (8192 * slots))
+        sets = waves * slots if waves >= 1 else max(1, -(-total // 8192))
         w = -(-total // sets)
         assert -(-L // w) + 1 <= n
