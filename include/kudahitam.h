@@ -176,6 +176,49 @@ int kh_score_packed_compat(const void* q, int64_t n_heads, int head_dim,
                            void* stream);
 
 /*
+ * kh_compress_hbba -- the HBBA mixed-codebook encoder.  Replaces
+ * ultra_fused_packed_hbba_fusion_cuda / _kernel (KudaHitamCUDA.cu:285-420),
+ * bound as ultra_fused_hbba_fusion (:801) and called by
+ * KudahitamCompressorHBBA.compress (KudaHitamQuant_full-reasoning.py:521).
+ * Its output is the packed cache kh_score_packed_compat reads.  Per row of
+ * x (fp32 / fp16 / bf16, row r at x + r*row_stride elements):
+ *   norm   = sqrt(sum x^2 + 1e-8)
+ *   y      = H(x / norm (.) d) / sqrt(D)
+ *   idx_i  = argmin_c |y_i - fp16(centroids[i][c])| over 16 levels when the
+ *            layer is HBBA ((active_mask >> layer_id) & 1, 0 <= layer_id < 8)
+ *            and bit (i & 31) of hbba_mask[i >> 5] is set, else over 2
+ *   out_packed  uint8 [n_rows][128] (HBBA layer: nibble (i & 1) of byte
+ *               i >> 1) or [n_rows][32] (bit (i & 7) of byte i >> 3); bytes
+ *               past the row's D indices are zero
+ *   out_norms   float [n_rows]; out_rnorms = sqrt(sum (y - c)^2 * D + 1e-8)
+ *   out_signs   fp16 [n_rows][D] = H(y - c[idx]) (unnormalised)
+ * Both sums of squares run over the whole row (the reference's reduce
+ * within one warp of its 256 threads, :312-314 and :377).  d [D],
+ * centroids [D][16] and hbba_mask [8] are DEVICE arrays, as in the
+ * reference binding.
+ */
+int kh_compress_hbba(const void* x, int dtype, int64_t n_rows, int head_dim,
+                     int64_t row_stride, const float* d, const float* centroids,
+                     const uint32_t* hbba_mask, int layer_id, int active_mask,
+                     uint8_t* out_packed, float* out_norms, float* out_rnorms,
+                     void* out_signs, void* stream);
+
+/*
+ * kh_hbba_calibrate -- per-dimension Lloyd-Max levels for the HBBA encoder.
+ * Replaces hbba_calibrate_cuda / hbba_calibrate_cuda_kernel
+ * (KudaHitamCUDA.cu:423-516, called from
+ * KudaHitamQuant_full-reasoning.py:490).  For dimension d with
+ * n = n_map[d] levels (clamped to [1, 16]): levels start uniform between
+ * the sample's min and max, then 10 rounds of nearest level (strict <,
+ * lowest index) and mean update (a level with no samples keeps its value).
+ * sample float [n_rows][head_dim] and n_map int [head_dim] are device
+ * arrays; writes out_centroids float [head_dim][16], unused entries 0.
+ * Sums accumulate in double in a fixed order (deterministic).
+ */
+int kh_hbba_calibrate(const float* sample, int64_t n_rows, int head_dim, const int* n_map,
+                      float* out_centroids, void* stream);
+
+/*
  * kh_decode_partial_gqa -- kh_decode_partial for grouped-query attention:
  * n_q query heads share each cache group (H_q = n_q * H_kv).  q is
  * [n_groups][n_q][D]; partial records (and the combine step's n_groups

@@ -490,6 +490,38 @@ int kh_decode_combine_from_peers(const float* records, const uint32_t* flags, ui
                                           d_v_host, out, static_cast<cudaStream_t>(stream));
 }
 
+int kh_compress_hbba(const void* x, int dtype, int64_t n_rows, int head_dim,
+                     int64_t row_stride, const float* d, const float* centroids,
+                     const uint32_t* hbba_mask, int layer_id, int active_mask,
+                     uint8_t* out_packed, float* out_norms, float* out_rnorms,
+                     void* out_signs, void* stream) {
+  if (dtype != KH_F32 && dtype != KH_F16 && dtype != KH_BF16) return KH_EINVAL;
+  if (!valid_head_dim(head_dim) || n_rows < 0 || n_rows >= (int64_t(1) << 40)) return KH_EINVAL;
+  if (row_stride < head_dim) return KH_EINVAL;
+  if (n_rows == 0) return KH_OK;
+  if (!x || !d || !centroids || !hbba_mask || !out_packed || !out_norms || !out_rnorms ||
+      !out_signs)
+    return KH_EINVAL;
+  if ((reinterpret_cast<uintptr_t>(x) & (dtype_size(dtype) - 1)) != 0 ||
+      !aligned4(out_packed) || !aligned4(out_norms) || !aligned4(out_rnorms) ||
+      (reinterpret_cast<uintptr_t>(out_signs) & 1) != 0 || !aligned4(d) || !aligned4(centroids) ||
+      !aligned4(hbba_mask))
+    return KH_EALIGN;
+  const int is_hbba = layer_id >= 0 && layer_id < 8 && (((active_mask & 0xFF) >> layer_id) & 1);
+  return launch_hbba_compress(x, dtype, n_rows, head_dim, row_stride, d, centroids, hbba_mask,
+                              is_hbba, out_packed, out_norms, out_rnorms, out_signs,
+                              static_cast<cudaStream_t>(stream));
+}
+
+int kh_hbba_calibrate(const float* sample, int64_t n_rows, int head_dim, const int* n_map,
+                      float* out_centroids, void* stream) {
+  if (n_rows < 1 || head_dim < 1 || head_dim > 1024) return KH_EINVAL;
+  if (!sample || !n_map || !out_centroids) return KH_EINVAL;
+  if (!aligned4(sample) || !aligned4(n_map) || !aligned4(out_centroids)) return KH_EALIGN;
+  return launch_hbba_calibrate(sample, n_rows, head_dim, n_map, out_centroids,
+                               static_cast<cudaStream_t>(stream));
+}
+
 int kh_decode_attn(const float* q, int64_t n_groups, int head_dim,
                    const uint32_t* k_code, const uint32_t* k_res,
                    const float* k_norms, const float* k_rnorms,

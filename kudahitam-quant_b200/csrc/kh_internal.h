@@ -111,6 +111,15 @@ kh_status launch_decode_combine_from_peers(const float* records, const uint32_t*
                                            uint32_t epoch, int64_t n_rows, int world, int D,
                                            const float* dv, float* out, cudaStream_t stream);
 
+// HBBA encoder and calibrator (kh_hbba.cu).  d, cent, mask and n_map are
+// device arrays, as in the reference binding.
+kh_status launch_hbba_compress(const void* x, int dtype, int64_t n_rows, int D,
+                               int64_t row_stride, const float* d, const float* cent,
+                               const uint32_t* mask, int is_hbba, uint8_t* packed,
+                               float* norms, float* rnorms, void* signs, cudaStream_t stream);
+kh_status launch_hbba_calibrate(const float* sample, int64_t n, int D, const int* n_map,
+                                float* out, cudaStream_t stream);
+
 // Device address of the sticky error word on the current device.
 uint32_t* device_error_ptr();
 

@@ -457,6 +457,60 @@ void decode_combine_from_peers(const Tensor& buf, int64_t rec_offset, int64_t fl
         "kh_decode_combine_from_peers");
 }
 
+// ------------------------------------------------------------------ HBBA
+
+std::tuple<Tensor, Tensor, Tensor, Tensor> ultra_fused_hbba_fusion(
+    const Tensor& x, const Tensor& d, const Tensor& centroids_table, const Tensor& mask,
+    int64_t layer_id, int64_t active_mask) {
+  require_cuda(x, "x");
+  TORCH_CHECK(x.dim() == 2, "x must be [N, D]");
+  const int64_t N = x.size(0), D = x.size(1);
+  const auto dev = x.device();
+  const auto prep = [&](const Tensor& t, at::ScalarType s, int64_t n, const char* what) {
+    TORCH_CHECK(t.numel() == n, what, " must hold ", n, " values");
+    Tensor u = t.to(dev, s).contiguous();
+    return u;
+  };
+  Tensor xr = x.stride(-1) == 1 ? x : x.contiguous();
+  Tensor dd = prep(d, at::kFloat, D, "d");
+  Tensor cb = prep(centroids_table, at::kFloat, D * 16, "centroids_table");
+  Tensor mk = prep(mask, at::kInt, 8, "mask");
+  const bool hbba = layer_id >= 0 && layer_id < 8 && (((active_mask & 0xFF) >> layer_id) & 1);
+  auto o = x.options();
+  Tensor packed = at::empty({N, hbba ? 128 : 32}, o.dtype(at::kByte));
+  Tensor norms = at::empty({N, 1}, o.dtype(at::kFloat));
+  Tensor rnorms = at::empty({N}, o.dtype(at::kFloat));
+  Tensor signs = at::empty({N, D}, o.dtype(at::kHalf));
+  c10::cuda::CUDAGuard guard(dev);
+  check(kh_compress_hbba(xr.data_ptr(), dtype_code(x.scalar_type()), N, (int)D,
+                         N > 1 ? xr.stride(0) : D, dd.data_ptr<float>(), cb.data_ptr<float>(),
+                         reinterpret_cast<const uint32_t*>(mk.data_ptr<int>()), (int)layer_id,
+                         (int)(active_mask & 0xFF), packed.data_ptr<uint8_t>(),
+                         norms.data_ptr<float>(), rnorms.data_ptr<float>(), signs.data_ptr(),
+                         stream_of(x)),
+        "kh_compress_hbba");
+  return {packed, norms, rnorms, signs};
+}
+
+Tensor hbba_calibrate_cuda(const Tensor& sample, const Tensor& n_map, int64_t layer_id,
+                           int64_t active_mask) {
+  require_cuda(sample, "sample");
+  TORCH_CHECK(sample.dim() == 2, "sample must be [N, D]");
+  const int64_t D = sample.size(1);
+  auto o = sample.options().dtype(at::kFloat);
+  Tensor out = at::zeros({D, 16}, o);
+  const bool hbba = layer_id >= 0 && layer_id < 8 && (((active_mask & 0xFF) >> layer_id) & 1);
+  if (!hbba || sample.size(0) == 0) return out;  // the reference returns zeros too (:499)
+  Tensor smp = sample.to(at::kFloat).contiguous();
+  TORCH_CHECK(n_map.numel() == D, "n_map must hold D values");
+  Tensor nm = n_map.to(sample.device(), at::kInt).contiguous();
+  c10::cuda::CUDAGuard guard(sample.device());
+  check(kh_hbba_calibrate(smp.data_ptr<float>(), smp.size(0), (int)D, nm.data_ptr<int>(),
+                          out.data_ptr<float>(), stream_of(sample)),
+        "kh_hbba_calibrate");
+  return out;
+}
+
 // ------------------------------------------------- reference-layout compat
 
 std::tuple<Tensor, Tensor, Tensor, Tensor, Tensor> ultra_fused_full_fusion(const Tensor& x,
@@ -534,6 +588,10 @@ TORCH_LIBRARY(kudahitam, m) {
         "int epoch, Tensor(a!) counter) -> ()");
   m.def("decode_combine_from_peers(Tensor buf, int rec_offset, int flag_offset, int epoch, "
         "int n_rows, int world, Tensor dv, Tensor(a!) out) -> ()");
+  m.def("ultra_fused_hbba_fusion(Tensor x, Tensor d, Tensor centroids_table, Tensor mask, "
+        "int layer_id, int active_mask) -> (Tensor, Tensor, Tensor, Tensor)");
+  m.def("hbba_calibrate_cuda(Tensor sample, Tensor n_map, int layer_id, int active_mask) "
+        "-> Tensor");
   m.def("ultra_fused_full_fusion(Tensor x, Tensor d, Tensor centroids) "
         "-> (Tensor, Tensor, Tensor, Tensor, Tensor)");
   m.def("fused_asymmetric_attention(Tensor q, Tensor k_packed, Tensor signs, Tensor d_vec, "
@@ -555,6 +613,8 @@ TORCH_LIBRARY_IMPL(kudahitam, CUDA, m) {
   m.impl("decode_attention", &decode_attention);
   m.impl("decode_merge_to_peers", &decode_merge_to_peers);
   m.impl("decode_combine_from_peers", &decode_combine_from_peers);
+  m.impl("ultra_fused_hbba_fusion", &ultra_fused_hbba_fusion);
+  m.impl("hbba_calibrate_cuda", &hbba_calibrate_cuda);
   m.impl("ultra_fused_full_fusion", &ultra_fused_full_fusion);
   m.impl("fused_asymmetric_attention", &fused_asymmetric_attention);
 }

@@ -38,6 +38,9 @@ SIGNATURES = {
                         _c_i, _vp, _vp]),
     "kh_score_packed_compat": (_c_i, [_vp, _c_i64, _c_i, _c_i64, _vp, _vp, _vp, _vp, _vp,
                                       _vp, _c_i, _c_i, _c_f, _vp, _vp]),
+    "kh_compress_hbba": (_c_i, [_vp, _c_i, _c_i64, _c_i, _c_i64, _vp, _vp, _vp, _c_i, _c_i,
+                                _vp, _vp, _vp, _vp, _vp]),
+    "kh_hbba_calibrate": (_c_i, [_vp, _c_i64, _c_i, _vp, _vp, _vp]),
     "kh_decode_workspace_bytes": (_c_i64, [_c_i64, _c_i, _c_i]),
     "kh_decode_partial": (_c_i, [_vp, _c_i64, _c_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                                  _vp, _c_i64, _c_i64, _c_i64, _vp, _vp, _vp, _c_i, _c_f,

@@ -522,6 +522,33 @@ def ultra_fused_full_fusion(x: torch.Tensor, d, centroids):
     return tuple(ext().ultra_fused_full_fusion(x, _host_f32(d), _host_f32(centroids)))
 
 
+def ultra_fused_hbba_fusion(x: torch.Tensor, d, centroids_table: torch.Tensor,
+                            mask: torch.Tensor, layer_id: int, active_mask: int):
+    """The HBBA encoder with the reference binding's arguments and outputs
+    (ultra_fused_hbba_fusion, KudaHitamCUDA.cu:397-420): x [N, D] (fp16 as in
+    the reference; bf16 / fp32 accepted), d [D], centroids_table [D, 16],
+    mask int32 [8].  Returns (packed uint8 [N, 128 or 32], norms [N, 1],
+    r_norms [N], signs fp16 [N, D])."""
+    dev = _require_cuda(x)
+    if x.dim() != 2 or x.shape[-1] not in HEAD_DIMS:
+        raise ValueError("x must be [N, D] with D in (128, 256)")
+    if x.dtype not in _DTYPE_CODE:
+        raise TypeError(f"unsupported dtype {x.dtype}")
+    d = torch.as_tensor(d).to(dev)
+    return tuple(ext().ultra_fused_hbba_fusion(x, d, centroids_table.to(dev), mask.to(dev),
+                                               int(layer_id), int(active_mask)))
+
+
+def hbba_calibrate(sample: torch.Tensor, n_map, layer_id: int, active_mask: int) -> torch.Tensor:
+    """Per-dimension levels for the HBBA encoder (hbba_calibrate_cuda,
+    KudaHitamCUDA.cu:498-516): sample [N, D] on the GPU, n_map [D] levels
+    (2 or 16).  Returns float32 [D, 16]; zeros when bit layer_id of
+    active_mask is clear, as the reference does."""
+    _require_cuda(sample)
+    return ext().hbba_calibrate_cuda(sample, torch.as_tensor(n_map).to(sample.device),
+                                     int(layer_id), int(active_mask))
+
+
 def fused_asymmetric_attention(q: torch.Tensor, k_packed: torch.Tensor, signs: torch.Tensor,
                                d_vec: torch.Tensor, k_norms: torch.Tensor,
                                r_norms: torch.Tensor, centroids: torch.Tensor,

@@ -14,6 +14,9 @@
  *              KudaHitamCUDA.cu:695-772 (packed-byte scorer); pinned bit for
  *              bit against the reference kernel itself on the GPU
  *              (build_ref.py, tests/test_gpu_reference_kernels.py)
+ *   hbba     : ultra_fused_packed_hbba_fusion_kernel, KudaHitamCUDA.cu:285-395
+ *              (with whole-row reductions; see khx_hbba_compress) and
+ *              hbba_calibrate_cuda_kernel, :423-496
  *
  * Arithmetic follows the kernel in fp32 and in its order: the same
  * butterfly stage order, the same segmented shuffle-tree reductions, the
@@ -322,6 +325,124 @@ void khx_compat_score(const _Float16* q, int64_t H, int D, int64_t S,
       const float t2 = kn * scale * l2[0];
       out[row] = fmaf(t2, r_norms[row], l1[0]);
     }
+  }
+}
+
+/*
+ * HBBA mixed-codebook encoder, ultra_fused_packed_hbba_fusion_kernel
+ * (KudaHitamCUDA.cu:285-395), with the reductions it intends.  The
+ * reference sums ||x||^2 and the residual's squares with a warp shuffle
+ * only (:312-314, :377) while 256 threads hold the row, so for D > 32 each
+ * warp divides its 32 elements by its own partial norm and the stored norms
+ * cover elements 0..31; its thread 0 also copies the packed bytes out
+ * (:378-381) with no barrier after the other warps' atomicOr.  Here both
+ * sums run over the whole row.  Per row:
+ *   norm   = sqrtf(sum x^2 + 1e-8)                                 (:313-315)
+ *   y      = H(x / norm (.) d) / sqrt(D), Sylvester order          (:323-341)
+ *   n_c    = 16 if the layer is HBBA and bit i of mask is set, else 2 (:345-347)
+ *   idx_i  = argmin_c |y_i - half(c[i][c])|, strict <, lowest index (:349-353)
+ *   packed = nibble (i & 1) of byte i >> 1 (HBBA layer, 128 bytes per row)
+ *            or bit (i & 7) of byte i >> 3 (32 bytes per row)        (:356-366)
+ *   diff_i = y_i - half(c[i][idx_i]); r_norm = sqrtf(sum diff^2 * D + 1e-8)
+ *   signs  = half(H diff), unnormalised                            (:368-395)
+ * Sums of squares accumulate in double.  x [n][D]; cent [D][16];
+ * mask [8]; packed [n][32 or 128] (zero-filled); signs [n][D].
+ */
+void khx_hbba_compress(const void* x, int dtype, int64_t n, int D, const float* d,
+                       const float* cent, const uint32_t* mask, int is_hbba,
+                       uint8_t* packed, float* norms, float* rnorms, _Float16* signs) {
+  const int bpt = is_hbba ? 128 : 32;
+  const float f_scale = 1.0f / sqrtf((float)D);
+#ifdef _OPENMP
+#pragma omp parallel for schedule(static)
+#endif
+  for (int64_t r = 0; r < n; ++r) {
+    float v[256], c16[256][16];
+    for (int i = 0; i < D; ++i)
+      for (int c = 0; c < 16; ++c) c16[i][c] = (float)(_Float16)cent[i * 16 + c];
+    double ss = 0.0;
+    for (int i = 0; i < D; ++i) {
+      v[i] = load_elt(x, dtype, r * D + i);
+      ss += (double)v[i] * (double)v[i];
+    }
+    const float norm = sqrtf((float)ss + 1e-8f);
+    norms[r] = norm;
+    const float inv = 1.0f / norm;
+    for (int i = 0; i < D; ++i) v[i] = (v[i] * inv) * d[i];
+    for (int h = 1; h < D; h <<= 1) stage(v, D, h);
+    uint8_t* pk = packed + r * bpt;
+    memset(pk, 0, bpt);
+    double rs = 0.0;
+    for (int i = 0; i < D; ++i) {
+      const float y = v[i] * f_scale;
+      const int n_c = (is_hbba && ((mask[i >> 5] >> (i & 31)) & 1u)) ? 16 : 2;
+      int best = 0;
+      float md = 1e18f;
+      for (int c = 0; c < n_c; ++c) {
+        const float dist = fabsf(y - c16[i][c]);
+        if (dist < md) {
+          md = dist;
+          best = c;
+        }
+      }
+      if (is_hbba) pk[i >> 1] |= (uint8_t)((best & 15) << ((i & 1) ? 4 : 0));
+      else pk[i >> 3] |= (uint8_t)((best & 1) << (i & 7));
+      const float diff = y - c16[i][best];
+      rs += (double)diff * (double)diff;
+      v[i] = diff;
+    }
+    rnorms[r] = sqrtf((float)rs * (float)D + 1e-8f);
+    for (int h = 1; h < D; h <<= 1) stage(v, D, h);
+    for (int i = 0; i < D; ++i) signs[r * D + i] = (_Float16)v[i];
+  }
+}
+
+/*
+ * HBBA calibrator, hbba_calibrate_cuda_kernel (KudaHitamCUDA.cu:423-496):
+ * per dimension d with n_c = n_map[d] levels (<= 16), centroids start
+ * uniform between the sample's min and max, c_k = min + k (max - min) /
+ * max(1, n_c - 1) (:458-462), then 10 rounds of nearest-centroid assignment
+ * (strict <, lowest index) and mean update, a centroid with no samples
+ * keeping its value (:466-488).  Sums accumulate in double (the reference
+ * adds with float atomics in unspecified order).  sample [n][D]; out
+ * [D][16], unused entries 0.
+ */
+void khx_hbba_calibrate(const float* sample, int64_t n, int D, const int* n_map, float* out) {
+#ifdef _OPENMP
+#pragma omp parallel for schedule(static)
+#endif
+  for (int d = 0; d < D; ++d) {
+    const int n_c = n_map[d] < 1 ? 1 : (n_map[d] > 16 ? 16 : n_map[d]);
+    float mn = 1e18f, mx = -1e18f;
+    for (int64_t i = 0; i < n; ++i) {
+      const float v = sample[i * D + d];
+      mn = fminf(mn, v);
+      mx = fmaxf(mx, v);
+    }
+    float c[16];
+    for (int k = 0; k < n_c; ++k)
+      c[k] = mn + (float)k * (mx - mn) / fmaxf(1.0f, (float)(n_c - 1));
+    for (int it = 0; it < 10; ++it) {
+      double sum[16] = {0};
+      int64_t cnt[16] = {0};
+      for (int64_t i = 0; i < n; ++i) {
+        const float v = sample[i * D + d];
+        int best = 0;
+        float md = 1e18f;
+        for (int k = 0; k < n_c; ++k) {
+          const float dist = fabsf(v - c[k]);
+          if (dist < md) {
+            md = dist;
+            best = k;
+          }
+        }
+        sum[best] += v;
+        cnt[best] += 1;
+      }
+      for (int k = 0; k < n_c; ++k)
+        if (cnt[k] > 0) c[k] = (float)(sum[k] / (double)cnt[k]);
+    }
+    for (int k = 0; k < 16; ++k) out[d * 16 + k] = k < n_c ? c[k] : 0.0f;
   }
 }
 

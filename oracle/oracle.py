@@ -53,6 +53,9 @@ def lib():
         L.khx_compat_score.argtypes = [_vp, ctypes.c_int64, ctypes.c_int, ctypes.c_int64, _vp,
                                        ctypes.c_int, _vp, _vp, _vp, _vp, _vp, ctypes.c_float,
                                        _vp]
+        L.khx_hbba_compress.argtypes = [_vp, ctypes.c_int, ctypes.c_int64, ctypes.c_int, _vp,
+                                        _vp, _vp, ctypes.c_int, _vp, _vp, _vp, _vp]
+        L.khx_hbba_calibrate.argtypes = [_vp, ctypes.c_int64, ctypes.c_int, _vp, _vp]
         L.khx_num_threads.restype = ctypes.c_int
         _lib = L
     return _lib
@@ -210,6 +213,37 @@ def compat_score(q, k_packed, signs, d, k_norms, r_norms, centroids, nibble: boo
     out = np.empty((H, S), np.float32)
     lib().khx_compat_score(_ptr(q), H, D, S, _ptr(kp), int(bool(nibble)), _ptr(sg),
                            *[_ptr(a) for a in arrs], float(scale), _ptr(out))
+    return out
+
+
+def hbba_compress(x, d, centroids, mask, is_hbba: bool) -> dict:
+    """The HBBA encoder (KudaHitamCUDA.cu:285-395, whole-row reductions):
+    x [..., D]; centroids [D, 16]; mask [8] uint32.  Returns packed uint8
+    [N, 128 or 32], norms [N], r_norms [N], signs float16 [N, D]."""
+    raw, code = as_raw(x)
+    D = raw.shape[-1]
+    raw = np.ascontiguousarray(raw.reshape(-1, D))
+    n = raw.shape[0]
+    d = np.ascontiguousarray(np.asarray(d, dtype=np.float32))
+    cen = np.ascontiguousarray(np.asarray(centroids, dtype=np.float32).reshape(D, 16))
+    m = np.ascontiguousarray(np.asarray(mask).astype(np.int64).astype(np.uint32).reshape(8))
+    bpt = 128 if is_hbba else 32
+    out = {"packed": np.zeros((n, bpt), np.uint8), "norms": np.empty(n, np.float32),
+           "rnorms": np.empty(n, np.float32), "signs": np.empty((n, D), np.float16)}
+    lib().khx_hbba_compress(_ptr(raw), code, n, D, _ptr(d), _ptr(cen), _ptr(m), int(is_hbba),
+                            _ptr(out["packed"]), _ptr(out["norms"]), _ptr(out["rnorms"]),
+                            _ptr(out["signs"]))
+    return out
+
+
+def hbba_calibrate(sample, n_map) -> np.ndarray:
+    """The HBBA calibrator (KudaHitamCUDA.cu:423-496): sample [N, D] float;
+    n_map [D] levels per dimension.  Returns centroids [D, 16]."""
+    smp = np.ascontiguousarray(np.asarray(sample, dtype=np.float32))
+    n, D = smp.shape
+    nm = np.ascontiguousarray(np.asarray(n_map, dtype=np.int32).reshape(D))
+    out = np.zeros((D, 16), np.float32)
+    lib().khx_hbba_calibrate(_ptr(smp), n, D, _ptr(nm), _ptr(out))
     return out
 
 

@@ -4,9 +4,12 @@
 // The reference (KudaHitamCUDA.cu) defines ultra_fused_full_fusion_cuda
 // (:197-231) but never exports it (its module, :799-804, binds only forward,
 // the HBBA encoder and calibrator, and fused_asymmetric_attention).  This
-// file declares the three launchers this engine replaces -- with the
+// file declares the launchers this engine is checked against -- with the
 // reference's signatures -- and exports them from a module of its own, so the
-// reference kernels can run unchanged beside the engine.  build_ref.py
+// reference kernels can run unchanged beside the engine.  (The HBBA encoder
+// is not exported: it reduces its sums within one warp of its 256 threads
+// and copies its packed bytes out without a barrier, KudaHitamCUDA.cu:312-381,
+// so its output is not a checker.)  build_ref.py
 // compiles KudaHitamCUDA.cu where it lies and links it with this file into
 // oracle/_ref/kh_ref.so.
 #include <torch/extension.h>
@@ -16,6 +19,8 @@
 std::vector<torch::Tensor> ultra_fused_full_fusion_cuda(torch::Tensor x, torch::Tensor d,
                                                         torch::Tensor centroids);
 void fwht_cuda_forward(torch::Tensor x);
+torch::Tensor hbba_calibrate_cuda(torch::Tensor sample, torch::Tensor n_map, int layer_id,
+                                  uint8_t active_mask);
 torch::Tensor fused_asymmetric_attention_packed_cuda(torch::Tensor q, torch::Tensor k_packed,
                                                      torch::Tensor signs, torch::Tensor d_vec,
                                                      torch::Tensor k_norms, torch::Tensor r_norms,
@@ -28,4 +33,6 @@ PYBIND11_MODULE(kh_ref, m) {
   m.def("forward", &fwht_cuda_forward, "reference orthonormal FWHT (KudaHitamCUDA.cu:233-283)");
   m.def("fused_asymmetric_attention", &fused_asymmetric_attention_packed_cuda,
         "reference packed scorer (KudaHitamCUDA.cu:695-797)");
+  m.def("hbba_calibrate_cuda", &hbba_calibrate_cuda,
+        "reference HBBA calibrator (KudaHitamCUDA.cu:423-516)");
 }

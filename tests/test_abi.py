@@ -160,7 +160,7 @@ def test_gqa_decode_and_compat_scorer_validate():
 TORCH_OPS = ["compress", "compress_out", "compress_many_out", "fwht_", "materialize", "score",
              "score_out", "decode_partial", "decode_combine", "decode_merge", "decode_attention",
              "decode_merge_to_peers", "decode_combine_from_peers", "ultra_fused_full_fusion",
-             "fused_asymmetric_attention"]
+             "ultra_fused_hbba_fusion", "hbba_calibrate_cuda", "fused_asymmetric_attention"]
 
 
 def test_torch_extension_registers_every_operator():

@@ -85,3 +85,64 @@ def test_decode_split_rule():
         sets = waves * slots if waves >= 1 else max(1, -(-total // 8192))
         w = -(-total // sets)
         assert -(-L // w) + 1 <= n
+
+
+def _launcher_ranges(G, nq, L, n_splits, sms):
+    """kh_decode.cu launch_decode_partial: (W, CTA count) of the v3 split."""
+    if L == 0:
+        return 0, G * nq
+    if n_splits == 1:
+        return L, G * nq
+    total = G * L
+    slots = max(1, 2 * sms // nq)
+    waves = min(4, total // (8192 * slots))
+    sets = waves * slots if waves >= 1 else max(1, -(-total // 8192))
+    W = max(-(-total // sets), -(-L // (n_splits - 1)))
+    return W, -(-total // W) * nq
+
+
+def _kernel_writes(G, nq, L, seq_begin, n_splits, W, n_cta):
+    """decode_v3_kernel / decode_b2_kernel: record slots written and (query
+    row, sequence row) pairs covered, from the kernel's index arithmetic."""
+    writes, cover = {}, {}
+    for b in range(n_cta):
+        if W == 0:
+            for p in range(n_splits):
+                writes.setdefault((b, p), []).append("empty")
+            continue
+        jq, st = b % nq, b // nq
+        wbeg, wend = st * W, min(st * W + W, G * L)
+        gk = wbeg // L
+        while gk * L < wend:
+            g = gk * nq + jq
+            s0, s1 = seq_begin + max(wbeg - gk * L, 0), seq_begin + min(wend - gk * L, L)
+            assert s1 > s0
+            rp = st - gk * L // W
+            assert 0 <= rp < n_splits, (G, nq, L, n_splits, W)
+            writes.setdefault((g, rp), []).append("rec")
+            for s in range(s0, s1):
+                cover[(g, s)] = cover.get((g, s), 0) + 1
+            if s1 == seq_begin + L:
+                for p in range(rp + 1, n_splits):
+                    writes.setdefault((g, p), []).append("empty")
+            gk += 1
+    return writes, cover
+
+
+def test_decode_work_split_covers_every_row_once():
+    import random
+    rng = random.Random(0)
+    cases = [(512, 1, 40000, 4, 148), (512, 1, 5000, 2, 148), (32, 1, 40000, 6, 148),
+             (6, 3, 3000, 2, 148), (48, 1, 3000, 8, 148), (1613, 1, 64, 5, 148),
+             (2, 3, 17, 4, 148), (3, 1, 1, 1, 148), (5, 2, 0, 3, 148)]
+    cases += [(rng.randint(1, 40), rng.choice([1, 2, 3, 4, 8]), rng.randint(0, 1500),
+               rng.randint(1, 9), rng.choice([4, 7, 148])) for _ in range(300)]
+    for G, nq, L, ns, sms in cases:
+        W, n_cta = _launcher_ranges(G, nq, L, ns, sms)
+        writes, cover = _kernel_writes(G, nq, L, 3, ns, W, n_cta)
+        for g in range(G * nq):
+            for p in range(ns):
+                assert len(writes.get((g, p), [])) == 1, (G, nq, L, ns, sms, g, p)
+            for s in range(3, 3 + L):
+                assert cover.get((g, s), 0) == 1, (G, nq, L, ns, g, s)
+        assert all(g < G * nq and p < ns for g, p in writes)
