@@ -373,8 +373,8 @@ def default_splits(n_groups: int, seq_len: int, device, n_q: int = 1) -> int:
     n_groups query rows (n_q per cache group) of seq_len cached rows.
 
     The decode kernel cuts the call's (cache group, row) pairs into equal
-    ranges, one to four whole waves of CTAs at two per SM and no range
-    under 8192 pairs, whatever the group count; a group spanning several ranges gets
+    ranges, one wave of CTAs at two per SM and no range under 8192 pairs,
+    whatever the group count; a group spanning several ranges gets
     one record per range.  This rule returns how many records the longest
     group can need at that range length, so the kernel runs balanced.  (The
     earlier one-CTA-per-(row, split) grid ran 1.73 waves for 512 query rows
@@ -385,16 +385,14 @@ def default_splits(n_groups: int, seq_len: int, device, n_q: int = 1) -> int:
 
 def splits_for(n_rows: int, seq_len: int, n_sms: int, n_q: int = 1) -> int:
     """The rule of ``default_splits`` for a GPU with n_sms SMs; mirrors the
-    decode launcher's range length (kh_decode.cu: one to four whole waves
-    of CTA sets of n_q CTAs at two CTAs per SM, about 8192 pairs per range
-    at least)."""
+    decode launcher's range length (kh_decode.cu: one wave of CTA sets of
+    n_q CTAs at two CTAs per SM, at least 8192 pairs per range)."""
     if seq_len <= 0 or n_rows <= 0:
         return 1
     groups = max(1, n_rows // max(n_q, 1))
     total = groups * seq_len
     slots = max(1, 2 * n_sms // max(n_q, 1))
-    waves = min(4, total // (8192 * slots))
-    sets = waves * slots if waves >= 1 else max(1, -(-total // 8192))
+    sets = max(1, min(slots, -(-total // 8192)))
     w_bal = -(-total // sets)
     return int(min(1024, -(-seq_len // w_bal) + 1))
 

@@ -67,22 +67,20 @@ def test_lloyd_max_other_dims_sorted_symmetric():
 
 def test_decode_split_rule():
     """Records per query row on a 148-SM GPU: the kernel cuts (group, row)
-    pairs into ranges over up to four waves of 296 CTAs, none under 8192
-    pairs; a group gets one record per range it touches."""
+    pairs into ranges over one wave of 296 CTAs, none under 8192 pairs; a
+    group gets one record per range it touches."""
     from kudahitam.ops import splits_for
-    assert [splits_for(512, s, 148) for s in (5000, 10000, 20000, 40000)] == [2, 3, 4, 4]
-    assert splits_for(32, 40000, 148) == 6       # one sequence of 32 heads
-    assert splits_for(1024, 131072, 148) == 3
+    assert [splits_for(512, s, 148) for s in (5000, 10000, 20000, 40000)] == [2, 2, 2, 2]
+    assert splits_for(32, 40000, 148) == 6       # one sequence of 32 heads: 157 ranges
+    assert splits_for(1024, 131072, 148) == 2
     assert splits_for(512, 100, 148) == 2 and splits_for(0, 0, 148) == 1
-    assert splits_for(1, 10 ** 9, 148) == 1024   # capped
+    assert splits_for(1, 10 ** 9, 148) == 297
     assert splits_for(64, 4096, 148, n_q=8) == 2  # 8 groups: 4 ranges of 8192
     # the launcher's range is never shorter than L / (n - 1): a group spans at most n ranges
     for R, L, nq in ((512, 40000, 1), (32, 40000, 1), (7, 12345, 1), (64, 9000, 4)):
         n = splits_for(R, L, 148, nq)
         total = (R // nq) * L
-        slots = 2 * 148 // nq
-        waves = min(4, total // (8192 * slots))
-        sets = waves * slots if waves >= 1 else max(1, -(-total // 8192))
+        sets = max(1, min(2 * 148 // nq, -(-total // 8192)))
         w = -(-total // sets)
         assert -(-L // w) + 1 <= n
 
@@ -95,8 +93,7 @@ def _launcher_ranges(G, nq, L, n_splits, sms):
         return L, G * nq
     total = G * L
     slots = max(1, 2 * sms // nq)
-    waves = min(4, total // (8192 * slots))
-    sets = waves * slots if waves >= 1 else max(1, -(-total // 8192))
+    sets = max(1, min(slots, -(-total // 8192)))
     W = max(-(-total // sets), -(-L // (n_splits - 1)))
     return W, -(-total // W) * nq
 
@@ -132,7 +129,7 @@ def _kernel_writes(G, nq, L, seq_begin, n_splits, W, n_cta):
 def test_decode_work_split_covers_every_row_once():
     import random
     rng = random.Random(0)
-    cases = [(512, 1, 40000, 4, 148), (512, 1, 5000, 2, 148), (32, 1, 40000, 6, 148),
+    cases = [(512, 1, 40000, 2, 148), (512, 1, 5000, 2, 148), (32, 1, 40000, 6, 148),
              (6, 3, 3000, 2, 148), (48, 1, 3000, 8, 148), (1613, 1, 64, 5, 148),
              (2, 3, 17, 4, 148), (3, 1, 1, 1, 148), (5, 2, 0, 3, 148)]
     cases += [(rng.randint(1, 40), rng.choice([1, 2, 3, 4, 8]), rng.randint(0, 1500),
