@@ -52,17 +52,19 @@ struct alignas(16) MatParams {
 };
 
 // One warp per row, rows strided over a persistent grid; lane l holds
-// elements l + 32 j, j < D/32 (coalesced writes).  Butterfly stages on
-// element bits 0..4 exchange across lanes, stages on bits 5.. stay in
-// registers.  The lane's d values and the centroids are read from the
-// kernel parameters once per thread, into registers: indexing the
-// parameter bank with a lane-dependent index serialises the warp's access,
-// which on every row made this kernel several times slower than its
-// stores.
+// elements l + 32 j, j < D/32, for the transform (coalesced 128-byte kmse
+// stores).  A row's code and residual words are read once per row, one word
+// per lane, and broadcast with shuffles; the next row's words are loaded
+// before this row is processed, so the loads overlap the work.  The lane's
+// d values and the centroids come from the kernel parameters once per
+// thread (indexing the parameter bank with a lane-dependent index
+// serialises the warp).  Butterfly stages on element bits 0..4 exchange
+// across lanes, stages on bits 5.. stay in registers.
 template <int D, int NC>
 __global__ void __launch_bounds__(256)
     materialize_kernel(const __grid_constant__ MatParams P) {
   constexpr int J = D / 32;
+  constexpr int E = D / 32;  // bytes of idx / signs a lane writes per row
   constexpr int kWords = (NC == 2) ? D / 32 : D / 16;
   const int lane = threadIdx.x & 31;
   float dv[J];
@@ -72,35 +74,35 @@ __global__ void __launch_bounds__(256)
   const float c2 = NC == 4 ? P.cb.c[2] : 0.f, c3 = NC == 4 ? P.cb.c[3] : 0.f;
   const float inv_sqrt_d = 1.0f / sqrtf((float)D);
   const int64_t warps = (int64_t)gridDim.x * (blockDim.x / 32);
-  for (int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
-       row < P.n_rows; row += warps) {  // uniform per warp
-    const uint32_t* cw = P.code + row * kWords;
-    uint32_t idx[J];
-    float r[J];
-#pragma unroll
-    for (int j = 0; j < J; ++j) {
-      const int e = lane + 32 * j;
-      if (NC == 2) {
-        idx[j] = (__ldg(cw + (e >> 5)) >> (e & 31)) & 1u;
-        r[j] = idx[j] ? c1 : c0;
-      } else {
-        idx[j] = (__ldg(cw + (e >> 4)) >> (2 * (e & 15))) & 3u;
-        r[j] = idx[j] < 2 ? (idx[j] ? c1 : c0) : (idx[j] == 2 ? c2 : c3);
-      }
+  const bool want_res = P.signs != nullptr;
+  const bool want_norm = P.kmse != nullptr;
+  int64_t row = (int64_t)blockIdx.x * (blockDim.x / 32) + (threadIdx.x >> 5);
+  uint32_t cw = 0, rw = 0;  // lane l: word l of the row's code / residual plane
+  float nrm = 0.f;
+  auto load = [&](int64_t r) {
+    if (r < P.n_rows) {
+      cw = lane < kWords ? __ldg(P.code + r * kWords + lane) : 0u;
+      rw = (want_res && lane < D / 32) ? __ldg(P.res + r * (D / 32) + lane) : 0u;
+      nrm = want_norm ? __ldg(P.norms + r) : 0.f;
     }
-    // idx and signs: lane l writes elements [E l, E (l + 1)), E = D / 32,
-    // as one 4- or 8-byte store (the kmse below keeps the butterfly's
-    // element-per-lane order, one coalesced 128-byte store per j)
-    constexpr int E = D / 32;
+  };
+  load(row);
+  for (; row < P.n_rows; row += warps) {  // uniform per warp
+    const uint32_t cwr = cw, rwr = rw;
+    const float nr = nrm;
+    load(row + warps);  // next row, in flight while this one is written
     if (P.idx) {
+      // lane l writes elements [E l, E (l + 1)) as one 4- or 8-byte store
       uint32_t w[E / 4];
       if (NC == 2) {
-        const uint32_t bits = (__ldg(cw + (E * lane >> 5)) >> ((E * lane) & 31)) & ((1u << E) - 1);
+        const uint32_t word = __shfl_sync(0xffffffffu, cwr, (E * lane) >> 5);
+        const uint32_t bits = (word >> ((E * lane) & 31)) & ((1u << E) - 1);
 #pragma unroll
         for (int h = 0; h < E / 4; ++h)  // 4 bits -> 4 bytes of 0 / 1 (no carries)
           w[h] = (((bits >> (4 * h)) & 0xFu) * 0x00204081u) & 0x01010101u;
       } else {
-        const uint32_t f = __ldg(cw + (E * lane >> 4)) >> (2 * ((E * lane) & 15));
+        const uint32_t word = __shfl_sync(0xffffffffu, cwr, (E * lane) >> 4);
+        const uint32_t f = word >> (2 * ((E * lane) & 15));
 #pragma unroll
         for (int h = 0; h < E / 4; ++h)
           w[h] = ((f >> (8 * h)) & 3u) | (((f >> (8 * h + 2)) & 3u) << 8) |
@@ -110,7 +112,32 @@ __global__ void __launch_bounds__(256)
       if constexpr (E == 4) *reinterpret_cast<uint32_t*>(dst) = w[0];
       else *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
     }
+    if (P.signs) {
+      const uint32_t word = __shfl_sync(0xffffffffu, rwr, (E * lane) >> 5);
+      const uint32_t bits = (word >> ((E * lane) & 31)) & ((1u << E) - 1);
+      uint32_t w[E / 4];
+#pragma unroll
+      for (int h = 0; h < E / 4; ++h) {
+        const uint32_t e = (((bits >> (4 * h)) & 0xFu) * 0x00204081u) & 0x01010101u;
+        w[h] = 0xFFFFFFFFu ^ (e * 0xFEu);  // per byte: bit 1 -> +1, bit 0 -> -1 (0xFF)
+      }
+      int8_t* dst = P.signs + row * D + E * lane;
+      if constexpr (E == 4) *reinterpret_cast<uint32_t*>(dst) = w[0];
+      else *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
+    }
     if (P.kmse) {
+      float r[J];
+#pragma unroll
+      for (int j = 0; j < J; ++j) {
+        if (NC == 2) {
+          const uint32_t word = __shfl_sync(0xffffffffu, cwr, j);
+          r[j] = ((word >> lane) & 1u) ? c1 : c0;
+        } else {
+          const uint32_t word = __shfl_sync(0xffffffffu, cwr, 2 * j + (lane >> 4));
+          const uint32_t idx = (word >> (2 * (lane & 15))) & 3u;
+          r[j] = idx < 2 ? (idx ? c1 : c0) : (idx == 2 ? c2 : c3);
+        }
+      }
 #pragma unroll
       for (int h = 1; h < 32; h <<= 1) {
 #pragma unroll
@@ -131,22 +158,9 @@ __global__ void __launch_bounds__(256)
         }
       }
       // k_mse = r * m_base * d, m_base = (1/sqrt(D)) * norm (KudaHitamCUDA.cu:142-148)
-      const float m_base = inv_sqrt_d * __ldg(P.norms + row);
+      const float m_base = inv_sqrt_d * nr;
 #pragma unroll
       for (int j = 0; j < J; ++j) P.kmse[row * D + lane + 32 * j] = r[j] * m_base * dv[j];
-    }
-    if (P.signs) {
-      const uint32_t* rw = P.res + row * (D / 32);
-      const uint32_t bits = (__ldg(rw + (E * lane >> 5)) >> ((E * lane) & 31)) & ((1u << E) - 1);
-      uint32_t w[E / 4];
-#pragma unroll
-      for (int h = 0; h < E / 4; ++h) {
-        const uint32_t e = (((bits >> (4 * h)) & 0xFu) * 0x00204081u) & 0x01010101u;
-        w[h] = 0xFFFFFFFFu ^ (e * 0xFEu);  // per byte: bit 1 -> +1, bit 0 -> -1 (0xFF)
-      }
-      int8_t* dst = P.signs + row * D + E * lane;
-      if constexpr (E == 4) *reinterpret_cast<uint32_t*>(dst) = w[0];
-      else *reinterpret_cast<uint2*>(dst) = make_uint2(w[0], w[1]);
     }
   }
 }
