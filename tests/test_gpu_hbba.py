@@ -9,8 +9,11 @@ Tolerances:
 * encoder: indices exact wherever the best level beats the second best by
   more than 1e-6 (ties may go either way, at most max(2, 1e-4 n)); norms
   1e-6 and residual norms 1e-5 relative; the fp16 residual transform within
-  2 fp16 ulps (its float input differs by summation order); bytes past the
-  row's indices zero;
+  2 fp16 ulps plus 2e-6 of the row's largest magnitude: the engine sums
+  ||x||^2 in float and the oracle in double, and a norm one float ulp apart
+  moves every element of the transform by up to ~2.5e-7 of the row's scale
+  (measured by nudging the oracle's norm), which is many fp16 ulps where an
+  element cancels to near zero; bytes past the row's indices zero;
 * scores through the packed-byte scorer: 1e-4 normwise against the
   oracle's scorer on the oracle's own encoding.
 """
@@ -128,7 +131,8 @@ def test_encoder_matches_oracle(dtype, D, hbba_layer):
     a = signs.cpu().numpy().astype(np.float32)[rows]
     b = ref["signs"].astype(np.float32)[rows]
     ulp = np.maximum(np.abs(b), 6.1e-5) * 2.0 ** -10
-    assert np.all(np.abs(a - b) <= 2 * ulp + 1e-7)
+    row_scale = np.abs(b).max(1, keepdims=True)
+    assert np.all(np.abs(a - b) <= 2 * ulp + 2e-6 * row_scale)
 
 
 def test_compressor_class_end_to_end_scores():
@@ -154,7 +158,7 @@ def test_compressor_class_end_to_end_scores():
     for h in range(4):
         kv = h // 2
         rows = slice(kv * S, (kv + 1) * S)
-        want = O.compat_score(q[0, h].half().cpu().numpy()[None], ref["packed"][rows][None],
+        want = O.compat_score(q[0, h].half().cpu().numpy(), ref["packed"][rows][None],
                               ref["signs"][rows][None], d, ref["norms"][rows][None],
                               ref["rnorms"][rows][None], c, True, 1 / math.sqrt(D))
         got_idx = _unpack(out["indices"][rows].cpu().numpy(), D, True)
