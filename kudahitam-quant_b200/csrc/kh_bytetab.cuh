@@ -125,6 +125,16 @@ __device__ __forceinline__ uint32_t tab_addr(uint32_t x, uint32_t slots) {
   return r;
 }
 
+// 2^x by the SFU's approximate base-2 exponential (ex2.approx.ftz: relative
+// error about 2^-22, -inf -> +0, results below 2^-126 flushed to zero).  The
+// softmax weights here are 2^(logit - running max) <= 1, where a flushed
+// weight is negligible against the row that set the max.
+__device__ __forceinline__ float ex2_approx(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // L2 eviction-priority policies (createpolicy) and loads that carry one.
 // Streams read once are loaded evict-first; values read again by the same
 // CTA later (decode's V norms, phase 1 then phase 2) evict-last, so the

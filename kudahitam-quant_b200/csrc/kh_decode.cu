@@ -698,18 +698,31 @@ struct RowKV {
 };
 
 
+// One segment's rows of the six arrays phase 1 reads, as bases at the
+// segment's first row: a row is then addressed by a 32-bit index (one
+// multiply-add per load instead of 64-bit index arithmetic).
+template <int D>
+struct SegK {
+  const uint32_t *code, *res;
+  const float *n, *rn, *vn, *vrn;
+  __device__ __forceinline__ SegK(const DecodeParams& P, int64_t row0)
+      : code(P.k_code + row0 * (D / 32)), res(P.k_res + row0 * (D / 32)),
+        n(P.k_norms + row0), rn(P.k_rnorms + row0), vn(P.v_norms + row0),
+        vrn(P.v_rnorms + row0) {}
+};
+
 // Phase-1 loads: K planes and norms are read once (evict-first); the V
 // norms are read again by phase 2 of the same segment (evict-last).
 template <int D>
-__device__ __forceinline__ void load_k_row(const DecodeParams& P, int64_t row, int wr, int bs,
+__device__ __forceinline__ void load_k_row(const SegK<D>& S, uint32_t i, int wr,
                                            uint64_t once, uint64_t again, RowKV<D>& a) {
-  constexpr int kW = D / 32;
-  load_plane_policy<D>(P.k_code + row * kW, wr, once, a.c);
-  load_plane_policy<D>(P.k_res + row * kW, wr, once, a.r);
-  a.n = ldg_policy(P.k_norms + row, once);
-  a.rn = ldg_policy(P.k_rnorms + row, once);
-  a.vn = ldg_policy(P.v_norms + row, again);
-  a.vrn = ldg_policy(P.v_rnorms + row, again);
+  constexpr uint32_t kW = D / 32;
+  load_plane_policy<D>(S.code + i * kW, wr, once, a.c);
+  load_plane_policy<D>(S.res + i * kW, wr, once, a.r);
+  a.n = ldg_policy(S.n + i, once);
+  a.rn = ldg_policy(S.rn + i, once);
+  a.vn = ldg_policy(S.vn + i, again);
+  a.vrn = ldg_policy(S.vrn + i, again);
 }
 
 template <int NT>
@@ -856,6 +869,10 @@ __global__ void __launch_bounds__(256, 2)
     const int n = (int)min((int64_t)C::kSeg, s1 - c0);
     const int64_t row0 = gk * P.seq_len + c0;
     const int nb = (n + NT * B - 1) / (NT * B);  // batches of B rows per thread
+    const uint32_t last = (uint32_t)n - 1;        // loads past the segment read this row
+    // half-row layout: this thread's logit of batch row k (= bi B + u) sits
+    // k (NT / 32) table rows below its first one
+    float* const lgt = reinterpret_cast<float*>(upper(t));
 
     // K table into entries 0..31 of every row
     build_byte_table<D>(reinterpret_cast<float*>(tabb), qt, t);
@@ -867,11 +884,12 @@ __global__ void __launch_bounds__(256, 2)
     float2 sums = make_float2(0.f, 0.f);
     {
       RowKV<D> a[C::kRing][B];
+      const SegK<D> seg(P, row0);
       auto load_batch = [&](RowKV<D>(&dst)[B], int bi) {
 #pragma unroll
         for (int u = 0; u < B; ++u) {
-          const int ii = t + (bi * B + u) * NT;
-          load_k_row<D>(P, row0 + (ii < n ? ii : 0), wr, bs, pol_once, pol_again, dst[u]);
+          const uint32_t ii = min((uint32_t)(t + (bi * B + u) * NT), last);
+          load_k_row<D>(seg, ii, wr, pol_once, pol_again, dst[u]);
         }
       };
       auto score_batch = [&](const RowKV<D>(&src)[B], int bi) {
@@ -895,21 +913,21 @@ __global__ void __launch_bounds__(256, 2)
                               inv_sqrt_d * (2.f * m.y - Q) * src[u].rn;
           const int ii = t + (bi * B + u) * NT;
           l2[u] = ii < n ? score * lscale : -INFINITY;
-          if (ii < n) {
-            if constexpr (C::kHalf)
-              *reinterpret_cast<float*>(upper(ii)) = l2[u];
-            else
-              lg[ii] = l2[u];
-          }
+          // every ii < nb B NT <= kSeg has a slot: rows past n store -inf,
+          // which phase 2 turns into a zero weight
+          if constexpr (C::kHalf)
+            lgt[(bi * B + u) * (NT / 32) * 64] = l2[u];
+          else
+            lg[ii] = l2[u];
           mb = fmaxf(mb, l2[u]);
         }
         if (mb > -INFINITY) {
-          const float sc = exp2f(mt - mb);  // 0 while mt is -inf
+          const float sc = ex2_approx(mt - mb);  // 0 while mt is -inf
           sums.x *= sc;
           sums.y *= sc;
 #pragma unroll
           for (int u = 0; u < B; ++u) {
-            const float p = exp2f(l2[u] - mb);  // 0 for rows past n
+            const float p = ex2_approx(l2[u] - mb);  // 0 for rows past n
             sums.x += p;
             sums.y += p * (src[u].vn * wa + src[u].vrn * wb);
           }
@@ -930,21 +948,24 @@ __global__ void __launch_bounds__(256, 2)
     // phase 2's first V rows, loaded now so that their latency overlaps the
     // block reductions below
     RowK<D> va[C::kRing][B];
+    const uint32_t* const vxs = vx + row0 * (D / 32);
+    const uint32_t* const vys = vy + row0 * (D / 32);
+    const float* const vxns = vxn + row0;
+    const float* const vyns = vyn + row0;
     auto load_vbatch = [&](RowK<D>(&dst)[B], int bi) {
 #pragma unroll
       for (int u = 0; u < B; ++u) {
-        const int ii = t + (bi * B + u) * NT;
-        const int64_t row = row0 + (ii < n ? ii : 0);
-        load_plane_policy<D>(vx + row * (D / 32), wr, pol_once, dst[u].c);
-        load_plane_policy<D>(vy + row * (D / 32), wr, pol_once, dst[u].r);
-        dst[u].n = ldg_policy(vxn + row, pol_once);
-        dst[u].rn = ldg_policy(vyn + row, pol_once);
+        const uint32_t ii = min((uint32_t)(t + (bi * B + u) * NT), last);
+        load_plane_policy<D>(vxs + ii * (uint32_t)(D / 32), wr, pol_once, dst[u].c);
+        load_plane_policy<D>(vys + ii * (uint32_t)(D / 32), wr, pol_once, dst[u].r);
+        dst[u].n = ldg_policy(vxns + ii, pol_once);
+        dst[u].rn = ldg_policy(vyns + ii, pol_once);
       }
     };
     static_for<C::kRing - 1>([&](auto jc) { load_vbatch(va[decltype(jc)::value], decltype(jc)::value); });
     const float m_seg = block_max<NT>(mt, red);  // also: phase-1 table reads done
     const float m_new = fmaxf(m_run, m_seg);
-    const float alpha = exp2f(m_run - m_new);  // 0 on the first segment
+    const float alpha = ex2_approx(m_run - m_new);  // 0 on the first segment
     m_run = m_new;
 
     // zero both histograms (D = 128: words 0..31 of every row, keeping the
@@ -958,7 +979,7 @@ __global__ void __launch_bounds__(256, 2)
       }
     }
     {
-      const float r = mt > -INFINITY ? exp2f(mt - m_new) : 0.f;
+      const float r = mt > -INFINITY ? ex2_approx(mt - m_new) : 0.f;
       sums.x *= r;
       sums.y *= r;
     }
@@ -976,14 +997,12 @@ __global__ void __launch_bounds__(256, 2)
       auto scatter_batch = [&](const RowK<D>(&src)[B], int bi) {
 #pragma unroll
         for (int u = 0; u < B; ++u) {
-          const int ii = t + (bi * B + u) * NT;
-          const bool ok = ii < n;
-          float l2;
+          float l2;  // -inf past n: weight 0
           if constexpr (C::kHalf)
-            l2 = *reinterpret_cast<const float*>(upper(ok ? ii : 0));
+            l2 = lgt[(bi * B + u) * (NT / 32) * 64];
           else
-            l2 = lg[ok ? ii : 0];
-          const float p = ok ? exp2f(l2 - m_new) : 0.f;
+            l2 = lg[t + (bi * B + u) * NT];
+          const float p = ex2_approx(l2 - m_new);
           const int fx = __float2int_rn(p * src[u].n * kx);
           const int fy = __float2int_rn(p * src[u].rn * ky);
           csum += (float)fx * cx + (float)fy * cy;
