@@ -899,10 +899,32 @@ def decode_timing(dev, args, world, q, pk, pv, dk, dv, c, S_loc, S_total,
         khdist.check_peer_timeout(dev)
         barrier(world)
         del ex
+        # the exchange fused into the partial kernel: its CTAs store their
+        # split records into every rank's buffer and merge the rows once all
+        # flags arrived (one kernel per step when the launch fits at once)
+        exf = khdist.PeerRecordExchange(R, D, device=dev, n_parts=n_splits)
+
+        def step_fused():
+            return khdist.decode_attention_seq_sharded(q, pk, pv, dk, dv, c, sm, n_splits,
+                                                       partials=buf, exchange=exf)
+
+        for _ in range(3):
+            step_fused()
+        torch.cuda.synchronize()
+        khdist.check_peer_timeout(dev)
+        barrier(world)
+        fms = max_over_ranks(statistics.median(time_loop(step_fused, n, stream)), world)
+        torch.cuda.synchronize()
+        khdist.check_peer_timeout(dev)
+        barrier(world)
+        del exf
         peer = {"us_per_step": pms * 1e3,
                 "note": "kh_decode_merge_to_peers + kh_decode_combine_from_peers (plain "
                         "stores to every rank's symmetric buffer, epoch flags) in place of "
-                        "merge + NCCL all-gather + combine"}
+                        "merge + NCCL all-gather + combine",
+                "fused_in_partial_us_per_step": fms * 1e3,
+                "fused_note": "kh_decode_partial_to_peers with out: the partial kernel stores "
+                              "its split records to every rank and merges the rows itself"}
     if bytes_per_row is None:
         bytes_per_row = 2 * (2 * D // 8 + 8)  # K and V: 2 one-bit planes + 2 norms each
     bytes_step = R * S_total * bytes_per_row  # whole job

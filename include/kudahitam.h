@@ -318,6 +318,46 @@ int kh_decode_combine_from_peers(const float* records, const uint32_t* flags, ui
                                  int64_t n_groups, int world, int head_dim,
                                  const float* d_v_host, float* out, void* stream);
 
+/* Sequence-sharded decode with the record exchange fused into the partial
+ * kernel itself (no counterpart in the reference; replaces
+ * kh_decode_partial_gqa + kh_decode_merge + an all-gather +
+ * kh_decode_combine_strided, or kh_decode_partial + the two calls above).
+ * Every rank holds a record buffer [world][n_groups * n_q][n_splits][D+2]
+ * and a flag array [world] (uint32, zero before the first call) that all
+ * ranks can address, and a local counter word (zero before the first call).
+ * kh_decode_partial_to_peers takes the arguments of kh_decode_partial_gqa
+ * except the partials view: each CTA stores its split records into slot
+ * [rank] of every rank's record buffer (peer_records[r], a host array of
+ * world device pointers; slots a group does not use are marked empty), and
+ * the last CTA stores epoch into slot [rank] of every rank's flag array.
+ * Only the table kernels (2-level codebook at D = 128 or 256, 4-level at
+ * D = 128) take this path: other requests return KH_ENOTSUP.
+ * With out != NULL the call also completes the step: once all world flags of
+ * this rank carry epoch, the world x n_splits records of each query row are
+ * merged into out[n_groups * n_q][D] with d_v_host applied (inside the same
+ * kernel when all its CTAs fit on the GPU at once, else by a second kernel
+ * on the stream).  With out == NULL, call kh_decode_combine_peer_records.
+ * kh_decode_combine_peer_records waits until all world local flags equal
+ * epoch and merges the world x n_parts records of each of the n_groups query
+ * rows into out[g][D] like kh_decode_combine (kh_decode_combine_from_peers is
+ * this call with n_parts = 1).  Its wait gives up after about a second, sets
+ * bit 2 of kh_device_error() and writes zeros.  epoch rules as above. */
+int kh_decode_partial_to_peers(const float* q, int64_t n_groups, int n_q, int head_dim,
+                               const uint32_t* k_code, const uint32_t* k_res,
+                               const float* k_norms, const float* k_rnorms,
+                               const uint32_t* v_code, const uint32_t* v_res,
+                               const float* v_norms, const float* v_rnorms,
+                               int64_t seq_len, int64_t seq_begin, int64_t seq_end,
+                               const float* d_k_host, const float* d_v_host,
+                               const float* centroids_host, int n_centroids,
+                               float sm_scale, int n_splits, float* const* peer_records,
+                               uint32_t* const* peer_flags, int rank, int world,
+                               uint32_t epoch, uint32_t* counter, float* out, void* stream);
+
+int kh_decode_combine_peer_records(const float* records, const uint32_t* flags, uint32_t epoch,
+                                   int64_t n_groups, int n_parts, int world, int head_dim,
+                                   const float* d_v_host, float* out, void* stream);
+
 int kh_decode_attn(const float* q, int64_t n_groups, int head_dim,
                    const uint32_t* k_code, const uint32_t* k_res,
                    const float* k_norms, const float* k_rnorms,

@@ -358,7 +358,19 @@ int64_t kh_decode_workspace_bytes(int64_t n_groups, int n_splits,
   return n_groups * (int64_t)n_splits * (head_dim + 2) * (int64_t)sizeof(float);
 }
 
-int kh_decode_partial_gqa(const float* q, int64_t n_groups, int n_q, int head_dim,
+// The checks and request of kh_decode_partial_gqa and, with `peers`, of
+// kh_decode_partial_to_peers (records to every rank's buffer instead of
+// `partials`).
+struct PeerTarget {
+  float* const* records;
+  uint32_t* const* flags;
+  int rank, world;
+  uint32_t epoch;
+  uint32_t* counter;
+  float* out;
+};
+
+static int decode_partial_impl(const float* q, int64_t n_groups, int n_q, int head_dim,
                           const uint32_t* k_code, const uint32_t* k_res,
                           const float* k_norms, const float* k_rnorms,
                           const uint32_t* v_code, const uint32_t* v_res,
@@ -367,27 +379,43 @@ int kh_decode_partial_gqa(const float* q, int64_t n_groups, int n_q, int head_di
                           const float* d_k_host, const float* d_v_host,
                           const float* centroids_host, int n_centroids,
                           float sm_scale, int n_splits, float* partials,
-                          int64_t part_stride, int64_t part_offset, void* stream) {
+                          int64_t part_stride, int64_t part_offset, const PeerTarget* peers,
+                          void* stream) {
   (void)d_v_host;  // V's diagonal is applied by the combine step
   if (n_groups < 0 || n_q < 1 || !valid_head_dim(head_dim)) return KH_EINVAL;
   if (n_groups * (int64_t)n_q >= 65536) return KH_EINVAL;  // grid.y limit
   if (n_splits < 1 || n_splits > 65535) return KH_EINVAL;
   if (seq_len < 0 || seq_begin < 0 || seq_end < seq_begin || seq_end > seq_len)
     return KH_EINVAL;
-  if (part_offset < 0 || part_stride < part_offset + n_splits) return KH_EINVAL;
+  if (!peers && (part_offset < 0 || part_stride < part_offset + n_splits)) return KH_EINVAL;
+  if (peers) {
+    if (peers->world < 1 || peers->world > 8 || peers->rank < 0 || peers->rank >= peers->world ||
+        peers->epoch == 0)
+      return KH_EINVAL;
+    if (!peers->records || !peers->flags || !peers->counter) return KH_EINVAL;
+    for (int p = 0; p < peers->world; ++p) {
+      if (!peers->records[p] || !peers->flags[p]) return KH_EINVAL;
+      if (!aligned4(peers->records[p]) || !aligned4(peers->flags[p])) return KH_EALIGN;
+    }
+    if (!aligned4(peers->counter)) return KH_EALIGN;
+    if (peers->out) {
+      if (!aligned4(peers->out)) return KH_EALIGN;
+      if (!check_d(d_v_host, head_dim)) return KH_EINVAL;
+    }
+  }
   if (!std::isfinite(sm_scale)) return KH_EINVAL;
   DecodeRequest r;
   memset(&r, 0, sizeof(r));
   if (!make_codebook(centroids_host, n_centroids, &r.cb)) return KH_EINVAL;
   if (!check_d(d_k_host, head_dim)) return KH_EINVAL;
   if (n_groups == 0) return KH_OK;
-  if (!q || !partials) return KH_EINVAL;
+  if (!q || (!partials && !peers)) return KH_EINVAL;
   if (seq_end > seq_begin &&
       (!k_code || !k_res || !k_norms || !k_rnorms || !v_code || !v_res ||
        !v_norms || !v_rnorms))
     return KH_EINVAL;
   if (!aligned16(k_code) || !aligned16(k_res) || !aligned16(v_code) ||
-      !aligned16(v_res) || !aligned4(q) || !aligned4(partials))
+      !aligned16(v_res) || !aligned4(q) || (!peers && !aligned4(partials)))
     return KH_EALIGN;
   for (int i = 0; i < head_dim; ++i) r.dk[i] = d_k_host[i];
   r.q = q;
@@ -402,7 +430,52 @@ int kh_decode_partial_gqa(const float* q, int64_t n_groups, int n_q, int head_di
   r.partials = partials;
   r.part_stride = part_stride;
   r.part_offset = part_offset;
+  if (peers) {
+    r.world = peers->world;
+    r.rank = peers->rank;
+    r.epoch = peers->epoch;
+    r.counter = peers->counter;
+    r.peer_records = peers->records;
+    r.peer_flags = peers->flags;
+    r.out = peers->out;
+    if (peers->out)
+      for (int i = 0; i < head_dim; ++i) r.dv[i] = d_v_host[i];
+  }
   return launch_decode_partial(r, static_cast<cudaStream_t>(stream));
+}
+
+int kh_decode_partial_gqa(const float* q, int64_t n_groups, int n_q, int head_dim,
+                          const uint32_t* k_code, const uint32_t* k_res,
+                          const float* k_norms, const float* k_rnorms,
+                          const uint32_t* v_code, const uint32_t* v_res,
+                          const float* v_norms, const float* v_rnorms,
+                          int64_t seq_len, int64_t seq_begin, int64_t seq_end,
+                          const float* d_k_host, const float* d_v_host,
+                          const float* centroids_host, int n_centroids,
+                          float sm_scale, int n_splits, float* partials,
+                          int64_t part_stride, int64_t part_offset, void* stream) {
+  return decode_partial_impl(q, n_groups, n_q, head_dim, k_code, k_res, k_norms, k_rnorms,
+                             v_code, v_res, v_norms, v_rnorms, seq_len, seq_begin, seq_end,
+                             d_k_host, d_v_host, centroids_host, n_centroids, sm_scale, n_splits,
+                             partials, part_stride, part_offset, nullptr, stream);
+}
+
+int kh_decode_partial_to_peers(const float* q, int64_t n_groups, int n_q, int head_dim,
+                               const uint32_t* k_code, const uint32_t* k_res,
+                               const float* k_norms, const float* k_rnorms,
+                               const uint32_t* v_code, const uint32_t* v_res,
+                               const float* v_norms, const float* v_rnorms,
+                               int64_t seq_len, int64_t seq_begin, int64_t seq_end,
+                               const float* d_k_host, const float* d_v_host,
+                               const float* centroids_host, int n_centroids,
+                               float sm_scale, int n_splits, float* const* peer_records,
+                               uint32_t* const* peer_flags, int rank, int world,
+                               uint32_t epoch, uint32_t* counter, float* out, void* stream) {
+  const PeerTarget pt{peer_records, peer_flags, rank, world, epoch, counter, out};
+  return decode_partial_impl(q, n_groups, n_q, head_dim, k_code, k_res, k_norms, k_rnorms,
+                             v_code, v_res, v_norms, v_rnorms, seq_len, seq_begin, seq_end,
+                             d_k_host, d_v_host, centroids_host, n_centroids, sm_scale, n_splits,
+                             nullptr, n_splits, 0, &pt, stream);
 }
 
 int kh_decode_partial(const float* q, int64_t n_groups, int head_dim,
@@ -477,17 +550,26 @@ int kh_decode_merge_to_peers(const float* partials, int64_t n_groups, int n_part
                                       counter, static_cast<cudaStream_t>(stream));
 }
 
-int kh_decode_combine_from_peers(const float* records, const uint32_t* flags, uint32_t epoch,
-                                 int64_t n_groups, int world, int head_dim,
-                                 const float* d_v_host, float* out, void* stream) {
-  if (n_groups < 0 || world < 1 || world > 8 || epoch == 0 || !valid_head_dim(head_dim))
+int kh_decode_combine_peer_records(const float* records, const uint32_t* flags, uint32_t epoch,
+                                   int64_t n_groups, int n_parts, int world, int head_dim,
+                                   const float* d_v_host, float* out, void* stream) {
+  if (n_groups < 0 || n_parts < 1 || world < 1 || world > 8 || epoch == 0 ||
+      !valid_head_dim(head_dim))
     return KH_EINVAL;
   if (!check_d(d_v_host, head_dim)) return KH_EINVAL;
   if (n_groups == 0) return KH_OK;
   if (!records || !flags || !out) return KH_EINVAL;
   if (!aligned4(records) || !aligned4(flags) || !aligned4(out)) return KH_EALIGN;
-  return launch_decode_combine_from_peers(records, flags, epoch, n_groups, world, head_dim,
-                                          d_v_host, out, static_cast<cudaStream_t>(stream));
+  return launch_decode_combine_from_peers(records, flags, epoch, n_groups, n_parts, world,
+                                          head_dim, d_v_host, out,
+                                          static_cast<cudaStream_t>(stream));
+}
+
+int kh_decode_combine_from_peers(const float* records, const uint32_t* flags, uint32_t epoch,
+                                 int64_t n_groups, int world, int head_dim,
+                                 const float* d_v_host, float* out, void* stream) {
+  return kh_decode_combine_peer_records(records, flags, epoch, n_groups, 1, world, head_dim,
+                                        d_v_host, out, stream);
 }
 
 int kh_compress_hbba(const void* x, int dtype, int64_t n_rows, int head_dim,

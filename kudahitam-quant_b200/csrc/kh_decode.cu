@@ -27,6 +27,20 @@
 namespace kh {
 namespace {
 
+constexpr int kMaxPeers = 8;
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_relaxed_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.relaxed.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void fence_acq_rel_sys() {
+  asm volatile("fence.acq_rel.sys;" ::: "memory");
+}
+
 struct alignas(16) DecodeParams {
   const float* q;
   const uint32_t *k_code, *k_res, *v_code, *v_res;
@@ -43,8 +57,177 @@ struct alignas(16) DecodeParams {
   // sequence row), set = b / n_q; W = 0: the sequence range is empty
   int64_t W;
   int64_t n_groups_kv;
+  // peer mode (world > 0): records go to slot [rank] of every rank's buffer
+  // [world][n_rows_q][n_splits][D+2] instead of `partials`; the last CTA
+  // raises epoch in slot [rank] of every rank's flag array
+  int world, rank;
+  uint32_t epoch;
+  uint32_t* counter;
+  int64_t n_rows_q;
+  float* peer_rec[kMaxPeers];
+  uint32_t* peer_flag[kMaxPeers];
+  // peer mode with the combine fused (fuse = 1; every CTA of the launch is
+  // resident at once): after the count-out, every CTA waits for all ranks'
+  // flags and merges its share of the query rows into out
+  int fuse;
+  float* out;
+  uint32_t* err;
   float dk[256];
+  float dv[256];
 };
+
+// Record (m, l, acc) of query row g, slot p: into the caller's partials, or
+// in peer mode into this rank's slot of every rank's record buffer.  Thread
+// t < D writes acc[t] (when with_acc), thread 0 writes m and l.
+template <int D>
+__device__ __forceinline__ void put_record(const DecodeParams& P, int64_t g, int64_t p, int t,
+                                           float m, float l, float a, bool with_acc) {
+  if (P.world == 0) {
+    float* rec = P.partials + (g * P.part_stride + P.part_offset + p) * (D + 2);
+    if (with_acc && t < D) rec[2 + t] = a;
+    if (t == 0) {
+      rec[0] = m;
+      rec[1] = l;
+    }
+    return;
+  }
+  const int64_t off = (((int64_t)P.rank * P.n_rows_q + g) * P.n_splits + p) * (D + 2);
+  for (int r = 0; r < P.world; ++r) {
+    float* rec = P.peer_rec[r] + off;
+    if (with_acc && t < D) rec[2 + t] = a;
+    if (t == 0) {
+      rec[0] = m;
+      rec[1] = l;
+    }
+  }
+}
+
+// Peer mode, once per CTA after its last record: every thread fences its
+// peer stores at system scope before the CTA's count; the last CTA to count
+// raises this call's epoch in every rank's flag array.
+__device__ __forceinline__ void peers_count_out(const DecodeParams& P) {
+  if (P.world == 0) return;
+  __threadfence_system();
+  __syncthreads();
+  if (threadIdx.x == 0) {
+    if (atomicAdd(P.counter, 1u) == gridDim.x - 1) {
+      atomicExch(P.counter, 0u);  // ready for the next call
+      __threadfence_system();
+      for (int r = 0; r < P.world; ++r) st_release_sys(P.peer_flag[r] + P.rank, P.epoch);
+    }
+  }
+}
+
+// Called by one warp: lane r < world polls rank r's flag (relaxed) until it
+// carries epoch, all flags at once; one acquire fence by lane 0 after the
+// last one arrived orders the record reads that follow a CTA barrier.  Each
+// wait gives up after about a second (2^31 cycles) and reports false; lane 0
+// then sets the peer-timeout bit of the error word.
+__device__ __forceinline__ bool wait_peer_flags(const uint32_t* flags, int world,
+                                                uint32_t epoch, uint32_t* err, int lane) {
+  bool good = true;
+  if (lane < world) {
+    const long long t0 = clock64();
+    while (ld_relaxed_sys(flags + lane) != epoch) {
+      if (clock64() - t0 > (1ll << 31)) {
+        good = false;
+        break;
+      }
+    }
+  }
+  const bool all = __all_sync(0xffffffffu, good);
+  if (lane == 0) {
+    if (!all) flag_error(err, kErrPeerTimeout);
+    fence_acq_rel_sys();
+  }
+  __syncwarp();
+  return all;
+}
+
+// One warp merges the world x n_parts records of query row g (records
+// [world][n_rows][n_parts][D+2], in (rank, part) order) and writes
+// out[g] = d (.) H(acc) / l, or zeros when !ok.  Element lane + 32 j; the
+// transform runs stage by stage in the order of the other combine kernels.
+template <int D>
+__device__ __forceinline__ void combine_peer_row(const float* __restrict__ recs, int64_t n_rows,
+                                                 int n_parts, int world, int64_t g,
+                                                 const float* dvec, float* __restrict__ out,
+                                                 int lane, bool ok) {
+  constexpr int kJ = D / 32;
+  float* o = out + g * D;
+  if (!ok) {
+#pragma unroll
+    for (int j = 0; j < kJ; ++j) o[lane + 32 * j] = 0.f;
+    return;
+  }
+  // records arrived over NVLink into this GPU's L2: read them there
+  const int64_t rs = (int64_t)n_parts * (D + 2);  // one rank's records of a row
+  const int64_t ws = n_rows * rs;                  // one rank's block
+  const float* base = recs + g * rs;
+  float M = -INFINITY;
+  for (int r = 0; r < world; ++r)
+    for (int p = 0; p < n_parts; ++p) {
+      const float* rec = base + r * ws + (int64_t)p * (D + 2);
+      if (__ldcg(rec + 1) > 0.f) M = fmaxf(M, __ldcg(rec));
+    }
+  float L = 0.f, acc[kJ];
+#pragma unroll
+  for (int j = 0; j < kJ; ++j) acc[j] = 0.f;
+  for (int r = 0; r < world; ++r)
+    for (int p = 0; p < n_parts; ++p) {
+      const float* rec = base + r * ws + (int64_t)p * (D + 2);
+      const float l = __ldcg(rec + 1);
+      if (l > 0.f) {
+        const float e = expf(__ldcg(rec) - M);
+        L += l * e;
+#pragma unroll
+        for (int j = 0; j < kJ; ++j) acc[j] += __ldcg(rec + 2 + lane + 32 * j) * e;
+      }
+    }
+#pragma unroll
+  for (int h = 1; h < 32; h <<= 1)
+#pragma unroll
+    for (int j = 0; j < kJ; ++j) {
+      const float x = __shfl_xor_sync(0xffffffffu, acc[j], h);
+      acc[j] = (lane & h) ? (x - acc[j]) : (acc[j] + x);
+    }
+#pragma unroll
+  for (int h = 1; h < kJ; h <<= 1)
+#pragma unroll
+    for (int j = 0; j < kJ; ++j)
+      if ((j & h) == 0) {
+        const float x = acc[j], y = acc[j + h];
+        acc[j] = x + y;
+        acc[j + h] = x - y;
+      }
+#pragma unroll
+  for (int j = 0; j < kJ; ++j)
+    o[lane + 32 * j] = L > 0.f ? acc[j] * dvec[lane + 32 * j] / L : 0.f;
+}
+
+// End of a partial kernel in peer mode: count out (the last CTA raises the
+// flags); with the combine fused, every CTA then waits for all ranks' flags
+// and its warps merge query rows blockIdx.x * warps + w, stepping by the
+// grid's warps.  Every CTA of the launch must reach this point.
+template <int D>
+__device__ __forceinline__ void peers_finish(const DecodeParams& P) {
+  if (P.world == 0) return;
+  peers_count_out(P);
+  if (!P.fuse) return;
+  __shared__ int s_ok;
+  const int t = threadIdx.x;
+  if (t < 32) {
+    const bool all = wait_peer_flags(P.peer_flag[P.rank], P.world, P.epoch, P.err, t);
+    if (t == 0) s_ok = all ? 1 : 0;
+  }
+  __syncthreads();
+  const bool ok = s_ok != 0;
+  const int warps = blockDim.x / 32;
+  for (int64_t g = (int64_t)blockIdx.x * warps + (t >> 5); g < P.n_rows_q;
+       g += (int64_t)gridDim.x * warps)
+    combine_peer_row<D>(P.peer_rec[P.rank], P.n_rows_q, P.n_splits, P.world, g, P.dv, P.out,
+                        t & 31, ok);
+}
 
 template <int D>
 __device__ __forceinline__ float block_reduce(float v, float* red, bool is_max) {
@@ -250,21 +433,10 @@ __global__ void __launch_bounds__(D)
 // raises this call's epoch in slot [rank] of every rank's flag array.  The
 // combine kernel waits (bounded) until all world flags carry the epoch, then
 // merges the world records of its row from local memory.
-constexpr int kMaxPeers = 8;
-
 struct PeerParams {
   float* rec[kMaxPeers];     // rank r's record buffer [world][n_rows][D+2]
   uint32_t* flag[kMaxPeers]; // rank r's flag array [world]
 };
-
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
 
 template <int D>
 __global__ void __launch_bounds__(D)
@@ -310,65 +482,28 @@ __global__ void __launch_bounds__(D)
   }
 }
 
+// Combine step of the peer exchange: waits (bounded) until all world flags
+// carry epoch, then merges the world x n_parts records of each query row
+// (records [world][n_rows][n_parts][D+2], stored into this GPU's memory by
+// the ranks' merge or partial kernels) and writes out[g] = d (.) H(acc) / l.
+// One warp per row, eight rows per CTA; lane r of warp 0 polls rank r's flag.
+// The records are merged in (rank, part) order and the transform runs stage
+// by stage in the order of the other combine kernels.
 template <int D>
-__global__ void __launch_bounds__(D)
-    decode_combine_from_peers_kernel(const float* __restrict__ recs, const uint32_t* flags,
-                                     uint32_t epoch, int64_t n_rows, int world,
-                                     float* __restrict__ out, uint32_t* err,
-                                     const __grid_constant__ DecodeParams P) {
-  __shared__ float sh[D];
+__global__ void __launch_bounds__(256)
+    decode_combine_peer_records_kernel(const float* __restrict__ recs, const uint32_t* flags,
+                                       uint32_t epoch, int64_t n_rows, int n_parts, int world,
+                                       float* __restrict__ out, uint32_t* err,
+                                       const __grid_constant__ DecodeParams P) {
   __shared__ int ok;
   const int t = threadIdx.x;
-  const int64_t g = blockIdx.x;
-  if (t == 0) {
-    int good = 1;
-    const long long t0 = clock64();
-    for (int r = 0; r < world && good; ++r) {
-      while (ld_acquire_sys(flags + r) != epoch) {
-        if (clock64() - t0 > (1ll << 31)) {  // about a second: give up
-          flag_error(err, kErrPeerTimeout);
-          good = 0;
-          break;
-        }
-      }
-    }
-    ok = good;
+  if (t < 32) {
+    const bool all = wait_peer_flags(flags, world, epoch, err, t);
+    if (t == 0) ok = all ? 1 : 0;
   }
   __syncthreads();
-  if (!ok) {
-    out[g * D + t] = 0.f;
-    return;
-  }
-  // peers' records arrived over NVLink into this GPU's L2: read them there
-  const int64_t ps = n_rows * (D + 2);
-  const float* base = recs + g * (D + 2);
-  float M = -INFINITY;
-  for (int r = 0; r < world; ++r) {
-    const float* rec = base + (int64_t)r * ps;
-    if (__ldcg(rec + 1) > 0.f) M = fmaxf(M, __ldcg(rec));
-  }
-  float L = 0.f, a = 0.f;
-  for (int r = 0; r < world; ++r) {
-    const float* rec = base + (int64_t)r * ps;
-    const float l = __ldcg(rec + 1);
-    if (l > 0.f) {
-      const float e = expf(__ldcg(rec) - M);
-      L += l * e;
-      a += __ldcg(rec + 2 + t) * e;
-    }
-  }
-  sh[t] = a;
-  __syncthreads();
-  for (int h = 1; h < D; h <<= 1) {
-    if (t < D / 2) {
-      const int lo = (t / h) * 2 * h + (t % h);
-      const float x = sh[lo], y = sh[lo + h];
-      sh[lo] = x + y;
-      sh[lo + h] = x - y;
-    }
-    __syncthreads();
-  }
-  out[g * D + t] = L > 0.f ? sh[t] * P.dk[t] / L : 0.f;
+  const int64_t g = (int64_t)blockIdx.x * 8 + (t >> 5);
+  if (g < n_rows) combine_peer_row<D>(recs, n_rows, n_parts, world, g, P.dk, out, t & 31, ok != 0);
 }
 
 // ---------------------------------------------------------------------------
@@ -825,12 +960,9 @@ __global__ void __launch_bounds__(256, 2)
   const int64_t L = P.seq_end - P.seq_begin;
   if (P.W == 0) {  // empty range: every record of query row blockIdx.x is empty
     if (t == 0)
-      for (int p = 0; p < P.n_splits; ++p) {
-        float* e = P.partials +
-                   ((int64_t)blockIdx.x * P.part_stride + P.part_offset + p) * (D + 2);
-        e[0] = -INFINITY;
-        e[1] = 0.f;
-      }
+      for (int p = 0; p < P.n_splits; ++p)
+        put_record<D>(P, blockIdx.x, p, 0, -INFINITY, 0.f, 0.f, false);
+    peers_finish<D>(P);
     return;
   }
   const int jq = (int)(blockIdx.x % (unsigned)P.n_q);
@@ -1114,23 +1246,15 @@ __global__ void __launch_bounds__(256, 2)
     __syncthreads();  // fold reads done before the next segment's table
   }
 
-  if (rpart < P.n_splits) {  // the host sizes W so that it always is
-    float* rec = P.partials + (g * P.part_stride + P.part_offset + rpart) * (D + 2);
-    if (t < D) rec[2 + t] = c_run + acc;
-    if (t == 0) {
-      rec[0] = m_run * kLn2;  // natural-log units for the combine step
-      rec[1] = l_run;
-    }
-  }
-  if (s1 == P.seq_end && t == 0) {  // this set ends the group: empty the unused slots
-    for (int64_t p = rpart + 1; p < P.n_splits; ++p) {
-      float* e = P.partials + (g * P.part_stride + P.part_offset + p) * (D + 2);
-      e[0] = -INFINITY;
-      e[1] = 0.f;
-    }
-  }
+  if (rpart < P.n_splits)  // the host sizes W so that it always is
+    // m in natural-log units for the combine step
+    put_record<D>(P, g, rpart, t, m_run * kLn2, l_run, c_run + acc, true);
+  if (s1 == P.seq_end && t == 0)  // this set ends the group: empty the unused slots
+    for (int64_t p = rpart + 1; p < P.n_splits; ++p)
+      put_record<D>(P, g, p, 0, -INFINITY, 0.f, 0.f, false);
   __syncthreads();  // q~ and the reduction scratch are rewritten by the next piece
   }
+  peers_finish<D>(P);
 }
 
 // ---------------------------------------------------------------------------
@@ -1222,12 +1346,9 @@ __global__ void __launch_bounds__(256, 2)
   const int64_t L = P.seq_end - P.seq_begin;
   if (P.W == 0) {
     if (t == 0)
-      for (int p = 0; p < P.n_splits; ++p) {
-        float* e = P.partials +
-                   ((int64_t)blockIdx.x * P.part_stride + P.part_offset + p) * (D + 2);
-        e[0] = -INFINITY;
-        e[1] = 0.f;
-      }
+      for (int p = 0; p < P.n_splits; ++p)
+        put_record<D>(P, blockIdx.x, p, 0, -INFINITY, 0.f, 0.f, false);
+    peers_finish<D>(P);
     return;
   }
   const int jq = (int)(blockIdx.x % (unsigned)P.n_q);
@@ -1481,23 +1602,14 @@ __global__ void __launch_bounds__(256, 2)
       __syncthreads();  // fold reads done before the next segment's table and logits
     }
 
-    if (rpart < P.n_splits) {
-      float* rec = P.partials + (g * P.part_stride + P.part_offset + rpart) * (D + 2);
-      if (t < D) rec[2 + t] = c_run + acc;
-      if (t == 0) {
-        rec[0] = m_run * kLn2;  // natural-log units for the combine step
-        rec[1] = l_run;
-      }
-    }
-    if (s1 == P.seq_end && t == 0) {
-      for (int64_t p = rpart + 1; p < P.n_splits; ++p) {
-        float* e = P.partials + (g * P.part_stride + P.part_offset + p) * (D + 2);
-        e[0] = -INFINITY;
-        e[1] = 0.f;
-      }
-    }
+    if (rpart < P.n_splits)  // m in natural-log units for the combine step
+      put_record<D>(P, g, rpart, t, m_run * kLn2, l_run, c_run + acc, true);
+    if (s1 == P.seq_end && t == 0)
+      for (int64_t p = rpart + 1; p < P.n_splits; ++p)
+        put_record<D>(P, g, p, 0, -INFINITY, 0.f, 0.f, false);
     __syncthreads();
   }
+  peers_finish<D>(P);
 }
 
 }  // namespace
@@ -1519,6 +1631,21 @@ kh_status launch_decode_partial(const DecodeRequest& r, cudaStream_t stream) {
   P.c1 = r.cb.c[1];
   for (int i = 0; i < 4; ++i) P.cb[i] = r.cb.c[i];
   for (int i = 0; i < r.D; ++i) P.dk[i] = r.dk[i];
+  P.world = r.world;
+  if (r.world > 0) {
+    if (r.world > kMaxPeers) return KH_EINVAL;
+    P.out = r.out;
+    P.err = device_error_ptr();
+    for (int i = 0; i < r.D; ++i) P.dv[i] = r.dv[i];
+    P.rank = r.rank;
+    P.epoch = r.epoch;
+    P.counter = r.counter;
+    P.n_rows_q = r.n_groups * r.n_q;
+    for (int i = 0; i < r.world; ++i) {
+      P.peer_rec[i] = r.peer_records[i];
+      P.peer_flag[i] = r.peer_flags[i];
+    }
+  }
   const dim3 grid((unsigned)r.n_splits, (unsigned)(r.n_groups * r.n_q));
   const char* env = getenv("KUDAHITAM_DECODE_PATH");
   int path = (env && strcmp(env, "v1") == 0) ? 1 : (env && strcmp(env, "v2") == 0) ? 2 : 3;
@@ -1551,6 +1678,7 @@ kh_status launch_decode_partial(const DecodeRequest& r, cudaStream_t stream) {
     n_cta = (total + P.W - 1) / P.W * r.n_q;
   }
   if (n_cta > 0x7fffffff) return KH_EINVAL;
+  if (r.world > 0 && path < 3) return KH_ENOTSUP;  // peer mode: table kernels only
   const dim3 grid3((unsigned)n_cta);
   if (path == 1) {
     if (r.cb.n_c == 4) {
@@ -1565,10 +1693,21 @@ kh_status launch_decode_partial(const DecodeRequest& r, cudaStream_t stream) {
     int dev = 0;
     if (cudaGetDevice(&dev) != cudaSuccess) return KH_ECUDA;
     static std::once_flag once[5][64];
+    static int resident[5][64];  // CTAs of the kernel one SM holds at once
     auto launch = [&](auto kern, int slot, int smem, int threads) {
       std::call_once(once[slot][dev & 63], [&] {
         cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        int nb = 0;
+        if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&nb, kern, threads, smem) !=
+            cudaSuccess)
+          nb = 0;
+        resident[slot][dev & 63] = nb;
       });
+      // the combine is fused only when every CTA of the launch is resident at
+      // once (the CTAs wait for each other's flag); else it runs as a
+      // separate kernel after this one
+      P.fuse = (r.world > 0 && r.out &&
+                n_cta <= (int64_t)resident[slot][dev & 63] * sm_count()) ? 1 : 0;
       if (path == 3)  // v3 waits for the previous kernel before its first read
         launch_programmatic(kern, grid3, dim3(threads), smem, stream, P);
       else
@@ -1584,7 +1723,12 @@ kh_status launch_decode_partial(const DecodeRequest& r, cudaStream_t stream) {
       else launch(decode_v3_kernel<256>, 3, V3Cfg<256>::kSmem, V3Cfg<256>::kThreads);
     }
   }
-  return cudaGetLastError() == cudaSuccess ? KH_OK : KH_ELAUNCH;
+  if (cudaGetLastError() != cudaSuccess) return KH_ELAUNCH;
+  if (r.world > 0 && r.out && !P.fuse)
+    return launch_decode_combine_from_peers(P.peer_rec[r.rank], P.peer_flag[r.rank], r.epoch,
+                                            r.n_groups * r.n_q, r.n_splits, r.world, r.D, r.dv,
+                                            r.out, stream);
+  return KH_OK;
 }
 
 kh_status launch_decode_combine(const float* partials, int64_t n_groups, int n_parts,
@@ -1634,20 +1778,21 @@ kh_status launch_decode_merge_to_peers(const float* partials, int64_t n_rows, in
 }
 
 kh_status launch_decode_combine_from_peers(const float* records, const uint32_t* flags,
-                                           uint32_t epoch, int64_t n_rows, int world, int D,
-                                           const float* dv, float* out, cudaStream_t stream) {
-  if (world < 1 || world > kMaxPeers || n_rows > 0x7fffffff) return KH_EINVAL;
+                                           uint32_t epoch, int64_t n_rows, int n_parts,
+                                           int world, int D, const float* dv, float* out,
+                                           cudaStream_t stream) {
+  if (world < 1 || world > kMaxPeers || n_parts < 1 || n_rows > 0x3ffffffffll) return KH_EINVAL;
   DecodeParams P;
   memset(&P, 0, sizeof(P));
   for (int i = 0; i < D; ++i) P.dk[i] = dv[i];
-  const dim3 grid((unsigned)n_rows);
+  const dim3 grid((unsigned)((n_rows + 7) / 8));
   uint32_t* err = device_error_ptr();
   if (D == 128)
-    decode_combine_from_peers_kernel<128><<<grid, 128, 0, stream>>>(records, flags, epoch, n_rows,
-                                                                    world, out, err, P);
+    decode_combine_peer_records_kernel<128><<<grid, 256, 0, stream>>>(
+        records, flags, epoch, n_rows, n_parts, world, out, err, P);
   else
-    decode_combine_from_peers_kernel<256><<<grid, 256, 0, stream>>>(records, flags, epoch, n_rows,
-                                                                    world, out, err, P);
+    decode_combine_peer_records_kernel<256><<<grid, 256, 0, stream>>>(
+        records, flags, epoch, n_rows, n_parts, world, out, err, P);
   return cudaGetLastError() == cudaSuccess ? KH_OK : KH_ELAUNCH;
 }
 

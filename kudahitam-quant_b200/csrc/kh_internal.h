@@ -90,6 +90,16 @@ struct DecodeRequest {
   int n_q = 1;  // queries per cache group; q and partials have n_groups * n_q rows
   float* partials;
   int64_t part_stride, part_offset;
+  // peer mode (world > 0): records to every rank's buffer, flags raised
+  int world = 0, rank = 0;
+  uint32_t epoch = 0;
+  uint32_t* counter = nullptr;
+  float* const* peer_records = nullptr;
+  uint32_t* const* peer_flags = nullptr;
+  // peer mode: out != nullptr also merges every rank's records into out
+  // [n_groups * n_q][D] (V's diagonal dv) once all flags arrived
+  float* out = nullptr;
+  float dv[256];
 };
 
 kh_status launch_decode_partial(const DecodeRequest& r, cudaStream_t stream);
@@ -108,8 +118,9 @@ kh_status launch_decode_merge_to_peers(const float* partials, int64_t n_rows, in
                                       int rank, int world, uint32_t epoch, uint32_t* counter,
                                       cudaStream_t stream);
 kh_status launch_decode_combine_from_peers(const float* records, const uint32_t* flags,
-                                           uint32_t epoch, int64_t n_rows, int world, int D,
-                                           const float* dv, float* out, cudaStream_t stream);
+                                           uint32_t epoch, int64_t n_rows, int n_parts,
+                                           int world, int D, const float* dv, float* out,
+                                           cudaStream_t stream);
 
 // HBBA encoder and calibrator (kh_hbba.cu).  d, cent, mask and n_map are
 // device arrays, as in the reference binding.

@@ -351,6 +351,63 @@ void decode_partial(const Tensor& q, const Tensor& kc, const Tensor& kr, const T
         "kh_decode_partial_gqa");
 }
 
+// decode_partial with the records stored into slot [rank] of every rank's
+// record buffer (peer_records: device addresses, one per rank) and the
+// epoch raised in every rank's flag array (peer_flags) by the last CTA.
+void decode_partial_to_peers(const Tensor& q, const Tensor& kc, const Tensor& kr,
+                             const Tensor& kn, const Tensor& krn, const Tensor& vc,
+                             const Tensor& vr, const Tensor& vn, const Tensor& vrn,
+                             int64_t seq_len, int64_t seq_begin, int64_t seq_end,
+                             const Tensor& dk, const Tensor& c, double sm_scale, int64_t n_splits,
+                             c10::IntArrayRef peer_records, c10::IntArrayRef peer_flags,
+                             int64_t rank, int64_t epoch, const Tensor& counter,
+                             const c10::optional<Tensor>& dv, const c10::optional<Tensor>& out) {
+  require_cuda(q, "q");
+  TORCH_CHECK(q.scalar_type() == at::kFloat && q.is_contiguous() && (q.dim() == 2 || q.dim() == 3),
+              "q must be a contiguous float32 [G, D] or [G, n_q, D] tensor");
+  const int64_t G = q.size(0), nq = q.dim() == 3 ? q.size(1) : 1, D = q.size(-1);
+  const auto dev = q.device();
+  for (const Tensor* t : {&kc, &kr, &kn, &krn, &vc, &vr, &vn, &vrn}) check_buf(*t, dev, "cache");
+  const int64_t rows = kn.numel();
+  TORCH_CHECK(G * seq_len <= rows && vn.numel() == rows && krn.numel() == rows &&
+                  vrn.numel() == rows && kc.numel() == rows * code_words(D, bits_of(c)) &&
+                  vc.numel() == kc.numel() && kr.numel() == rows * (D / 32) &&
+                  vr.numel() == kr.numel(),
+              "K / V caches do not hold G * seq_len rows of head_dim ", D);
+  const size_t world = peer_records.size();
+  TORCH_CHECK(world >= 1 && world <= 8 && peer_flags.size() == world,
+              "one record buffer and flag array per rank, at most 8 ranks");
+  TORCH_CHECK(epoch > 0 && epoch <= 0xFFFFFFFFll, "epoch must be in [1, 2^32)");
+  std::vector<float*> recs(world);
+  std::vector<uint32_t*> flags(world);
+  for (size_t i = 0; i < world; ++i) {
+    recs[i] = reinterpret_cast<float*>(static_cast<uintptr_t>(peer_records[i]));
+    flags[i] = reinterpret_cast<uint32_t*>(static_cast<uintptr_t>(peer_flags[i]));
+  }
+  const float* ch = host_c(c);
+  const float* dh = host_f32(dk, D, "dk");
+  float* op = nullptr;
+  std::vector<float> dvh(D, 1.f);
+  if (out.has_value()) {
+    TORCH_CHECK(dv.has_value(), "out needs dv");
+    TORCH_CHECK(out->scalar_type() == at::kFloat && out->is_contiguous() &&
+                    out->numel() == G * nq * D && out->device() == dev,
+                "out must be a contiguous float32 tensor of G * n_q * D values on q's device");
+    const float* d2 = host_f32(*dv, D, "dv");
+    std::copy(d2, d2 + D, dvh.begin());
+    op = out->data_ptr<float>();
+  }
+  const Cache K = cache_of(kc, kr, kn, krn), V = cache_of(vc, vr, vn, vrn);
+  c10::cuda::CUDAGuard guard(q.device());
+  check(kh_decode_partial_to_peers(q.data_ptr<float>(), G, (int)nq, (int)D, K.code, K.res,
+                                   K.norms, K.rnorms, V.code, V.res, V.norms, V.rnorms, seq_len,
+                                   seq_begin, seq_end, dh, dvh.data(), ch, (int)c.numel(),
+                                   (float)sm_scale, (int)n_splits, recs.data(), flags.data(),
+                                   (int)rank, (int)world, (uint32_t)epoch, u32(counter), op,
+                                   stream_of(q)),
+        "kh_decode_partial_to_peers");
+}
+
 // records: merged (m, l, acc) records of n_rows query rows, record p of row
 // g at offset g * group_stride + p * part_stride floats.
 void decode_combine(const Tensor& records, int64_t n_rows, int64_t n_parts, int64_t group_stride,
@@ -438,11 +495,12 @@ void decode_merge_to_peers(const Tensor& partials, int64_t n_rows, int64_t n_par
 
 void decode_combine_from_peers(const Tensor& buf, int64_t rec_offset, int64_t flag_offset,
                                int64_t epoch, int64_t n_rows, int64_t world, const Tensor& dv,
-                               const Tensor& out) {
+                               const Tensor& out, int64_t n_parts) {
   require_cuda(buf, "buf");
   const int64_t D = out.size(-1);
+  TORCH_CHECK(n_parts >= 1, "n_parts must be at least 1");
   TORCH_CHECK(rec_offset >= 0 && flag_offset >= 0 && flag_offset + 4 * world <= buf.nbytes() &&
-                  rec_offset + world * n_rows * (D + 2) * 4 <= buf.nbytes(),
+                  rec_offset + world * n_rows * n_parts * (D + 2) * 4 <= buf.nbytes(),
               "record buffer or flags outside buf");
   TORCH_CHECK(out.scalar_type() == at::kFloat && out.is_contiguous() && out.numel() == n_rows * D,
               "out must be a contiguous float32 tensor of n_rows * D values");
@@ -450,11 +508,11 @@ void decode_combine_from_peers(const Tensor& buf, int64_t rec_offset, int64_t fl
   const float* dh = host_f32(dv, D, "dv");
   char* base = static_cast<char*>(buf.data_ptr());
   c10::cuda::CUDAGuard guard(buf.device());
-  check(kh_decode_combine_from_peers(reinterpret_cast<const float*>(base + rec_offset),
-                                     reinterpret_cast<const uint32_t*>(base + flag_offset),
-                                     (uint32_t)epoch, n_rows, (int)world, (int)D, dh,
-                                     out.data_ptr<float>(), stream_of(buf)),
-        "kh_decode_combine_from_peers");
+  check(kh_decode_combine_peer_records(reinterpret_cast<const float*>(base + rec_offset),
+                                       reinterpret_cast<const uint32_t*>(base + flag_offset),
+                                       (uint32_t)epoch, n_rows, (int)n_parts, (int)world, (int)D,
+                                       dh, out.data_ptr<float>(), stream_of(buf)),
+        "kh_decode_combine_peer_records");
 }
 
 // ------------------------------------------------------------------ HBBA
@@ -587,7 +645,12 @@ TORCH_LIBRARY(kudahitam, m) {
         "int part_stride, int head_dim, int[] peer_records, int[] peer_flags, int rank, "
         "int epoch, Tensor(a!) counter) -> ()");
   m.def("decode_combine_from_peers(Tensor buf, int rec_offset, int flag_offset, int epoch, "
-        "int n_rows, int world, Tensor dv, Tensor(a!) out) -> ()");
+        "int n_rows, int world, Tensor dv, Tensor(a!) out, int n_parts=1) -> ()");
+  m.def("decode_partial_to_peers(Tensor q, Tensor k_code, Tensor k_res, Tensor k_norms, "
+        "Tensor k_rnorms, Tensor v_code, Tensor v_res, Tensor v_norms, Tensor v_rnorms, "
+        "int seq_len, int seq_begin, int seq_end, Tensor dk, Tensor centroids, float sm_scale, "
+        "int n_splits, int[] peer_records, int[] peer_flags, int rank, int epoch, "
+        "Tensor(a!) counter, Tensor? dv=None, Tensor(b!)? out=None) -> ()");
   m.def("ultra_fused_hbba_fusion(Tensor x, Tensor d, Tensor centroids_table, Tensor mask, "
         "int layer_id, int active_mask) -> (Tensor, Tensor, Tensor, Tensor)");
   m.def("hbba_calibrate_cuda(Tensor sample, Tensor n_map, int layer_id, int active_mask) "
@@ -613,6 +676,7 @@ TORCH_LIBRARY_IMPL(kudahitam, CUDA, m) {
   m.impl("decode_attention", &decode_attention);
   m.impl("decode_merge_to_peers", &decode_merge_to_peers);
   m.impl("decode_combine_from_peers", &decode_combine_from_peers);
+  m.impl("decode_partial_to_peers", &decode_partial_to_peers);
   m.impl("ultra_fused_hbba_fusion", &ultra_fused_hbba_fusion);
   m.impl("hbba_calibrate_cuda", &hbba_calibrate_cuda);
   m.impl("ultra_fused_full_fusion", &ultra_fused_full_fusion);

@@ -56,6 +56,12 @@ SIGNATURES = {
                                         _c_i, _c_i, ctypes.c_uint32, _vp, _vp]),
     "kh_decode_combine_from_peers": (_c_i, [_vp, _vp, ctypes.c_uint32, _c_i64, _c_i, _c_i,
                                             _vp, _vp, _vp]),
+    "kh_decode_partial_to_peers": (_c_i, [_vp, _c_i64, _c_i, _c_i, _vp, _vp, _vp, _vp, _vp,
+                                          _vp, _vp, _vp, _c_i64, _c_i64, _c_i64, _vp, _vp, _vp,
+                                          _c_i, _c_f, _c_i, _vp, _vp, _c_i, _c_i,
+                                          ctypes.c_uint32, _vp, _vp, _vp]),
+    "kh_decode_combine_peer_records": (_c_i, [_vp, _vp, ctypes.c_uint32, _c_i64, _c_i, _c_i,
+                                              _c_i, _vp, _vp, _vp]),
     "kh_decode_attn": (_c_i, [_vp, _c_i64, _c_i, _vp, _vp, _vp, _vp, _vp, _vp, _vp, _vp,
                               _c_i64, _vp, _vp, _vp, _c_i, _c_f, _c_i, _vp, _c_i64, _vp,
                               _vp]),

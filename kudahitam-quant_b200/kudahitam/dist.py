@@ -69,24 +69,37 @@ def next_epoch(epoch: int) -> int:
 
 
 class PeerRecordExchange:
-    """Buffers for the fused record exchange of a sequence-sharded decode
-    (``kh_decode_merge_to_peers`` / ``kh_decode_combine_from_peers``): one
-    symmetric-memory allocation per rank, addressable by every rank over
-    NVLink, holding two sets (alternating between calls) of a record buffer
-    [world, n_rows, D+2] and a flag array [world], plus a local counter.
+    """Buffers for the record exchange of a sequence-sharded decode over peer
+    memory: one symmetric-memory allocation per rank, addressable by every
+    rank over NVLink, holding two sets (alternating between calls) of a
+    record buffer [world, n_rows, n_parts, D+2] and a flag array [world],
+    plus a local counter.  Two ways to use it:
+
+    * ``decode``: the partial kernel itself stores its split records into
+      every rank's buffer (``kh_decode_partial_to_peers``, up to n_parts
+      records per query row) and one combine kernel merges them
+      (``kh_decode_combine_peer_records``): two kernels per step, no
+      collective call;
+    * ``combine``: after a local partial kernel, ``kh_decode_merge_to_peers``
+      merges each rank's splits and stores one record per row, then
+      ``kh_decode_combine_from_peers`` merges the world records.
+
     Collective to create: every rank of the group builds one with the same
-    arguments, and every rank must make the same sequence of ``combine``
-    calls.  Release it (``del``) after a device synchronisation and before
+    arguments, and every rank must make the same sequence of calls.  Release
+    it (``del``) after a device synchronisation and before
     ``destroy_process_group``.  world <= 8."""
 
-    def __init__(self, n_rows: int, head_dim: int, group=None, device=None):
+    def __init__(self, n_rows: int, head_dim: int, group=None, device=None, n_parts: int = 1):
         import torch.distributed._symmetric_memory as symm
         world, rank = _world(group)
         if world > 8:
             raise ValueError("the peer record exchange supports at most 8 ranks")
+        if n_parts < 1:
+            raise ValueError("n_parts must be at least 1")
         dev = torch.device("cuda", torch.cuda.current_device()) if device is None else device
         self.world, self.rank, self.n_rows, self.head_dim = world, rank, n_rows, head_dim
-        self.rec_bytes = world * n_rows * (head_dim + 2) * 4
+        self.n_parts = n_parts
+        self.rec_bytes = world * n_rows * n_parts * (head_dim + 2) * 4
         self.flag_off = 2 * self.rec_bytes
         total = self.flag_off + 2 * world * 4
         total = (total + 255) // 256 * 256
@@ -130,6 +143,41 @@ class PeerRecordExchange:
             check_peer_timeout(dev)
         return out
 
+    def decode(self, q: torch.Tensor, k_local: ops.PackedKV, v_local: ops.PackedKV, dk, dv,
+               centroids, sm_scale: float, n_splits: int, out: torch.Tensor,
+               checked: bool = False) -> torch.Tensor:
+        """The whole sequence-sharded decode step in one kernel: this rank's
+        split-K partial kernel stores its records straight into every rank's
+        buffer, and once every rank's flag has arrived its CTAs merge the
+        world x n_splits records of each query row into ``out`` (a second
+        kernel does the merge if the launch does not fit on the GPU at once).
+        q: [G, D] or [G, n_q, D] (float32 on this rank's GPU); the caches hold
+        G * S_local rows.  Timeouts behave as in ``combine``."""
+        if n_splits > self.n_parts:
+            raise ValueError(f"exchange built for {self.n_parts} records per row, "
+                             f"got n_splits={n_splits}")
+        G, D = q.shape[0], q.shape[-1]
+        R = q.numel() // D
+        if R != self.n_rows or D != self.head_dim:
+            raise ValueError(f"exchange built for {self.n_rows} rows of {self.head_dim}")
+        S_loc = k_local.n_rows // max(G, 1)
+        qf = q if (q.dtype == torch.float32 and q.is_contiguous()) else \
+            q.to(torch.float32).contiguous()
+        self.epoch = next_epoch(self.epoch)
+        par = self.epoch & 1
+        w = self.world
+        K = ops.ext()
+        K.decode_partial_to_peers(qf, k_local.code, k_local.res, k_local.norms, k_local.rnorms,
+                                  v_local.code, v_local.res, v_local.norms, v_local.rnorms,
+                                  S_loc, 0, S_loc, ops._host_f32(dk), ops._host_f32(centroids),
+                                  float(sm_scale), n_splits,
+                                  [p + par * self.rec_bytes for p in self.ptrs],
+                                  [p + self.flag_off + par * w * 4 for p in self.ptrs],
+                                  self.rank, self.epoch, self.counter, ops._host_f32(dv), out)
+        if checked:
+            check_peer_timeout(q.device)
+        return out
+
 
 class PeerTimeoutError(RuntimeError):
     """A peer-memory record exchange stopped waiting for a peer's records
@@ -162,9 +210,11 @@ def decode_attention_seq_sharded(q: torch.Tensor, k_local: ops.PackedKV,
     (k_local / v_local: G * S_local rows).  q is [G, D] or [G, n_q, D]
     (grouped-query heads).  Returns float32 with q's shape on every rank.
     With ``exchange`` (a PeerRecordExchange of this group and shape) the
-    records cross NVLink inside the merge kernel instead of one NCCL
-    all-gather; if a peer never arrives that path returns zeros and flags
-    bit 2 of the device error word, and ``checked=True`` turns that into a
+    records cross NVLink by plain stores instead of one NCCL all-gather: from
+    the partial kernel itself when the exchange holds n_splits records per
+    row (and the codebook has a table kernel), else from the merge kernel.
+    If a peer never arrives these paths return zeros and flag bit 2 of the
+    device error word, and ``checked=True`` turns that into a
     PeerTimeoutError (at the cost of a stream synchronisation)."""
     world, _ = _world(group)
     G, D = q.shape[0], q.shape[-1]
@@ -178,10 +228,15 @@ def decode_attention_seq_sharded(q: torch.Tensor, k_local: ops.PackedKV,
     need = seq_sharded_workspace_numel(R, n_splits, world, D)
     if partials is None or partials.numel() < need:
         partials = torch.empty(need, dtype=torch.float32, device=q.device)
+    out = torch.empty(q.shape, dtype=torch.float32, device=q.device)
+    if (world > 1 and exchange is not None and n_splits <= exchange.n_parts
+            and (ops._check_codebook(centroids)[0] == 2 or D == 128)):
+        # the partial kernel stores its records into every rank's buffer
+        return exchange.decode(q, k_local, v_local, dk, dv, centroids, sm_scale, n_splits, out,
+                               checked=checked)
     local = partials[: R * n_splits * rec].view(R, n_splits, rec)
     ops.decode_partial(q, k_local, v_local, dk, dv, centroids, sm_scale, n_splits, local,
                        part_stride=n_splits, part_offset=0, seq_len=S_loc)
-    out = torch.empty(q.shape, dtype=torch.float32, device=q.device)
     if world == 1:
         return ops.decode_combine(local, n_splits, dv, out)
     if exchange is not None:

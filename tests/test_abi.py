@@ -129,6 +129,25 @@ def test_other_entry_points_validate():
                                           None) == _lib.KH_EINVAL  # no d vector
     assert L.kh_decode_combine_from_peers(FAKE, FAKE, 1, 0, 2, 128, D128, FAKE,
                                           None) == _lib.KH_OK
+    assert L.kh_decode_combine_peer_records(FAKE, FAKE, 1, 2, 0, 2, 128, D128, FAKE,
+                                            None) == _lib.KH_EINVAL  # no parts
+    assert L.kh_decode_combine_peer_records(FAKE, FAKE, 1, 2, 3, 9, 128, D128, FAKE,
+                                            None) == _lib.KH_EINVAL  # world > 8
+    assert L.kh_decode_combine_peer_records(FAKE, FAKE, 1, 0, 3, 2, 128, D128, FAKE,
+                                            None) == _lib.KH_OK
+
+    def to_peers(rank, world, epoch, counter, n_groups=2, records=P2):
+        return L.kh_decode_partial_to_peers(
+            FAKE, n_groups, 1, 128, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, FAKE, 100, 0, 100,
+            D128, D128, C2, 2, 0.1, 2, records, P2, rank, world, epoch, counter, None, None)
+    assert to_peers(0, 9, 1, FAKE) == _lib.KH_EINVAL  # world > 8
+    assert to_peers(2, 2, 1, FAKE) == _lib.KH_EINVAL  # rank >= world
+    assert to_peers(0, 2, 0, FAKE) == _lib.KH_EINVAL  # epoch 0
+    assert to_peers(0, 2, 1, None) == _lib.KH_EINVAL  # no counter
+    assert to_peers(0, 2, 1, FAKE, records=None) == _lib.KH_EINVAL
+    odd = ctypes.cast((ctypes.c_void_p * 2)(0x10002, 0x20000), ctypes.c_void_p)
+    assert to_peers(0, 2, 1, FAKE, records=odd) == _lib.KH_EALIGN
+    assert to_peers(0, 2, 1, FAKE, n_groups=0) == _lib.KH_OK
 
 
 def test_gqa_decode_and_compat_scorer_validate():

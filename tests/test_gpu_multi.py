@@ -7,7 +7,8 @@ Skipped when fewer than two GPUs are visible.
   single-GPU decode of the whole cache;
 * the same decode with the record exchange fused into the merge kernel over
   peer memory (symmetric memory, NVLink stores and flags) must equal the
-  all-gather path bit for bit, call after call;
+  all-gather path bit for bit, call after call; fused into the partial
+  kernel instead, within 1e-5 normwise;
 * row-sharded compression: ranks compress disjoint batch x head slices with
   no communication; the union must equal the single-GPU result bit for bit."""
 import datetime
@@ -68,6 +69,18 @@ def _worker(rank, world, port, q):
             peer_same = peer_same and torch.equal(alt, got)
         peer_same = peer_same and _lib.device_error() == 0
         del ex
+        # the exchange fused into the partial kernel (records of every split
+        # stored to every rank, one combine): the same attention within 1e-5
+        # normwise (merge order differs), over calls on both buffer sets
+        exf = khdist.PeerRecordExchange(G, D, device=dev, n_parts=3)
+        fused_err = 0.0
+        for _ in range(5):
+            alt = khdist.decode_attention_seq_sharded(qv, pk, pv, dk, dv, c, 1 / math.sqrt(D),
+                                                      n_splits=3, exchange=exf)
+            torch.cuda.synchronize()
+            fused_err = max(fused_err, ((alt - got).abs().max() / got.abs().max()).item())
+        peer_same = peer_same and fused_err < 1e-5 and _lib.device_error() == 0
+        del exf
         torch.cuda.synchronize()
         dist.barrier()
         # compression shards: no communication, bit-identical to the whole
