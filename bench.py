@@ -869,7 +869,10 @@ def decode_timing(dev, args, world, q, pk, pv, dk, dv, c, S_loc, S_total,
         phases["combine"] = lambda: ops.decode_combine_records(gathered.transpose(0, 1), dv, outp)
     else:
         phases["combine"] = lambda: ops.decode_combine(local, n_splits, dv, outp)
-    for _ in range(3):
+    # ten warm-up steps: right after the 8-GPU workload's compression the
+    # first decode steps ran up to 40 % slower than the same steps a few
+    # hundred milliseconds later
+    for _ in range(max(10, args.warmup)):
         step()
     torch.cuda.synchronize()
     barrier(world)
