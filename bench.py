@@ -54,7 +54,7 @@ FALLBACK_HBM_GBS = 6650.0
 NCU_TRAFFIC_BYTES_PER_ROW = (268.480256e6 + 8.786688e6) / 524288
 # Same for the decode step (an ncu capture of decode_v3_kernel<128> on the
 # bench's decode workload itself): bytes per cached row of K and V.
-NCU_DECODE_TRAFFIC_BYTES_PER_ROW = (1.725821e9 + 4.288e6) / (512 * 40000)
+NCU_DECODE_TRAFFIC_BYTES_PER_ROW = (1.639580e9 + 4.611072e6) / (512 * 40000)
 
 
 def peaks() -> tuple[float, str]:
