@@ -715,7 +715,8 @@ def decode_bench(dev, args, world: int = 1, rank: int = 0) -> dict:
                            bytes_per_row=2 * (DEC_D // 16 * 4 + DEC_D // 8 + 8))
         d2["roofline"]["kernel"] = "decode_b2_kernel + decode_combine_kernel<128>"
         dec["bits2_codebook"] = {k: d2[k] for k in ("us_per_step", "n_splits",
-                                                    "phase_us_max_over_ranks", "roofline")}
+                                                    "phase_us_max_over_ranks", "roofline",
+                                                    "sustained")}
         del pk, pv
     return {"config": "q bf16 [32,16,128]; K and V 2-bit-mode packed, S=40000"
                       + (f", sequence-sharded over {world} GPUs + one NCCL all-gather"
@@ -869,15 +870,38 @@ def decode_timing(dev, args, world, q, pk, pv, dk, dv, c, S_loc, S_total,
         phases["combine"] = lambda: ops.decode_combine_records(gathered.transpose(0, 1), dv, outp)
     else:
         phases["combine"] = lambda: ops.decode_combine(local, n_splits, dv, outp)
-    # ten warm-up steps: right after the 8-GPU workload's compression the
-    # first decode steps ran up to 40 % slower than the same steps a few
-    # hundred milliseconds later
+    # One idle second first: right after the 8-GPU workload's compression
+    # (at the power cap) the first decode steps ran up to 40 % slower than
+    # the same steps a second later.  Then two figures:
+    # * us_per_step: ten warm-up steps, then n timed steps (a few ms of load);
+    # * sustained: after at least half a second of back-to-back steps, when
+    #   the power limit has lowered the SM clock (sw_power_cap), with the SM
+    #   clock sampled in that window.  The warm-up step count comes from three
+    #   timed steps and is the max over ranks, so every rank runs the same
+    #   number of collectives.
+    torch.cuda.synchronize()
+    time.sleep(1.0)
+    barrier(world)
     for _ in range(max(10, args.warmup)):
         step()
     torch.cuda.synchronize()
     barrier(world)
     n = max(5, min(args.steps, 20))
     ms = max_over_ranks(statistics.median(time_loop(step, n, stream)), world)
+    t3 = statistics.median(time_loop(step, 3, stream))
+    n_warm = int(max_over_ranks(float(math.ceil(500.0 / max(t3, 1e-3))), world))
+    with ClockSampler(torch.cuda.current_device(), period_s=0.002) as clk:
+        for i in range(n_warm):
+            step()
+            if i % 50 == 49:
+                torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        barrier(world)
+        t0 = time.perf_counter()
+        ms_sus = max_over_ranks(statistics.median(time_loop(step, n, stream)), world)
+        clk.mark_region(t0, time.perf_counter())
+    sustained = {"us_per_step": ms_sus * 1e3, "warmup_steps": n_warm,
+                 "clocks": clk.summary()}
     phase_us = {}
     for name, fn in phases.items():
         barrier(world)
@@ -939,7 +963,10 @@ def decode_timing(dev, args, world, q, pk, pv, dk, dv, c, S_loc, S_total,
             "gbs": bytes_step / (ms / 1e3) / 1e9,
             "frac_of_measured_hbm_per_gpu": per_gpu / peak,
             "roofline": {"bound": "hbm", "achieved": per_gpu, "peak": peak, "unit": "GB/s",
-                         "frac": per_gpu / peak, "algorithmic_bytes": bytes_step / world}}
+                         "frac": per_gpu / peak, "algorithmic_bytes": bytes_step / world},
+            "sustained": {**sustained,
+                          "frac_of_measured_hbm_per_gpu":
+                              bytes_step / world / (ms_sus / 1e3) / 1e9 / peak}}
 
 
 def main():

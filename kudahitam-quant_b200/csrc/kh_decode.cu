@@ -852,8 +852,8 @@ template <int D>
 __device__ __forceinline__ void load_k_row(const SegK<D>& S, uint32_t i, int wr,
                                            uint64_t once, uint64_t again, RowKV<D>& a) {
   constexpr uint32_t kW = D / 32;
-  load_plane_policy<D>(S.code + i * kW, wr, once, a.c);
-  load_plane_policy<D>(S.res + i * kW, wr, once, a.r);
+  load_plane_x<D>(S.code + i * kW, wr, once, a.c);
+  load_plane_x<D>(S.res + i * kW, wr, once, a.r);
   a.n = ldg_policy(S.n + i, once);
   a.rn = ldg_policy(S.rn + i, once);
   a.vn = ldg_policy(S.vn + i, again);
@@ -917,18 +917,15 @@ __global__ void __launch_bounds__(256, 2)
   const float c0dc = P.c0 / dc;
   const float wa = inv_sqrt_d * dc, wb = 2.f * qjl;  // V weight = p (wa |v| + wb r_norm)
 
-  // lane constants: byte k of a rotated plane is plane byte (k + rr) mod kP,
-  // looked up in slot ((k + lane) mod kP) + kP (lane / kP)
+  // lane constants: at step k this lane reads plane byte k ^ rr (XOR order),
+  // looked up in slot (k ^ rr) + kP (lane / kP)
   const int rr = lane % kP;
-  const int wr = rr >> 2, bs = 8 * (rr & 3);
+  const int wr = rr >> 2;
+  const XorSel xs = xor_selectors(rr);
   uint32_t slot4[kP / 4];  // byte (k & 3) of slot4[k >> 2] = 4 * slot(k)
   static_for<kP / 4>([&](auto mc) {
     constexpr int m = decltype(mc)::value;
-    uint32_t w = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-      w |= (4u * (uint32_t)(((4 * m + j + lane) % kP) + kP * (lane / kP))) << (8 * j);
-    slot4[m] = w;
+    slot4[m] = xor_slots<kP>(m, rr, lane / kP);
   });
 
   // phase-2 plane order.  Half-row layout: the code-plane histogram is slots
@@ -1031,14 +1028,14 @@ __global__ void __launch_bounds__(256, 2)
         for (int u = 0; u < B; ++u) {
           float2 m = make_float2(0.f, 0.f);
           uint32_t rc[D / 32], rs[D / 32];
-          rotate_plane<D>(src[u].c, wr, bs, rc);
-          rotate_plane<D>(src[u].r, wr, bs, rs);
+          xor_plane<D>(src[u].c, wr, rc);
+          xor_plane<D>(src[u].r, wr, rs);
           static_for<kP>([&](auto kc) {
             constexpr int k = decltype(kc)::value;
             const float x1 = *reinterpret_cast<const float*>(
-                tabb + tab_addr<k & 3>(rc[k >> 2], slot4[k >> 2]));
+                tabb + tab_addr_x(rc[k >> 2], slot4[k >> 2], xs.s[k & 3]));
             const float x2 = *reinterpret_cast<const float*>(
-                tabb + tab_addr<k & 3>(rs[k >> 2], slot4[k >> 2]));
+                tabb + tab_addr_x(rs[k >> 2], slot4[k >> 2], xs.s[k & 3]));
             m = __fadd2_rn(m, make_float2(x1, x2));
           });
           const float score = src[u].n * (P.c0 * Q + dc * m.x) +
@@ -1088,8 +1085,8 @@ __global__ void __launch_bounds__(256, 2)
 #pragma unroll
       for (int u = 0; u < B; ++u) {
         const uint32_t ii = min((uint32_t)(t + (bi * B + u) * NT), last);
-        load_plane_policy<D>(vxs + ii * (uint32_t)(D / 32), wr, pol_once, dst[u].c);
-        load_plane_policy<D>(vys + ii * (uint32_t)(D / 32), wr, pol_once, dst[u].r);
+        load_plane_x<D>(vxs + ii * (uint32_t)(D / 32), wr, pol_once, dst[u].c);
+        load_plane_x<D>(vys + ii * (uint32_t)(D / 32), wr, pol_once, dst[u].r);
         dst[u].n = ldg_policy(vxns + ii, pol_once);
         dst[u].rn = ldg_policy(vyns + ii, pol_once);
       }
@@ -1139,18 +1136,20 @@ __global__ void __launch_bounds__(256, 2)
           const int fy = __float2int_rn(p * src[u].rn * ky);
           csum += (float)fx * cx + (float)fy * cy;
           uint32_t rx[D / 32], ry[D / 32];
-          rotate_plane<D>(src[u].c, wr, bs, rx);
-          rotate_plane<D>(src[u].r, wr, bs, ry);
+          xor_plane<D>(src[u].c, wr, rx);
+          xor_plane<D>(src[u].r, wr, ry);
           static_for<kP>([&](auto kc) {
             constexpr int k = decltype(kc)::value;
-            atomicAdd(reinterpret_cast<int*>(tabb + tab_addr<k & 3>(rx[k >> 2], slot4[k >> 2])),
+            atomicAdd(reinterpret_cast<int*>(
+                          tabb + tab_addr_x(rx[k >> 2], slot4[k >> 2], xs.s[k & 3])),
                       fx);
             if constexpr (C::kHalf)
-              atomicAdd(reinterpret_cast<int*>(tabb + tab_addr<k & 3>(ry[k >> 2], slot4y[k >> 2])),
+              atomicAdd(reinterpret_cast<int*>(
+                            tabb + tab_addr_x(ry[k >> 2], slot4y[k >> 2], xs.s[k & 3])),
                         fy);
             else
-              atomicAdd(reinterpret_cast<int*>(tabb + 128 +
-                                               tab_addr<k & 3>(ry[k >> 2], slot4[k >> 2])),
+              atomicAdd(reinterpret_cast<int*>(
+                            tabb + 128 + tab_addr_x(ry[k >> 2], slot4[k >> 2], xs.s[k & 3])),
                         fy);
           });
         }
@@ -1318,27 +1317,23 @@ __global__ void __launch_bounds__(256, 2)
   const float wb = 2.f * qjl;  // V weight = p (|v| / sqrt(D) + wb r_norm)
   const float cv0 = P.cb[0], cv1 = P.cb[1], cv2 = P.cb[2], cv3 = P.cb[3];
 
-  // lane constants: code plane rotated by lane bytes (of 32), slots 0..31;
-  // residual plane rotated by lane mod 16, slots 32 + pos + 16 (lane / 16)
-  const int wrc = lane >> 2, bsc = 8 * (lane & 3);
+  // lane constants (XOR byte order): at step k the code plane's byte k ^ lane
+  // (of 32), slot k ^ lane; the residual plane's byte k ^ (lane mod 16), slot
+  // 32 + (k ^ (lane mod 16)) + 16 (lane / 16).  Both share the selectors
+  // (they depend on lane mod 4 only).
+  const int wrc = lane >> 2;
+  const XorSel xs = xor_selectors(lane);
   uint32_t slotc[C::kPC / 4];
   static_for<C::kPC / 4>([&](auto mc) {
     constexpr int m = decltype(mc)::value;
-    uint32_t v = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) v |= (4u * (uint32_t)((4 * m + j + lane) % C::kPC)) << (8 * j);
-    slotc[m] = v;
+    slotc[m] = xor_slots<C::kPC>(m, lane, 0);
   });
   const int rr = lane % C::kPR;
-  const int wrr = rr >> 2, bsr = 8 * (rr & 3);
+  const int wrr = rr >> 2;
   uint32_t slotr[C::kPR / 4];
   static_for<C::kPR / 4>([&](auto mc) {
     constexpr int m = decltype(mc)::value;
-    uint32_t v = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-      v |= (4u * (uint32_t)(((4 * m + j + lane) % C::kPR) + C::kPR * (lane / C::kPR))) << (8 * j);
-    slotr[m] = v;
+    slotr[m] = xor_slots<C::kPR>(m, rr, lane / C::kPR);
   });
   const unsigned char* tabr = tabb + 128;  // entries 32..63 of each table row
 
@@ -1421,8 +1416,8 @@ __global__ void __launch_bounds__(256, 2)
         auto load = [&](RowK2& dst, int bi) {
           const int ii = t + bi * NT;
           const int64_t row = row0 + (ii < n ? ii : 0);
-          load_plane_policy<256>(P.k_code + row * C::kWC, wrc, pol_once, dst.k.c);  // 32-byte plane
-          load_plane_policy<128>(P.k_res + row * C::kWR, wrr, pol_once, dst.k.r);
+          load_plane_x<256>(P.k_code + row * C::kWC, wrc, pol_once, dst.k.c);  // 32-byte plane
+          load_plane_x<128>(P.k_res + row * C::kWR, wrr, pol_once, dst.k.r);
           dst.k.n = ldg_policy(P.k_norms + row, pol_once);
           dst.k.rn = ldg_policy(P.k_rnorms + row, pol_once);
           dst.vn = ldg_policy(P.v_norms + row, pol_again);
@@ -1430,19 +1425,19 @@ __global__ void __launch_bounds__(256, 2)
         };
         auto score = [&](const RowK2& src, int bi) {
           uint32_t rc[C::kWC], rs[C::kWR];
-          rotate_plane<256>(src.k.c, wrc, bsc, rc);
-          rotate_plane<128>(src.k.r, wrr, bsr, rs);
+          xor_plane<256>(src.k.c, wrc, rc);
+          xor_plane<128>(src.k.r, wrr, rs);
           float2 mc = make_float2(0.f, 0.f), mr = make_float2(0.f, 0.f);
           static_for<C::kPC>([&](auto kc) {
             constexpr int k = decltype(kc)::value;
             const float x = *reinterpret_cast<const float*>(
-                tabb + tab_addr<k & 3>(rc[k >> 2], slotc[k >> 2]));
+                tabb + tab_addr_x(rc[k >> 2], slotc[k >> 2], xs.s[k & 3]));
             if constexpr (k & 1) mc.y += x; else mc.x += x;
           });
           static_for<C::kPR>([&](auto kc) {
             constexpr int k = decltype(kc)::value;
             const float x = *reinterpret_cast<const float*>(
-                tabr + tab_addr<k & 3>(rs[k >> 2], slotr[k >> 2]));
+                tabr + tab_addr_x(rs[k >> 2], slotr[k >> 2], xs.s[k & 3]));
             if constexpr (k & 1) mr.y += x; else mr.x += x;
           });
           const float sc = src.k.n * (mc.x + mc.y) +
@@ -1474,8 +1469,8 @@ __global__ void __launch_bounds__(256, 2)
       auto load_v = [&](RowB2& dst, int bi) {
         const int ii = t + bi * NT;
         const int64_t row = row0 + (ii < n ? ii : 0);
-        load_plane_policy<256>(P.v_code + row * C::kWC, wrc, pol_once, dst.c);
-        load_plane_policy<128>(P.v_res + row * C::kWR, wrr, pol_once, dst.r);
+        load_plane_x<256>(P.v_code + row * C::kWC, wrc, pol_once, dst.c);
+        load_plane_x<128>(P.v_res + row * C::kWR, wrr, pol_once, dst.r);
         dst.n = ldg_policy(P.v_norms + row, pol_once);
         dst.rn = ldg_policy(P.v_rnorms + row, pol_once);
       };
@@ -1510,17 +1505,18 @@ __global__ void __launch_bounds__(256, 2)
           const int fy = __float2int_rn(p * src.rn * k2);
           csum += -0.5f * (float)fy;
           uint32_t rc[C::kWC], rs[C::kWR];
-          rotate_plane<256>(src.c, wrc, bsc, rc);
-          rotate_plane<128>(src.r, wrr, bsr, rs);
+          xor_plane<256>(src.c, wrc, rc);
+          xor_plane<128>(src.r, wrr, rs);
           static_for<C::kPC>([&](auto kc) {
             constexpr int k = decltype(kc)::value;
-            atomicAdd(reinterpret_cast<int*>(tabb + tab_addr<k & 3>(rc[k >> 2], slotc[k >> 2])),
+            atomicAdd(reinterpret_cast<int*>(
+                          tabb + tab_addr_x(rc[k >> 2], slotc[k >> 2], xs.s[k & 3])),
                       fx);
           });
           static_for<C::kPR>([&](auto kc) {
             constexpr int k = decltype(kc)::value;
             atomicAdd(reinterpret_cast<int*>(const_cast<unsigned char*>(tabr) +
-                                             tab_addr<k & 3>(rs[k >> 2], slotr[k >> 2])),
+                                             tab_addr_x(rs[k >> 2], slotr[k >> 2], xs.s[k & 3])),
                       fy);
           });
         };

@@ -216,16 +216,25 @@ __global__ void __launch_bounds__(256, 2)
   build_byte_table<D>(reinterpret_cast<float*>(tabb), qt, t);
   __syncthreads();
 
+  // D = 128: XOR byte order (at step k this lane reads plane byte k ^ rr, in
+  // slot (k ^ rr) + kP (lane / kP)); D = 256 keeps the rotated order (plane
+  // byte (k + rr) mod kP), which needs fewer registers with its 8-word planes
+  constexpr bool kX = D == 128;
   const int rr = lane % kP;
   const int wr = rr >> 2, bs = 8 * (rr & 3);
+  const XorSel xs = xor_selectors(rr);
   uint32_t slot4[kP / 4];  // byte (k & 3) of slot4[k >> 2] = 4 * slot(k)
   static_for<kP / 4>([&](auto mc) {
     constexpr int m = decltype(mc)::value;
-    uint32_t w = 0;
+    if constexpr (kX) {
+      slot4[m] = xor_slots<kP>(m, rr, lane / kP);
+    } else {
+      uint32_t w = 0;
 #pragma unroll
-    for (int j = 0; j < 4; ++j)
-      w |= (4u * (uint32_t)(((4 * m + j + lane) % kP) + kP * (lane / kP))) << (8 * j);
-    slot4[m] = w;
+      for (int j = 0; j < 4; ++j)
+        w |= (4u * (uint32_t)(((4 * m + j + lane) % kP) + kP * (lane / kP))) << (8 * j);
+      slot4[m] = w;
+    }
   });
 
   struct Row {
@@ -238,10 +247,16 @@ __global__ void __launch_bounds__(256, 2)
     for (int u = 0; u < B; ++u) {
       const int ii = t + (bi * B + u) * NT;
       const int64_t row = row0 + (ii < n ? ii : 0);
-      load_plane<D>(P.code + row * kW, wr, dst[u].c);
+      if constexpr (kX)
+        load_plane_xg<D>(P.code + row * kW, wr, dst[u].c);
+      else
+        load_plane<D>(P.code + row * kW, wr, dst[u].c);
       dst[u].n = __ldg(P.norms + row);
       if constexpr (RES) {
-        load_plane<D>(P.res + row * kW, wr, dst[u].r);
+        if constexpr (kX)
+          load_plane_xg<D>(P.res + row * kW, wr, dst[u].r);
+        else
+          load_plane<D>(P.res + row * kW, wr, dst[u].r);
         dst[u].rn = __ldg(P.rnorms + row);
       }
     }
@@ -251,16 +266,24 @@ __global__ void __launch_bounds__(256, 2)
     for (int u = 0; u < B; ++u) {
       float2 m = make_float2(0.f, 0.f);
       uint32_t rc[kW], rs[RES ? kW : 1];
-      rotate_plane<D>(src[u].c, wr, bs, rc);
-      if constexpr (RES) rotate_plane<D>(src[u].r, wr, bs, rs);
+      if constexpr (kX) {
+        xor_plane<D>(src[u].c, wr, rc);
+        if constexpr (RES) xor_plane<D>(src[u].r, wr, rs);
+      } else {
+        rotate_plane<D>(src[u].c, wr, bs, rc);
+        if constexpr (RES) rotate_plane<D>(src[u].r, wr, bs, rs);
+      }
       static_for<kP>([&](auto kc) {
         constexpr int k = decltype(kc)::value;
-        const float x1 = *reinterpret_cast<const float*>(
-            tabb + tab_addr<k & 3>(rc[k >> 2], slot4[k >> 2]));
+        const uint32_t a1 = kX ? tab_addr_x(rc[k >> 2], slot4[k >> 2], xs.s[k & 3])
+                               : tab_addr<k & 3>(rc[k >> 2], slot4[k >> 2]);
+        const float x1 = *reinterpret_cast<const float*>(tabb + a1);
         float x2 = 0.f;
-        if constexpr (RES)
-          x2 = *reinterpret_cast<const float*>(
-              tabb + tab_addr<k & 3>(rs[k >> 2], slot4[k >> 2]));
+        if constexpr (RES) {
+          const uint32_t a2 = kX ? tab_addr_x(rs[k >> 2], slot4[k >> 2], xs.s[k & 3])
+                                 : tab_addr<k & 3>(rs[k >> 2], slot4[k >> 2]);
+          x2 = *reinterpret_cast<const float*>(tabb + a2);
+        }
         m = __fadd2_rn(m, make_float2(x1, x2));
       });
       float sc = src[u].n * (c0 * Q + dc * m.x);
@@ -354,27 +377,23 @@ __global__ void __launch_bounds__(256, 2)
   if constexpr (RES) build_byte_table<D>(tab + 32, qt, t);
   __syncthreads();
 
-  // code plane: rotation by lane bytes (of 32), slots 0..31
-  const int wrc = lane >> 2, bsc = 8 * (lane & 3);
+  // XOR byte order.  Code plane: at step k byte k ^ lane (of 32), slot
+  // k ^ lane.  Residual plane: byte k ^ (lane mod 16), two copies (slots 32 +
+  // (k ^ (lane mod 16)) + 16 (lane / 16)).  The selectors depend on lane mod
+  // 4 only, so both planes share them.
+  const int wrc = lane >> 2;
+  const XorSel xs = xor_selectors(lane);
   uint32_t slotc[kPC / 4];
   static_for<kPC / 4>([&](auto mc) {
     constexpr int m = decltype(mc)::value;
-    uint32_t v = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j) v |= (4u * (uint32_t)((4 * m + j + lane) % kPC)) << (8 * j);
-    slotc[m] = v;
+    slotc[m] = xor_slots<kPC>(m, lane, 0);
   });
-  // residual plane: rotation by lane mod 16, two copies (slots 32 + ...)
   const int rr = lane % kPR;
-  const int wrr = rr >> 2, bsr = 8 * (rr & 3);
+  const int wrr = rr >> 2;
   uint32_t slotr[kPR / 4];
   static_for<kPR / 4>([&](auto mc) {
     constexpr int m = decltype(mc)::value;
-    uint32_t v = 0;
-#pragma unroll
-    for (int j = 0; j < 4; ++j)
-      v |= (4u * (uint32_t)(((4 * m + j + lane) % kPR) + kPR * (lane / kPR))) << (8 * j);
-    slotr[m] = v;
+    slotr[m] = xor_slots<kPR>(m, rr, lane / kPR);
   });
   const unsigned char* tabr = tabb + 128;  // entries 32..63 of each table row
 
@@ -388,10 +407,10 @@ __global__ void __launch_bounds__(256, 2)
     for (int u = 0; u < B; ++u) {
       const int ii = t + (bi * B + u) * NT;
       const int64_t row = row0 + (ii < n ? ii : 0);
-      load_plane<256>(P.code + row * kWC, wrc, dst[u].c);  // 32-byte plane, words rotated
+      load_plane_xg<256>(P.code + row * kWC, wrc, dst[u].c);  // 32-byte plane, words permuted
       dst[u].n = __ldg(P.norms + row);
       if constexpr (RES) {
-        load_plane<128>(P.res + row * kWR, wrr, dst[u].r);
+        load_plane_xg<128>(P.res + row * kWR, wrr, dst[u].r);
         dst[u].rn = __ldg(P.rnorms + row);
       }
     }
@@ -401,22 +420,22 @@ __global__ void __launch_bounds__(256, 2)
     for (int u = 0; u < B; ++u) {
       float2 m = make_float2(0.f, 0.f);
       uint32_t rc[kWC];
-      rotate_plane<256>(src[u].c, wrc, bsc, rc);
+      xor_plane<256>(src[u].c, wrc, rc);
       static_for<kPC>([&](auto kc) {
         constexpr int k = decltype(kc)::value;
         const float x = *reinterpret_cast<const float*>(
-            tabb + tab_addr<k & 3>(rc[k >> 2], slotc[k >> 2]));
+            tabb + tab_addr_x(rc[k >> 2], slotc[k >> 2], xs.s[k & 3]));
         if constexpr (k & 1) m.y += x; else m.x += x;
       });
       float sc = src[u].n * (m.x + m.y);
       if constexpr (RES) {
         uint32_t rs[kWR];
-        rotate_plane<128>(src[u].r, wrr, bsr, rs);
+        xor_plane<128>(src[u].r, wrr, rs);
         float2 mr = make_float2(0.f, 0.f);
         static_for<kPR>([&](auto kc) {
           constexpr int k = decltype(kc)::value;
           const float x = *reinterpret_cast<const float*>(
-              tabr + tab_addr<k & 3>(rs[k >> 2], slotr[k >> 2]));
+              tabr + tab_addr_x(rs[k >> 2], slotr[k >> 2], xs.s[k & 3]));
           if constexpr (k & 1) mr.y += x; else mr.x += x;
         });
         sc += inv_sqrt_d * (2.f * (mr.x + mr.y) - Q) * src[u].rn;
