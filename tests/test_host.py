@@ -99,8 +99,9 @@ def _launcher_ranges(G, nq, L, n_splits, sms):
 
 
 def _kernel_writes(G, nq, L, seq_begin, n_splits, W, n_cta):
-    """decode_v3_kernel / decode_b2_kernel: record slots written and (query
-    row, sequence row) pairs covered, from the kernel's index arithmetic."""
+    """decode_v3_kernel / decode_b2_kernel: record slots written and the
+    sequence intervals [s0, s1) each query row's pieces cover, from the
+    kernel's index arithmetic."""
     writes, cover = {}, {}
     for b in range(n_cta):
         if W == 0:
@@ -117,8 +118,7 @@ def _kernel_writes(G, nq, L, seq_begin, n_splits, W, n_cta):
             rp = st - gk * L // W
             assert 0 <= rp < n_splits, (G, nq, L, n_splits, W)
             writes.setdefault((g, rp), []).append("rec")
-            for s in range(s0, s1):
-                cover[(g, s)] = cover.get((g, s), 0) + 1
+            cover.setdefault(g, []).append((s0, s1))
             if s1 == seq_begin + L:
                 for p in range(rp + 1, n_splits):
                     writes.setdefault((g, p), []).append("empty")
@@ -140,6 +140,8 @@ def test_decode_work_split_covers_every_row_once():
         for g in range(G * nq):
             for p in range(ns):
                 assert len(writes.get((g, p), [])) == 1, (G, nq, L, ns, sms, g, p)
-            for s in range(3, 3 + L):
-                assert cover.get((g, s), 0) == 1, (G, nq, L, ns, g, s)
+            # the pieces of query row g tile [3, 3 + L) exactly once
+            iv = sorted(cover.get(g, []))
+            edges = [3] + [b for _, b in iv]
+            assert [a for a, _ in iv] == edges[:-1] and edges[-1] == 3 + L, (G, nq, L, ns, g)
         assert all(g < G * nq and p < ns for g, p in writes)
