@@ -340,4 +340,37 @@ __device__ __forceinline__ void xor_plane(const uint32_t (&w)[D / 32], int wx,
   }
 }
 
+// A 32-byte plane (8 words) in the XOR order, as two 16-byte loads: bit 2
+// of wx swaps the two halves through the addresses, and xor_plane32 then
+// permutes the words within each half by wx mod 4, so that z[i] = plane word
+// i ^ wx.  (Eight 4-byte loads at permuted addresses touch four times as
+// many L1 wavefronts per warp.)
+__device__ __forceinline__ void load_plane32_x(const uint32_t* __restrict__ plane, int wx,
+                                               uint64_t pol, uint32_t (&w)[8]) {
+  const int hs = (wx >> 2) & 1;
+  const uint4 a = ldg_policy(reinterpret_cast<const uint4*>(plane) + hs, pol);
+  const uint4 b = ldg_policy(reinterpret_cast<const uint4*>(plane) + (hs ^ 1), pol);
+  w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+  w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+}
+__device__ __forceinline__ void load_plane32_xg(const uint32_t* __restrict__ plane, int wx,
+                                                uint32_t (&w)[8]) {
+  const int hs = (wx >> 2) & 1;
+  const uint4 a = __ldg(reinterpret_cast<const uint4*>(plane) + hs);
+  const uint4 b = __ldg(reinterpret_cast<const uint4*>(plane) + (hs ^ 1));
+  w[0] = a.x; w[1] = a.y; w[2] = a.z; w[3] = a.w;
+  w[4] = b.x; w[5] = b.y; w[6] = b.z; w[7] = b.w;
+}
+__device__ __forceinline__ void xor_plane32(const uint32_t (&w)[8], int wx, uint32_t (&z)[8]) {
+  const uint32_t lo[4] = {w[0], w[1], w[2], w[3]}, hi[4] = {w[4], w[5], w[6], w[7]};
+  uint32_t zl[4], zh[4];
+  xor_plane<128>(lo, wx, zl);
+  xor_plane<128>(hi, wx, zh);
+#pragma unroll
+  for (int i = 0; i < 4; ++i) {
+    z[i] = zl[i];
+    z[4 + i] = zh[i];
+  }
+}
+
 }  // namespace kh

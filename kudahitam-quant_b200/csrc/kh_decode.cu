@@ -1416,7 +1416,7 @@ __global__ void __launch_bounds__(256, 2)
         auto load = [&](RowK2& dst, int bi) {
           const int ii = t + bi * NT;
           const int64_t row = row0 + (ii < n ? ii : 0);
-          load_plane_x<256>(P.k_code + row * C::kWC, wrc, pol_once, dst.k.c);  // 32-byte plane
+          load_plane32_x(P.k_code + row * C::kWC, wrc, pol_once, dst.k.c);  // 32-byte plane
           load_plane_x<128>(P.k_res + row * C::kWR, wrr, pol_once, dst.k.r);
           dst.k.n = ldg_policy(P.k_norms + row, pol_once);
           dst.k.rn = ldg_policy(P.k_rnorms + row, pol_once);
@@ -1425,20 +1425,25 @@ __global__ void __launch_bounds__(256, 2)
         };
         auto score = [&](const RowK2& src, int bi) {
           uint32_t rc[C::kWC], rs[C::kWR];
-          xor_plane<256>(src.k.c, wrc, rc);
+          xor_plane32(src.k.c, wrc, rc);
           xor_plane<128>(src.k.r, wrr, rs);
+          // (x = even steps, y = odd steps)
           float2 mc = make_float2(0.f, 0.f), mr = make_float2(0.f, 0.f);
-          static_for<C::kPC>([&](auto kc) {
-            constexpr int k = decltype(kc)::value;
-            const float x = *reinterpret_cast<const float*>(
+          static_for<C::kPC / 2>([&](auto jc) {
+            constexpr int k = 2 * decltype(jc)::value;
+            const float x0 = *reinterpret_cast<const float*>(
                 tabb + tab_addr_x(rc[k >> 2], slotc[k >> 2], xs.s[k & 3]));
-            if constexpr (k & 1) mc.y += x; else mc.x += x;
+            const float x1 = *reinterpret_cast<const float*>(
+                tabb + tab_addr_x(rc[k >> 2], slotc[k >> 2], xs.s[(k + 1) & 3]));
+            mc = __fadd2_rn(mc, make_float2(x0, x1));
           });
-          static_for<C::kPR>([&](auto kc) {
-            constexpr int k = decltype(kc)::value;
-            const float x = *reinterpret_cast<const float*>(
+          static_for<C::kPR / 2>([&](auto jc) {
+            constexpr int k = 2 * decltype(jc)::value;
+            const float x0 = *reinterpret_cast<const float*>(
                 tabr + tab_addr_x(rs[k >> 2], slotr[k >> 2], xs.s[k & 3]));
-            if constexpr (k & 1) mr.y += x; else mr.x += x;
+            const float x1 = *reinterpret_cast<const float*>(
+                tabr + tab_addr_x(rs[k >> 2], slotr[k >> 2], xs.s[(k + 1) & 3]));
+            mr = __fadd2_rn(mr, make_float2(x0, x1));
           });
           const float sc = src.k.n * (mc.x + mc.y) +
                            inv_sqrt_d * (2.f * (mr.x + mr.y) - Q) * src.k.rn;
@@ -1469,7 +1474,7 @@ __global__ void __launch_bounds__(256, 2)
       auto load_v = [&](RowB2& dst, int bi) {
         const int ii = t + bi * NT;
         const int64_t row = row0 + (ii < n ? ii : 0);
-        load_plane_x<256>(P.v_code + row * C::kWC, wrc, pol_once, dst.c);
+        load_plane32_x(P.v_code + row * C::kWC, wrc, pol_once, dst.c);
         load_plane_x<128>(P.v_res + row * C::kWR, wrr, pol_once, dst.r);
         dst.n = ldg_policy(P.v_norms + row, pol_once);
         dst.rn = ldg_policy(P.v_rnorms + row, pol_once);
@@ -1505,7 +1510,7 @@ __global__ void __launch_bounds__(256, 2)
           const int fy = __float2int_rn(p * src.rn * k2);
           csum += -0.5f * (float)fy;
           uint32_t rc[C::kWC], rs[C::kWR];
-          xor_plane<256>(src.c, wrc, rc);
+          xor_plane32(src.c, wrc, rc);
           xor_plane<128>(src.r, wrr, rs);
           static_for<C::kPC>([&](auto kc) {
             constexpr int k = decltype(kc)::value;

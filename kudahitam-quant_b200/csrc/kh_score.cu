@@ -407,7 +407,7 @@ __global__ void __launch_bounds__(256, 2)
     for (int u = 0; u < B; ++u) {
       const int ii = t + (bi * B + u) * NT;
       const int64_t row = row0 + (ii < n ? ii : 0);
-      load_plane_xg<256>(P.code + row * kWC, wrc, dst[u].c);  // 32-byte plane, words permuted
+      load_plane32_xg(P.code + row * kWC, wrc, dst[u].c);  // 32-byte plane
       dst[u].n = __ldg(P.norms + row);
       if constexpr (RES) {
         load_plane_xg<128>(P.res + row * kWR, wrr, dst[u].r);
@@ -420,23 +420,27 @@ __global__ void __launch_bounds__(256, 2)
     for (int u = 0; u < B; ++u) {
       float2 m = make_float2(0.f, 0.f);
       uint32_t rc[kWC];
-      xor_plane<256>(src[u].c, wrc, rc);
-      static_for<kPC>([&](auto kc) {
-        constexpr int k = decltype(kc)::value;
-        const float x = *reinterpret_cast<const float*>(
+      xor_plane32(src[u].c, wrc, rc);
+      static_for<kPC / 2>([&](auto jc) {  // (x = even steps, y = odd steps)
+        constexpr int k = 2 * decltype(jc)::value;
+        const float x0 = *reinterpret_cast<const float*>(
             tabb + tab_addr_x(rc[k >> 2], slotc[k >> 2], xs.s[k & 3]));
-        if constexpr (k & 1) m.y += x; else m.x += x;
+        const float x1 = *reinterpret_cast<const float*>(
+            tabb + tab_addr_x(rc[k >> 2], slotc[k >> 2], xs.s[(k + 1) & 3]));
+        m = __fadd2_rn(m, make_float2(x0, x1));
       });
       float sc = src[u].n * (m.x + m.y);
       if constexpr (RES) {
         uint32_t rs[kWR];
         xor_plane<128>(src[u].r, wrr, rs);
         float2 mr = make_float2(0.f, 0.f);
-        static_for<kPR>([&](auto kc) {
-          constexpr int k = decltype(kc)::value;
-          const float x = *reinterpret_cast<const float*>(
+        static_for<kPR / 2>([&](auto jc) {
+          constexpr int k = 2 * decltype(jc)::value;
+          const float x0 = *reinterpret_cast<const float*>(
               tabr + tab_addr_x(rs[k >> 2], slotr[k >> 2], xs.s[k & 3]));
-          if constexpr (k & 1) mr.y += x; else mr.x += x;
+          const float x1 = *reinterpret_cast<const float*>(
+              tabr + tab_addr_x(rs[k >> 2], slotr[k >> 2], xs.s[(k + 1) & 3]));
+          mr = __fadd2_rn(mr, make_float2(x0, x1));
         });
         sc += inv_sqrt_d * (2.f * (mr.x + mr.y) - Q) * src[u].rn;
       }
