@@ -54,7 +54,7 @@ FALLBACK_HBM_GBS = 6650.0
 NCU_TRAFFIC_BYTES_PER_ROW = (268.480256e6 + 8.786688e6) / 524288
 # Same for the decode step (an ncu capture of decode_v3_kernel<128> on the
 # bench's decode workload itself): bytes per cached row of K and V.
-NCU_DECODE_TRAFFIC_BYTES_PER_ROW = (1.639580e9 + 4.611072e6) / (512 * 40000)
+NCU_DECODE_TRAFFIC_BYTES_PER_ROW = (1.639534e9 + 3.693824e6) / (512 * 40000)
 
 
 def peaks() -> tuple[float, str]:
@@ -873,8 +873,10 @@ def decode_timing(dev, args, world, q, pk, pv, dk, dv, c, S_loc, S_total,
     # One idle second first: right after the 8-GPU workload's compression
     # (at the power cap) the first decode steps ran up to 40 % slower than
     # the same steps a second later.  Then two figures:
-    # * us_per_step: ten warm-up steps, then n timed steps (a few ms of load);
-    # * sustained: after at least half a second of back-to-back steps, when
+    # * us_per_step: ten warm-up steps, then n timed steps (a few ms of load),
+    #   followed by each phase alone and the peer-memory variants, all in the
+    #   same few-ms state;
+    # * sustained, last: after at least half a second of back-to-back steps, when
     #   the power limit has lowered the SM clock (sw_power_cap), with the SM
     #   clock sampled in that window.  The warm-up step count comes from three
     #   timed steps and is the max over ranks, so every rank runs the same
@@ -888,20 +890,6 @@ def decode_timing(dev, args, world, q, pk, pv, dk, dv, c, S_loc, S_total,
     barrier(world)
     n = max(5, min(args.steps, 20))
     ms = max_over_ranks(statistics.median(time_loop(step, n, stream)), world)
-    t3 = statistics.median(time_loop(step, 3, stream))
-    n_warm = int(max_over_ranks(float(math.ceil(500.0 / max(t3, 1e-3))), world))
-    with ClockSampler(torch.cuda.current_device(), period_s=0.002) as clk:
-        for i in range(n_warm):
-            step()
-            if i % 50 == 49:
-                torch.cuda.synchronize()
-        torch.cuda.synchronize()
-        barrier(world)
-        t0 = time.perf_counter()
-        ms_sus = max_over_ranks(statistics.median(time_loop(step, n, stream)), world)
-        clk.mark_region(t0, time.perf_counter())
-    sustained = {"us_per_step": ms_sus * 1e3, "warmup_steps": n_warm,
-                 "clocks": clk.summary()}
     phase_us = {}
     for name, fn in phases.items():
         barrier(world)
@@ -952,6 +940,20 @@ def decode_timing(dev, args, world, q, pk, pv, dk, dv, c, S_loc, S_total,
                 "fused_in_partial_us_per_step": fms * 1e3,
                 "fused_note": "kh_decode_partial_to_peers with out: the partial kernel stores "
                               "its split records to every rank and merges the rows itself"}
+    t3 = statistics.median(time_loop(step, 3, stream))
+    n_warm = int(max_over_ranks(float(math.ceil(500.0 / max(t3, 1e-3))), world))
+    with ClockSampler(torch.cuda.current_device(), period_s=0.002) as clk:
+        for i in range(n_warm):
+            step()
+            if i % 50 == 49:
+                torch.cuda.synchronize()
+        torch.cuda.synchronize()
+        barrier(world)
+        t0 = time.perf_counter()
+        ms_sus = max_over_ranks(statistics.median(time_loop(step, n, stream)), world)
+        clk.mark_region(t0, time.perf_counter())
+    sustained = {"us_per_step": ms_sus * 1e3, "warmup_steps": n_warm,
+                 "clocks": clk.summary()}
     if bytes_per_row is None:
         bytes_per_row = 2 * (2 * D // 8 + 8)  # K and V: 2 one-bit planes + 2 norms each
     bytes_step = R * S_total * bytes_per_row  # whole job
