@@ -145,3 +145,71 @@ def test_decode_work_split_covers_every_row_once():
             edges = [3] + [b for _, b in iv]
             assert [a for a, _ in iv] == edges[:-1] and edges[-1] == 3 + L, (G, nq, L, ns, g)
         assert all(g < G * nq and p < ns for g, p in writes)
+
+
+def _prmt(a, b, sel):
+    """prmt.b32 generic mode: result byte i = source byte (sel nibble i & 7) of
+    (b:a), or that byte's sign bit replicated when the nibble's bit 3 is set."""
+    src = [(a >> (8 * i)) & 255 for i in range(4)] + [(b >> (8 * i)) & 255 for i in range(4)]
+    r = 0
+    for i in range(4):
+        n = (sel >> (4 * i)) & 15
+        byte = src[n & 7]
+        if n & 8:
+            byte = 255 if byte & 128 else 0
+        r |= byte << (8 * i)
+    return r
+
+
+def _xor_selectors(r):
+    """kh_bytetab.cuh xor_selectors."""
+    return [((8 | (4 + b)) << 12) | ((8 | (4 + b)) << 8) | ((b ^ (r & 3)) << 4) | (4 + b)
+            for b in range(4)]
+
+
+def _xor_slots(P, m, r, cp):
+    """kh_bytetab.cuh xor_slots."""
+    return sum((4 * (((4 * m + j) ^ r) + P * cp)) << (8 * j) for j in range(4))
+
+
+def _xor_view(w, wx):
+    """xor_plane<128> (two select stages) / xor_plane32 (halves swapped by the
+    load addresses, then xor_plane<128> within each half)."""
+    def x128(q):
+        y = [q[2], q[3], q[0], q[1]] if wx & 2 else list(q)
+        return [y[1], y[0], y[3], y[2]] if wx & 1 else y
+    if len(w) == 4:
+        return x128(w)
+    hs = (wx >> 2) & 1
+    return x128(w[4 * hs:4 * hs + 4]) + x128(w[4 * (hs ^ 1):4 * (hs ^ 1) + 4])
+
+
+def test_xor_byte_order_addresses_and_banks():
+    """The XOR byte order of the table kernels, restated from the device code:
+    at step k lane l's byte-permute yields 256 * (plane byte k ^ r) + 4 * slot
+    with slot = (k ^ r) + P (l / P), r = l mod P, and the 32 lanes of a warp
+    touch 32 distinct banks (16-byte planes with two table copies, 32-byte
+    planes with one; also the second V atomic's slots of the half-row layout)."""
+    import random
+    rng = random.Random(1)
+    for nwords in (4, 8):
+        P = 4 * nwords
+        for _ in range(20):
+            planes = [[rng.getrandbits(32) for _ in range(nwords)] for _ in range(32)]
+            for k in range(P):
+                banks, banks_y = set(), set()
+                for lane in range(32):
+                    r = lane % P
+                    z = _xor_view(planes[lane], r >> 2)
+                    slots = _xor_slots(P, k >> 2, r, lane // P)
+                    a = _prmt(z[k >> 2], slots, _xor_selectors(r)[k & 3])
+                    p = k ^ r
+                    v = (planes[lane][p >> 2] >> (8 * (p & 3))) & 255
+                    slot = p + P * (lane // P)
+                    assert a == 256 * v + 4 * slot, (nwords, k, lane)
+                    banks.add(slot % 32)
+                    if P == 16:  # decode v3's second atomic: the other copy
+                        a2 = _prmt(z[k >> 2], slots ^ 0x40404040, _xor_selectors(r)[k & 3])
+                        assert a2 == 256 * v + 4 * (p + 16 * (1 - lane // 16))
+                        banks_y.add((p + 16 * (1 - lane // 16)) % 32)
+                assert len(banks) == 32 and (P != 16 or len(banks_y) == 32)
