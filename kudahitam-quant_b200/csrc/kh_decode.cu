@@ -779,7 +779,8 @@ __global__ void __launch_bounds__(256)
 // Table and histograms share one array of 256 rows (one per byte value) of
 // 64 32-bit entries; row v starts at byte 256 v, so one byte-permute of
 // (plane word, lane slot offset) yields the byte address 256 v + 4 slot.
-// Slots follow the conflict-free rotation described for v2.
+// Slots follow the XOR byte order of kh_bytetab.cuh (lane l visits byte
+// k ^ (l mod D/8) at step k; 32 distinct banks per warp instruction).
 //   D = 128 (half-row layout): the K table (two copies of 16 positions) and
 //     the two V histograms (one copy each: code plane slots 0..15, residual
 //     plane 16..31) use entries 0..31; half the lanes scatter the residual
@@ -1263,7 +1264,7 @@ __global__ void __launch_bounds__(256, 2)
 // of byte p).
 //   K table  entries 0..31 of each 64-word row: T2[v][p] =
 //            sum_{k<4} q~[4p + k] c[(v >> 2k) & 3] (one copy; lane l looks up
-//            position (k + l) mod 32 at step k); entries 32..63: the 1-bit
+//            position k ^ l at step k); entries 32..63: the 1-bit
 //            residual table (16 positions, two copies).
 //   score    norm * sum_p T2 + r_norm / sqrt(D) (2 M_res - Q).
 //   V        the code plane's histogram H2[v][p] takes w = p_s |v_s| / sqrt(D)
