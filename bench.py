@@ -838,9 +838,11 @@ def cfg5_bench(dev, args, world: int, rank: int) -> dict:
 def decode_timing(dev, args, world, q, pk, pv, dk, dv, c, S_loc, S_total,
                   bytes_per_row: int = None) -> dict:
     """Times decode attention (q [R, D] against R groups of S_loc cached rows
-    on this rank; S_total over all ranks): whole steps, and each phase on its
-    own (partial kernel, local merge, NCCL all-gather, combine), every time
-    the max over ranks of the median of CUDA-event timings."""
+    on this rank; S_total over all ranks): whole steps, each phase on its
+    own (partial kernel, local merge, NCCL all-gather, combine), the
+    peer-memory exchanges (N > 1), and whole steps again after half a second
+    of back-to-back steps (`sustained`, with the SM clock of that window);
+    every time the max over ranks of the median of CUDA-event timings."""
     from kudahitam import dist as khdist
     from kudahitam import ops
     R, D = q.shape
